@@ -1,0 +1,337 @@
+"""Training manager and engine.
+
+`TrainingManager` keeps the reference's contract (`train_gpt.py:2009-2198`): the parameter
+table, scatter/work orders, `advance_schedule`, `get_forward_args`, `step_optimizers`,
+`reset`/`get_state`, sparse-row bookkeeping.  `Trainer` is the public engine: it builds model,
+loaders and manager for a preset and exposes `train_step`, `validate`, `run` (the full loop
+with the reference's log lines), checkpoint save/resume and device-timed step statistics.
+"""
+from __future__ import annotations
+
+import copy
+import os
+import sys
+import time
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from .config import (Hyperparameters, ModelConfig, TrainingSchedule, track1_model, track1_stages)
+from .data.loader import TokenLoader
+from .models.gpt import GPT, ForwardScheduleConfig
+from .optim.normuon_adam import NorMuonAndAdam
+from .parallel.collectives import TorchCollectives
+from .parallel.sparse_comms import RowTracker, SparseRowExchange
+from .runtime.dist import DistEnv, broadcast_model
+from .utils.logging import RunLogger
+
+
+def track1_param_table() -> dict:
+    """`train_gpt.py:2026-2050`."""
+    A = "adam"
+    t = {
+        "qk_bank": {"optim": "normuon", "comms": "sharded", "adam_betas": None},
+        "vo_bank": {"optim": "normuon", "comms": "sharded", "adam_betas": None},
+        "mlp_bank": {"optim": "normuon", "comms": "sharded", "adam_betas": None},
+        "scalars": {"optim": A, "comms": "replicated", "adam_betas": [0.9, 0.99], "lr_mul": 5.0, "wd_mul": 0.0},
+        "smear_gate": {"optim": A, "comms": "replicated", "adam_betas": [0.9, 0.99], "lr_mul": 0.01, "wd_mul": 0.0},
+        "ve_gate_bank": {"optim": A, "comms": "replicated", "adam_betas": [0.9, 0.99]},
+        "lm_head": {"optim": A, "comms": "sharded", "adam_betas": [0.5, 0.95], "wd_mul": 150.0},
+        "bigram_embed": {"optim": A, "comms": "sharded_sparse", "adam_betas": [0.75, 0.95], "lr_mul": 75.0, "wd_mul": 5.0},
+        "post_lambdas": {"optim": A, "comms": "replicated", "adam_betas": [0.9, 0.95], "lr_mul": 1.0, "wd_mul": 0.0},
+        "resid_lambdas": {"optim": A, "comms": "replicated", "adam_betas": [0.9, 0.95], "lr_mul": 5.0, "wd_mul": 0.0},
+        "value_embeds": {"optim": A, "comms": "sharded", "adam_betas": [0.75, 0.95], "lr_mul": 75.0, "wd_mul": 5.0},
+        "embed": {"optim": A, "comms": "sharded", "adam_betas": [0.5, 0.95], "wd_mul": 150.0},
+    }
+    for name, lr in (("mudd", 0.25), ("mudd_gate", 0.1)):
+        t[f"{name}_w1"] = {"optim": A, "comms": "replicated", "adam_betas": [0.9, 0.99], "lr_mul": lr}
+        t[f"{name}_w2"] = {"optim": A, "comms": "replicated", "adam_betas": [0.9, 0.99], "lr_mul": lr}
+        t[f"{name}_b2"] = {"optim": A, "comms": "replicated", "adam_betas": [0.9, 0.99], "lr_mul": lr, "wd_mul": 0.0}
+    t["_mudd_gate_scale"] = {"optim": A, "comms": "replicated", "adam_betas": [0.9, 0.99], "lr_mul": 0.1, "wd_mul": 0.0}
+    return t
+
+
+TRACK1_WORK_ORDER = [
+    "scalars", "smear_gate", "ve_gate_bank", "mudd_b2", "mudd_gate_b2", "_mudd_gate_scale", "post_lambdas",
+    "resid_lambdas", "mudd_w2", "mudd_gate_w2", "value_embeds", "bigram_embed", "mudd_w1", "mudd_gate_w1",
+    "lm_head", "embed", "qk_bank", "vo_bank", "mlp_bank",
+]
+
+
+class TrainingManager:
+    def __init__(self, model: GPT, schedule: TrainingSchedule, hp: Hyperparameters, env: DistEnv,
+                 collectives=None, math=None, sparse_min_world: int = 8):
+        self.model, self.schedule, self.hp, self.env = model, schedule, hp, env
+        self.block_size = hp.block_size
+        self.param_table = track1_param_table()
+        self.work_order = list(TRACK1_WORK_ORDER)
+        dev = next(model.parameters()).device
+        self.sparse = None
+        self.row_tracker = None
+        if (hasattr(model, "bigram_embed") and env.world_size >= sparse_min_world and env.world_size > 1
+                and env.grad_accum_steps == 1):
+            n = model.bigram_embed.weight.shape[0]
+            self.sparse = SparseRowExchange(n, env.rank, env.world_size, dev)
+            self.row_tracker = RowTracker(n)
+        self.optimizer = NorMuonAndAdam(
+            model.named_parameters(), self.param_table, list(self.param_table), self.work_order,
+            adam_defaults=dict(lr=hp.adam_lr, eps=hp.adam_eps, weight_decay=hp.adam_wd),
+            normuon_defaults=dict(lr=hp.muon_lr, momentum=hp.muon_momentum, beta2=hp.muon_beta2, weight_decay=hp.muon_wd),
+            collectives=collectives or TorchCollectives(), math=math, sparse_exchange=self.sparse,
+            rank=env.rank, world_size=env.world_size)
+        self.split_step = schedule.split_step
+        self.device = dev
+        self.reset()
+
+    # -- schedule ------------------------------------------------------------------------
+    def apply_final_ws_ext(self):
+        self.ws_long = self.schedule.ws_post_yarn_ext
+
+    def get_forward_args(self) -> ForwardScheduleConfig:
+        return ForwardScheduleConfig(self.mtp_weights, self.prefix_weight, self.ws_short * self.block_size,
+                                     self.ws_long * self.block_size, self.train_max_seq_len)
+
+    @staticmethod
+    def is_adam_step(step: int) -> bool:
+        return step % 2 == 1
+
+    def get_transition_steps(self):
+        return self.schedule.transition_steps()
+
+    def advance_schedule(self, step: int):
+        stage, _ = self.schedule.lookup(step)
+        self.ws_short, new_long = stage.window_sizes
+        if new_long != self.ws_long:
+            for y in (self.model.yarn, self.model.yarn_paired_head):
+                y.apply(self.ws_long * self.block_size, new_long * self.block_size)
+        if stage.batch_size != self.batch_size or stage.train_max_seq_len != self.train_max_seq_len:
+            self.train_loader_send_args = (stage.batch_size, stage.train_max_seq_len, self.env.grad_accum_steps)
+            self.batch_size, self.train_max_seq_len = stage.batch_size, stage.train_max_seq_len
+        else:
+            self.train_loader_send_args = None
+        self.ws_long = new_long
+        self.mtp_weights = torch.tensor(self.schedule.mtp_weights[step], dtype=torch.float32, device=self.device)
+        self.prefix_weight = torch.tensor([self.schedule.prefix_weights[step]], dtype=torch.float32, device=self.device)
+
+    def step_optimizers(self, step: int):
+        lr_mul = self.schedule.get_lr(step)
+        mom = self.schedule.muon_momentum(step)
+        for c in self.optimizer.cfgs.values():
+            c.lr = c.initial_lr * lr_mul
+            if c.optim == "normuon":
+                c.momentum = mom
+        self.optimizer.step(do_adam=self.is_adam_step(step))
+        if step == self.split_step and "embed" in self.optimizer.params:
+            self.optimizer.copy_lm_state_to_embed()
+
+    def reset(self, state=None):
+        if state is not None:
+            self.optimizer.load_state_dict(state)
+        self.optimizer.reset()
+        stage, _ = self.schedule.lookup(0)
+        self.ws_short, self.ws_long = stage.window_sizes
+        self.batch_size, self.train_max_seq_len = stage.batch_size, stage.train_max_seq_len
+        self.train_loader_send_args = None
+        self.model.yarn.reset()
+        self.model.yarn_paired_head.reset()
+        if self.row_tracker is not None:
+            self.row_tracker.mask.fill(0)
+
+    def get_state(self):
+        return copy.deepcopy(self.optimizer.state_dict())
+
+    # -- sparse bigram rows --------------------------------------------------------------
+    def sparse_index_update(self, step: int, bigram_rows: np.ndarray):
+        if self.sparse is None:
+            return
+        self.row_tracker.mark(bigram_rows)
+        if self.is_adam_step(step):
+            self.sparse.start(self.row_tracker.peek())
+
+    def sparse_index_share(self, step: int):
+        if self.sparse is None or not self.is_adam_step(step):
+            return
+        self.sparse.share_indexes()
+        self.row_tracker.mask.fill(0)
+
+
+@dataclass
+class StepStats:
+    loss: float
+    device_ms: float
+
+
+class Trainer:
+    """Public engine.  `Trainer(model_cfg, schedule, hp, env)`; `train_step(step)` runs
+    grad_accum micro-batches (H2D copy of the inputs, forward, backward), the optimizer step and
+    the FP8 weight refresh; `validate()` the evaluation pass; `run()` the whole schedule."""
+
+    def __init__(self, model_cfg: ModelConfig | None, schedule: TrainingSchedule | None, hp: Hyperparameters,
+                 env: DistEnv, *, param_dtype=torch.bfloat16, collectives=None, math=None, logger=None,
+                 model: GPT | None = None, sparse_min_world: int = 8, use_cuda_graphs: bool | None = None):
+        self.hp, self.env = hp, env
+        self.schedule = schedule or TrainingSchedule(track1_stages(), hp.num_scheduled_iterations,
+                                                     hp.num_extension_iterations, cooldown_frac=hp.cooldown_frac)
+        eval_seq = hp.val_batch_size // (env.grad_accum_steps * env.world_size)
+        model_cfg = model_cfg or track1_model(eval_seq)
+        torch.manual_seed(hp.seed)
+        self.model = model or GPT(model_cfg, world_size=env.world_size, grad_scale=env.grad_scale,
+                                  use_fp8=not hp.disable_fp8, eval_seq_len=eval_seq)
+        self.model.to(env.device)
+        if param_dtype != torch.float32:
+            self.model.cast_params_(param_dtype)
+        broadcast_model(self.model)
+        if env.device.type == "cuda" and collectives is None and math is None:
+            from .parallel.nvlink import make_device_backends
+            collectives, math = make_device_backends(self.model, env)
+        self.manager = TrainingManager(self.model, self.schedule, hp, env, collectives, math, sparse_min_world)
+        self.model.quantize_mlp_fp8(bootstrap_down=True)
+        self.log = logger or RunLogger(hp.run_id, env.master)
+        self.train_loader = None
+        self.step = 0
+        self.training_time_ms = 0.0
+        self._bigram_vocab = model_cfg.bigram_vocab_size
+        self.model.train()
+
+    # -- data ----------------------------------------------------------------------------
+    def make_train_loader(self):
+        st = self.schedule.stages[0]
+        return TokenLoader(self.hp.train_files, st.batch_size, st.train_max_seq_len, self.env.grad_accum_steps,
+                           True, self.env.rank, self.env.world_size, self.env.device, self._bigram_vocab)
+
+    def make_val_loader(self):
+        return TokenLoader(self.hp.val_files, self.hp.val_batch_size, -1, self.env.grad_accum_steps, False,
+                           self.env.rank, self.env.world_size, self.env.device, self._bigram_vocab)
+
+    # -- one optimizer step ----------------------------------------------------------------
+    def micro_step(self, batch, step: int) -> torch.Tensor:
+        m = self.manager
+        m.sparse_index_update(step, batch.bigram_cpu)
+        losses = self.model(batch.inputs, batch.targets, batch.cum_seqlens, batch.bigram_inputs, m.get_forward_args())
+        loss = losses.sum() * self.env.grad_scale
+        m.sparse_index_share(step)
+        loss.backward()
+        return loss.detach()
+
+    def train_step(self, step: int | None = None) -> torch.Tensor:
+        """Returns the (detached, device) sum-loss of the step's micro-batches."""
+        step = self.step if step is None else step
+        if self.train_loader is None:
+            self.train_loader = self.make_train_loader()
+        self.manager.advance_schedule(step)
+        total = None
+        for _ in range(self.env.grad_accum_steps):
+            batch = self.train_loader.next_batch(self.manager.train_loader_send_args)
+            self.manager.train_loader_send_args = None
+            l = self.micro_step(batch, step)
+            total = l if total is None else total + l
+        self.manager.step_optimizers(step)
+        self.model.quantize_mlp_fp8(bootstrap_down=(step < 16))
+        self.step = step + 1
+        return total
+
+    @torch.no_grad()
+    def validate(self, val_tokens: int | None = None) -> torch.Tensor:
+        hp, env = self.hp, self.env
+        val_tokens = val_tokens or hp.val_tokens
+        assert val_tokens % hp.val_batch_size == 0
+        steps = env.grad_accum_steps * val_tokens // hp.val_batch_size
+        loader = self.make_val_loader()
+        self.model.eval()
+        tot = 0
+        for _ in range(steps):
+            b = loader.next_batch()
+            tot = tot + self.model(b.inputs, b.targets, b.cum_seqlens, b.bigram_inputs, self.manager.get_forward_args()).mean()
+        tot = tot / steps
+        if dist.is_initialized() and env.world_size > 1:
+            dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+            tot = tot / env.world_size
+        self.model.train()
+        return tot
+
+    # -- checkpoint ------------------------------------------------------------------------
+    def save_checkpoint(self, path: str | None = None):
+        from .utils.checkpoint import save_checkpoint
+        return save_checkpoint(self, path)
+
+    def load_checkpoint(self, path: str):
+        from .utils.checkpoint import load_checkpoint
+        return load_checkpoint(self, path)
+
+    # -- the whole run -----------------------------------------------------------------------
+    def _sync(self):
+        if self.env.device.type == "cuda":
+            torch.cuda.synchronize()
+
+    def warmup(self):
+        """Run real steps at both ends of every stage transition so that every kernel variant
+        and CUDA graph exists before the clock starts, then restore the initial state
+        (`train_gpt.py:2264-2301`)."""
+        m = self.manager
+        init = dict(model=copy.deepcopy(self.model.state_dict()), optimizer=m.get_state())
+        self.train_loader = self.make_train_loader()
+        val_loader = self.make_val_loader()
+        trans = m.get_transition_steps()
+        steps = sorted({0, 1} | {s + o for s in trans for o in (-2, -1, 0, 1) if s + o >= 2})
+        self.log.print0(f"Sampling steps {steps} for warmup", console=True)
+        for step in steps:
+            m.advance_schedule(step)
+            self.model.eval()
+            with torch.no_grad():
+                b = val_loader.next_batch()
+                self.model(b.inputs, b.targets, b.cum_seqlens, b.bigram_inputs, m.get_forward_args()).mean()
+            self.model.train()
+            for _ in range(self.env.grad_accum_steps):
+                batch = self.train_loader.next_batch(m.train_loader_send_args)
+                m.train_loader_send_args = None
+                self.micro_step(batch, step)
+            m.step_optimizers(step)
+            self.model.quantize_mlp_fp8(bootstrap_down=True)
+        self.log.print0("Resetting Model", console=True)
+        self.model.zero_grad(set_to_none=True)
+        self.model.load_state_dict(init["model"])
+        m.reset(init["optimizer"])
+        self.model.quantize_mlp_fp8(bootstrap_down=True)
+        self.model.train()
+        self.train_loader = None
+        self.step = 0
+
+    def run(self, do_warmup: bool = True, start_step: int = 0):
+        hp, env, m, log = self.hp, self.env, self.manager, self.log
+        if do_warmup and start_step == 0:
+            self.warmup()
+        if self.train_loader is None:
+            self.train_loader = self.make_train_loader()
+        total = self.schedule.total_steps if not hp.max_steps else min(hp.max_steps, self.schedule.total_steps)
+        from .data.prefix import build_prefix_table
+        self._sync()
+        t0 = time.perf_counter()
+        if start_step == 0:
+            self.model.prefix_table.copy_(build_prefix_table(self.model.vocab_size))
+        val_loss = None
+        for step in range(start_step, total + 1):
+            last = step == total
+            m.advance_schedule(step)
+            if last or (hp.val_loss_every > 0 and step % hp.val_loss_every == 0):
+                if last and total == self.schedule.total_steps:
+                    m.apply_final_ws_ext()
+                self._sync()
+                self.training_time_ms += 1000 * (time.perf_counter() - t0)
+                val_loss = float(self.validate())
+                log.print0(f"step:{step}/{total} val_loss:{val_loss:.4f} train_time:{self.training_time_ms:.0f}ms "
+                           f"step_avg:{self.training_time_ms / max(step, 1):.2f}ms", console=True)
+                self._sync()
+                t0 = time.perf_counter()
+            if last:
+                if hp.save_checkpoint:
+                    self.save_checkpoint()
+                break
+            self.train_step(step)
+            approx = self.training_time_ms + 1000 * (time.perf_counter() - t0)
+            log.print0(f"step:{step + 1}/{total} train_time:{approx:.0f}ms step_avg:{approx / (step + 1):.2f}ms", console=True)
+        if env.device.type == "cuda":
+            log.print0(f"peak memory allocated: {torch.cuda.max_memory_allocated() // 1024 // 1024} MiB "
+                       f"reserved: {torch.cuda.max_memory_reserved() // 1024 // 1024} MiB", console=True)
+        return val_loss
