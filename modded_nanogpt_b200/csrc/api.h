@@ -1,0 +1,98 @@
+// C interface between the CUDA translation units and the Python binding.  Plain pointers and
+// integers only, so the .cu files compile without the PyTorch headers.
+#pragma once
+#include <stdint.h>
+#include "comm.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { MNG_BF16 = 0, MNG_E4M3 = 1, MNG_E5M2 = 2 };
+enum { MNG_EPI_STORE = 0, MNG_EPI_RELU2 = 1, MNG_EPI_DPRE = 2 };
+
+// D[b] = epi(A[b] (MxK) * B[b]^T (NxK)).  a_mn / b_mn: operand is stored [K, rows] instead of [rows, K].
+typedef struct {
+  const void* a;
+  const void* b;
+  int M, N, K, batch;
+  int dtype_a, dtype_b;
+  int a_mn, b_mn;
+  long long lda, ldb;                 // row stride of the stored arrays, in elements
+  long long a_bstride, b_bstride;     // batch strides in elements
+  int epilogue;
+  int bn;                             // CTA tile width: 128 or 256
+  int out_f32;
+  void* out;
+  long long ldc, c_bstride;
+  const void* cin;                    // STORE: addend (beta); DPRE: saved post activations
+  float alpha, beta;
+  const float* alpha_ptr;             // optional device scalar folded into alpha
+  const float* row_scale;
+  const float* col_scale;
+  void* out8;                         // RELU2: e4m3 copy of the output
+  const float* act_scale;
+  unsigned int* amax_bits;
+  int max_ctas;                       // 0 = one CTA per SM
+  void* stream;
+  uint32_t* status;
+} GemmDesc;
+
+int mng_gemm(const GemmDesc* g);
+
+// ---- pointwise / normalisation (pointwise.cu) ---------------------------------------------------
+// y = x / rms(x) per row of `cols` bf16 elements; optional e4m3 copy with one scale per row
+// (scale = amax/448) for the row-scaled FP8 GEMMs.
+int mng_rmsnorm_fwd(const void* x, void* y, void* y8, float* row_scale, float* rstd, long long rows, int cols, void* stream);
+int mng_rmsnorm_bwd(const void* x, const void* dy, const float* rstd, void* dx, long long rows, int cols, int accumulate,
+                    void* stream);
+// Row-wise e4m3 quantisation: q = x / s, s[r] = amax(x[r,:])/448 (bf16 in).
+int mng_quant_rows_e4m3(const void* x, void* q, float* scale, long long rows, int cols, void* stream);
+// dst[c, r] = src[r, c] (optionally += ), bf16; 32x32 tiles through shared memory.
+int mng_transpose_bf16(const void* src, void* dst, long long rows, long long cols, int accumulate, void* stream);
+// Row-scaled e4m3 quantisation of the transpose: q[c, :] = src[:, c] / s[c], s[c] = amax(src[:, c]) / 448.
+// `amax_scratch`: `cols` 32-bit words of scratch memory owned by the caller.
+int mng_quant_transpose_e4m3(const void* src, void* q, float* scale, unsigned int* amax_scratch, long long rows,
+                             long long cols, void* stream);
+
+// ---- softcapped cross entropy (ce.cu) -------------------------------------------------------------
+// One CTA per token row: z = A*sigmoid((logit+B)/C), loss = sum_k w_k (lse - z[t_{i+k}]) + w_p (lse - z[p_i]),
+// dlogits (e5m2 or bf16) = grad_mul * d loss / d logit.
+int mng_softcap_ce(const void* logits_bf16, const long long* targets, const float* mtp_weights, int n_predict,
+                   const long long* prefix_targets, const float* prefix_weight, float* losses, void* dlogits,
+                   int dlogits_is_e5m2, long long rows, int vocab, long long ld_logits, float A, float B, float C,
+                   float grad_mul, void* stream);
+
+// ---- optimizer (optim.cu) ---------------------------------------------------------------------------
+// Gradients are summed over `grads.n` ranks' buffers (peer pointers) and scaled by grad_mul; updated
+// values are stored to every buffer in `params`.  `off` = element offset of this rank's shard.
+typedef struct {
+  PeerPtrs grads;
+  PeerPtrs params;
+  long long off;
+  float* exp_avg;
+  float* exp_avg_sq;
+  long long n;
+  int p_is_f32;
+  float beta1, beta2, eps, step_size, eff_wd, grad_mul;
+} AdamDesc;
+int mng_adam(const AdamDesc* d, void* stream);
+
+//   g = bf16(grad_mul * sum_r grads[r]); buf = lerp(buf, g, 1-mu); u = lerp(g, buf, mu);
+//   out = bf16(u); sumsq[mat] = sum(out^2)
+int mng_nesterov(const PeerPtrs* grads, long long off, float* buf, void* out_bf16, float* sumsq, long long mats,
+                 long long per_mat, float momentum, float grad_mul, void* stream);
+// x[mat] /= bf16(bf16(||x[mat]||_F) * 1.02) + 1e-6   (bf16, in place)
+int mng_scale_by_norm(void* x_bf16, const float* sumsq, long long mats, long long per_mat, void* stream);
+// NorMuon second-moment normalisation + cautious weight decay on bf16 weight + uint16 mantissa.
+//   red_rows != 0: statistics per row (reduce over columns), else per column (reduce over rows).
+//   scale_scratch: mats * max(rows, cols) floats of scratch.
+int mng_normuon_apply(const PeerPtrs* params, long long off, void* mantissa_u16, const void* v_bf16, float* second_mom,
+                      float* scale_scratch, long long mats, int rows, int cols, int red_rows, float beta2, float eff_wd,
+                      const float* eff_lr_per_mat, void* stream);
+// Barrier across ranks on signal pads (bounded wait; sets *status on expiry).
+int mng_peer_barrier(const PeerPtrs* pads, int rank, uint32_t epoch, uint32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,166 @@
+// Softcapped cross-entropy, forward and gradient in one pass over the logits.
+//
+// One CTA per token row.  z = A*sigmoid((logit+B)/C) is bounded by A, so the log-sum-exp needs no
+// running maximum: sum_j exp(z_j - A) stays within fp32 range.  The row of sigmoids is parked in
+// shared memory as bf16 (vocab*2 bytes) between the reduction and the gradient sweep, so the
+// logits are read from HBM exactly once and the gradient is written exactly once:
+//   loss_i  = sum_k w_k (lse - z[t_{i+k}]) + w_p (lse - z[p_i])            (k < n_predict, i+k < rows)
+//   dlogit  = grad_mul * (A/C) * (S_w * softmax(z) - [targets]) * s(1-s)
+// Same contract as the reference kernel `triton_kernels.py:914-1171` (S_w sums all MTP weights,
+// targets past the end of the batch drop out of the loss but not of S_w, prefix target < 0 = none).
+#include "api.h"
+#include "ptx.cuh"
+
+namespace mng {
+
+constexpr int CE_THREADS = 256;
+constexpr int CE_MAX_PREDICT = 8;
+
+__device__ __forceinline__ float fast_sigmoid(float u) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u * 0.5f));
+  return 0.5f + 0.5f * t;
+}
+
+template <bool OUT_E5M2>
+__global__ void __launch_bounds__(CE_THREADS, 2)
+softcap_ce_kernel(const __nv_bfloat16* __restrict__ logits, const long long* __restrict__ targets,
+                  const float* __restrict__ mtp_weights, int n_predict, const long long* __restrict__ prefix_targets,
+                  const float* __restrict__ prefix_weight_ptr, float* __restrict__ losses, void* __restrict__ dlogits,
+                  long long rows, int vocab, long long ld, float A, float B, float C, float grad_mul) {
+  extern __shared__ __nv_bfloat16 sig[];
+  __shared__ float red[CE_THREADS / 32];
+  __shared__ float s_lse;
+  const long long row = blockIdx.x;
+  const __nv_bfloat16* lrow = logits + row * ld;
+  const float inv_c = 1.f / C, b_over_c = B / C;
+  const int nvec = vocab >> 3;
+
+  float part = 0.f;
+  for (int i = threadIdx.x; i < nvec; i += CE_THREADS) {
+    uint4 u = *reinterpret_cast<const uint4*>(lrow + i * 8);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+    uint4 w;
+    uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      float2 f = __bfloat1622float2(h[t]);
+      __nv_bfloat162 s2 = __floats2bfloat162_rn(fast_sigmoid(f.x * inv_c + b_over_c), fast_sigmoid(f.y * inv_c + b_over_c));
+      wp[t] = *reinterpret_cast<uint32_t*>(&s2);
+      float2 s = __bfloat1622float2(s2);
+      part += __expf(A * s.x - A) + __expf(A * s.y - A);
+    }
+    *reinterpret_cast<uint4*>(sig + i * 8) = w;
+  }
+  part = warp_sum(part);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = part;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < CE_THREADS / 32; ++i) tot += red[i];
+    s_lse = A + __logf(tot);
+  }
+  __syncthreads();
+  const float lse = s_lse;
+
+  const float prefix_weight = prefix_weight_ptr ? prefix_weight_ptr[0] : 0.f;
+  const long long ptgt = prefix_targets ? prefix_targets[row] : -1;
+  const bool pvalid = ptgt >= 0 && ptgt < vocab;
+  float S_w = pvalid ? prefix_weight : 0.f;
+  for (int k = 0; k < n_predict; ++k) S_w += mtp_weights[k];
+
+  if (threadIdx.x == 0) {
+    float loss = 0.f;
+    for (int k = 0; k < n_predict; ++k) {
+      const long long ti = row + k;
+      if (ti < rows) {
+        const long long t = targets[ti];
+        if (t >= 0 && t < vocab) loss += mtp_weights[k] * (lse - A * __bfloat162float(sig[t]));
+      }
+    }
+    if (pvalid) loss += prefix_weight * (lse - A * __bfloat162float(sig[ptgt]));
+    losses[row] = loss;
+  }
+
+  const float gscale = grad_mul * (A * inv_c);
+  for (int i = threadIdx.x; i < nvec; i += CE_THREADS) {
+    uint4 u = *reinterpret_cast<const uint4*>(sig + i * 8);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+    float g[8];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      float2 s = __bfloat1622float2(h[t]);
+      g[2 * t] = gscale * S_w * __expf(A * s.x - lse) * s.x * (1.f - s.x);
+      g[2 * t + 1] = gscale * S_w * __expf(A * s.y - lse) * s.y * (1.f - s.y);
+    }
+    if constexpr (OUT_E5M2) {
+      uint2 w;
+      w.x = pack_e5m2x2(g[0], g[1]) | ((uint32_t)pack_e5m2x2(g[2], g[3]) << 16);
+      w.y = pack_e5m2x2(g[4], g[5]) | ((uint32_t)pack_e5m2x2(g[6], g[7]) << 16);
+      *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(dlogits) + row * ld + i * 8) = w;
+    } else {
+      uint4 w;
+      w.x = pack_bf16x2(g[0], g[1]); w.y = pack_bf16x2(g[2], g[3]); w.z = pack_bf16x2(g[4], g[5]); w.w = pack_bf16x2(g[6], g[7]);
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(dlogits) + row * ld + i * 8) = w;
+    }
+  }
+  __syncthreads();
+
+  // Target columns: subtract the weights of every prediction that lands on the column.  Threads
+  // that hit the same column compute the same value, so concurrent writes agree.
+  if (threadIdx.x <= n_predict) {
+    const int i = threadIdx.x;
+    long long tgt = -1;
+    bool valid;
+    if (i < n_predict) {
+      valid = row + i < rows;
+      if (valid) tgt = targets[row + i];
+      valid = valid && tgt >= 0 && tgt < vocab;
+    } else {
+      tgt = ptgt;
+      valid = pvalid;
+    }
+    if (valid) {
+      const float s = __bfloat162float(sig[tgt]);
+      float hit = 0.f;
+      for (int k = 0; k < n_predict; ++k)
+        if (row + k < rows && targets[row + k] == tgt) hit += mtp_weights[k];
+      if (pvalid && ptgt == tgt) hit += prefix_weight;
+      const float gv = gscale * (S_w * __expf(A * s - lse) - hit) * s * (1.f - s);
+      if constexpr (OUT_E5M2)
+        reinterpret_cast<uint8_t*>(dlogits)[row * ld + tgt] = (uint8_t)(pack_e5m2x2(gv, 0.f) & 0xff);
+      else
+        reinterpret_cast<__nv_bfloat16*>(dlogits)[row * ld + tgt] = __float2bfloat16(gv);
+    }
+  }
+}
+
+}  // namespace mng
+
+using namespace mng;
+
+extern "C" int mng_softcap_ce(const void* logits, const long long* targets, const float* mtp_weights, int n_predict,
+                              const long long* prefix_targets, const float* prefix_weight, float* losses, void* dlogits,
+                              int dlogits_is_e5m2, long long rows, int vocab, long long ld, float A, float B, float C,
+                              float grad_mul, void* stream) {
+  if (rows == 0) return 0;
+  if (vocab % 8 || ld % 8 || n_predict > CE_MAX_PREDICT || n_predict < 1) return -1;
+  const size_t smem = (size_t)vocab * 2;
+  if (smem > 200 * 1024) return -2;
+  cudaError_t e;
+  if (dlogits_is_e5m2) {
+    static bool set = false;
+    if (!set) { e = cudaFuncSetAttribute(softcap_ce_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); if (e) return -3; set = true; }
+    softcap_ce_kernel<true><<<(unsigned)rows, CE_THREADS, smem, (cudaStream_t)stream>>>(
+        (const __nv_bfloat16*)logits, targets, mtp_weights, n_predict, prefix_targets, prefix_weight, losses, dlogits, rows, vocab,
+        ld, A, B, C, grad_mul);
+  } else {
+    static bool set = false;
+    if (!set) { e = cudaFuncSetAttribute(softcap_ce_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); if (e) return -3; set = true; }
+    softcap_ce_kernel<false><<<(unsigned)rows, CE_THREADS, smem, (cudaStream_t)stream>>>(
+        (const __nv_bfloat16*)logits, targets, mtp_weights, n_predict, prefix_targets, prefix_weight, losses, dlogits, rows, vocab,
+        ld, A, B, C, grad_mul);
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}

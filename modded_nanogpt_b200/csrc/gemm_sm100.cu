@@ -1,0 +1,337 @@
+// Epilogues, tensor-map construction and host launcher for the tcgen05 GEMM (gemm_sm100.cuh).
+#include "api.h"
+#include "gemm_sm100.cuh"
+
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+namespace mng {
+
+// ================================== epilogues =====================================================
+
+// out = alpha * acc * row_scale[m] * col_scale[n] + beta * Cin[m,n]   (bf16 or fp32 output)
+template <bool OUT_F32>
+struct EpiStore {
+  struct Params {
+    void* out;
+    const void* cin;            // same dtype/layout as out; may alias out
+    const float* row_scale;     // [batch*M] or null
+    const float* col_scale;     // [batch*N] or null
+    const float* alpha_ptr;     // optional device scalar multiplied into alpha
+    long long ld, bstride;      // elements
+    float alpha, beta;
+  };
+  __device__ static void apply(const Params& p, const float (&acc)[32], int b, int row, int col0, int M, int N) {
+    if (row >= M) return;
+    float a = p.alpha;
+    if (p.alpha_ptr) a *= *p.alpha_ptr;
+    if (p.row_scale) a *= p.row_scale[(long long)b * M + row];
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = acc[j] * a;
+    if (p.col_scale) {
+      const float* cs = p.col_scale + (long long)b * N + col0;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] *= (col0 + j < N) ? cs[j] : 0.f;
+    }
+    const long long off = (long long)b * p.bstride + (long long)row * p.ld + col0;
+    const bool full = (col0 + 32 <= N);
+    if constexpr (OUT_F32) {
+      float* o = reinterpret_cast<float*>(p.out) + off;
+      if (p.beta != 0.f) {
+        const float* ci = reinterpret_cast<const float*>(p.cin) + off;
+        if (full) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            float4 c = *reinterpret_cast<const float4*>(ci + j);
+            v[j] += p.beta * c.x; v[j + 1] += p.beta * c.y; v[j + 2] += p.beta * c.z; v[j + 3] += p.beta * c.w;
+          }
+        } else {
+          for (int j = 0; j < 32; ++j) if (col0 + j < N) v[j] += p.beta * ci[j];
+        }
+      }
+      if (full) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+      } else {
+        for (int j = 0; j < 32; ++j) if (col0 + j < N) o[j] = v[j];
+      }
+    } else {
+      __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + off;
+      if (p.beta != 0.f) {
+        const __nv_bfloat16* ci = reinterpret_cast<const __nv_bfloat16*>(p.cin) + off;
+        if (full) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            uint4 c = *reinterpret_cast<const uint4*>(ci + j);
+            const __nv_bfloat162* c2 = reinterpret_cast<const __nv_bfloat162*>(&c);
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              float2 f = __bfloat1622float2(c2[t]);
+              v[j + 2 * t] += p.beta * f.x;
+              v[j + 2 * t + 1] += p.beta * f.y;
+            }
+          }
+        } else {
+          for (int j = 0; j < 32; ++j) if (col0 + j < N) v[j] += p.beta * __bfloat162float(ci[j]);
+        }
+      }
+      if (full) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          uint4 w;
+          w.x = pack_bf16x2(v[j], v[j + 1]); w.y = pack_bf16x2(v[j + 2], v[j + 3]);
+          w.z = pack_bf16x2(v[j + 4], v[j + 5]); w.w = pack_bf16x2(v[j + 6], v[j + 7]);
+          *reinterpret_cast<uint4*>(o + j) = w;
+        }
+      } else {
+        for (int j = 0; j < 32; ++j) if (col0 + j < N) o[j] = __float2bfloat16(v[j]);
+      }
+    }
+  }
+};
+
+// MLP up projection: pre = acc * row_scale[m] * col_scale[n] rounded to bf16; post = relu(pre)^2 in
+// bf16 (store); e4m3 copy min(post / act_scale, 448) (store); running max of post -> amax (atomic).
+struct EpiRelu2 {
+  struct Params {
+    __nv_bfloat16* post;
+    uint8_t* post8;             // may be null
+    const float* row_scale;
+    const float* col_scale;
+    const float* act_scale;     // device scalar
+    unsigned int* amax_bits;    // device scalar, float bits (values are >= 0 so integer max works)
+    long long ld;
+  };
+  __device__ static void apply(const Params& p, const float (&acc)[32], int b, int row, int col0, int M, int N) {
+    // N is a multiple of 32 for this epilogue (checked on the host).  Rows past M stay in the warp
+    // (the amax reduction below is a warp collective) with their stores predicated off.
+    const bool live = row < M;
+    if (!live) row = M - 1;
+    const float rs = p.row_scale ? p.row_scale[row] : 1.f;
+    float post[32];
+    float mx = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float cs = p.col_scale ? p.col_scale[col0 + j] : 1.f;
+      float pre = __bfloat162float(__float2bfloat16(acc[j] * rs * cs));
+      float r = fmaxf(pre, 0.f);
+      float q = __bfloat162float(__float2bfloat16(r * r));
+      post[j] = q;
+      mx = fmaxf(mx, q);
+    }
+    if (!live) mx = 0.f;
+    __nv_bfloat16* o = p.post + (long long)row * p.ld + col0;
+#pragma unroll
+    for (int j = 0; live && j < 32; j += 8) {
+      uint4 w;
+      w.x = pack_bf16x2(post[j], post[j + 1]); w.y = pack_bf16x2(post[j + 2], post[j + 3]);
+      w.z = pack_bf16x2(post[j + 4], post[j + 5]); w.w = pack_bf16x2(post[j + 6], post[j + 7]);
+      *reinterpret_cast<uint4*>(o + j) = w;
+    }
+    if (p.post8) {
+      const float inv = 1.f / *p.act_scale;
+      uint8_t* o8 = p.post8 + (long long)row * p.ld + col0;
+#pragma unroll
+      for (int j = 0; live && j < 32; j += 16) {
+        uint32_t w[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          uint32_t lo = pack_e4m3x2(post[j + 4 * t] * inv, post[j + 4 * t + 1] * inv);
+          uint32_t hi = pack_e4m3x2(post[j + 4 * t + 2] * inv, post[j + 4 * t + 3] * inv);
+          w[t] = lo | (hi << 16);
+        }
+        *reinterpret_cast<uint4*>(o8 + j) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      mx = warp_max(mx);
+      if ((threadIdx.x & 31) == 0 && mx > 0.f) atomicMax(p.amax_bits, __float_as_uint(mx));
+    }
+  }
+};
+
+// MLP backward: dpre = bf16( 2 * bf16(acc) * sqrt(post) ) with post = relu(pre)^2 saved by the forward.
+struct EpiDpre {
+  struct Params {
+    __nv_bfloat16* out;
+    const __nv_bfloat16* post;
+    long long ld;
+  };
+  __device__ static void apply(const Params& p, const float (&acc)[32], int b, int row, int col0, int M, int N) {
+    if (row >= M) return;
+    const long long off = (long long)row * p.ld + col0;
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      uint4 c = *reinterpret_cast<const uint4*>(p.post + off + j);
+      const __nv_bfloat162* c2 = reinterpret_cast<const __nv_bfloat162*>(&c);
+      float o[8];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        float2 f = __bfloat1622float2(c2[t]);
+        o[2 * t] = 2.f * __bfloat162float(__float2bfloat16(acc[j + 2 * t])) * sqrtf(f.x);
+        o[2 * t + 1] = 2.f * __bfloat162float(__float2bfloat16(acc[j + 2 * t + 1])) * sqrtf(f.y);
+      }
+      uint4 w;
+      w.x = pack_bf16x2(o[0], o[1]); w.y = pack_bf16x2(o[2], o[3]);
+      w.z = pack_bf16x2(o[4], o[5]); w.w = pack_bf16x2(o[6], o[7]);
+      *reinterpret_cast<uint4*>(p.out + off + j) = w;
+    }
+  }
+};
+
+// ================================== tensor maps ====================================================
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 3-D map {inner, outer, batch} of a row-major [batch][outer][inner] array with 128-byte swizzle.
+// box = {box_inner, box_outer, 1}.  Returns 0 on success.
+int make_tensor_map(CUtensorMap* out, const void* ptr, int elem_size, long long inner, long long outer, long long batch,
+                    long long ld_elems, long long bstride_elems, int box_inner, int box_outer) {
+  EncodeTiledFn enc = get_encode();
+  if (!enc) return -1;
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || ((ld_elems * elem_size) & 15) || ((bstride_elems * elem_size) & 15)) return -2;
+  if (box_inner * elem_size != 128 || box_outer > 256) return -3;
+  cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)outer, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld_elems * elem_size), (cuuint64_t)((batch > 1 ? bstride_elems : ld_elems * outer) * elem_size)};
+  cuuint32_t box[3] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUtensorMapDataType dt = elem_size == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  CUresult r = enc(out, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -100 - (int)r;
+}
+
+struct MapKey {
+  const void* p; int es; long long a, b, c, ld, bs; int bi, bo;
+  bool operator<(const MapKey& o) const {
+    return std::tie(p, es, a, b, c, ld, bs, bi, bo) < std::tie(o.p, o.es, o.a, o.b, o.c, o.ld, o.bs, o.bi, o.bo);
+  }
+};
+
+static int cached_map(CUtensorMap* out, const void* ptr, int es, long long inner, long long outer, long long batch,
+                      long long ld, long long bs, int bi, int bo) {
+  static std::map<MapKey, CUtensorMap> cache;
+  static std::mutex mu;
+  MapKey k{ptr, es, inner, outer, batch, ld, bs, bi, bo};
+  std::lock_guard<std::mutex> g(mu);
+  auto it = cache.find(k);
+  if (it == cache.end()) {
+    CUtensorMap m;
+    int rc = make_tensor_map(&m, ptr, es, inner, outer, batch, ld, bs, bi, bo);
+    if (rc) return rc;
+    if (cache.size() > 4096) cache.clear();
+    it = cache.emplace(k, m).first;
+  }
+  *out = it->second;
+  return 0;
+}
+
+// ================================== launcher =======================================================
+
+static int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int BN, int ES, bool A_MN, bool B_MN, uint32_t AF, uint32_t BF, class Epi>
+static int launch_one(const GemmDesc& g, const typename Epi::Params& ep, int max_ctas) {
+  using SM = GemmSmem<BN, ES>;
+  constexpr int BK = GEMM_STAGE_K_BYTES / ES;
+  CUtensorMap ma, mb;
+  int rc;
+  if (!A_MN) rc = cached_map(&ma, g.a, ES, g.K, g.M, g.batch, g.lda, g.a_bstride, BK, GEMM_BM);
+  else rc = cached_map(&ma, g.a, ES, g.M, g.K, g.batch, g.lda, g.a_bstride, 128 / ES, BK);
+  if (rc) return rc;
+  if (!B_MN) rc = cached_map(&mb, g.b, ES, g.K, g.N, g.batch, g.ldb, g.b_bstride, BK, BN);
+  else rc = cached_map(&mb, g.b, ES, g.N, g.K, g.batch, g.ldb, g.b_bstride, 128 / ES, BK);
+  if (rc) return rc - 1000;
+  auto kern = gemm_tcgen05_kernel<BN, ES, A_MN, B_MN, AF, BF, Epi>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::TOTAL);
+    if (e != cudaSuccess) return -2000 - (int)e;
+    attr_set = true;
+  }
+  const int tiles = ((g.M + GEMM_BM - 1) / GEMM_BM) * ((g.N + BN - 1) / BN) * g.batch;
+  int grid = tiles < num_sms() ? tiles : num_sms();
+  if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
+  GemmShape shape{g.M, g.N, g.K, g.batch};
+  kern<<<grid, GEMM_THREADS, SM::TOTAL, (cudaStream_t)g.stream>>>(ma, mb, shape, ep, g.status);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : -3000 - (int)e;
+}
+
+template <int ES, bool A_MN, bool B_MN, uint32_t AF, uint32_t BF>
+static int launch_store(const GemmDesc& g) {
+  if (g.out_f32) {
+    EpiStore<true>::Params p{g.out, g.cin, g.row_scale, g.col_scale, g.alpha_ptr, g.ldc, g.c_bstride, g.alpha, g.beta};
+    return g.bn == 256 ? launch_one<256, ES, A_MN, B_MN, AF, BF, EpiStore<true>>(g, p, g.max_ctas)
+                       : launch_one<128, ES, A_MN, B_MN, AF, BF, EpiStore<true>>(g, p, g.max_ctas);
+  }
+  EpiStore<false>::Params p{g.out, g.cin, g.row_scale, g.col_scale, g.alpha_ptr, g.ldc, g.c_bstride, g.alpha, g.beta};
+  return g.bn == 256 ? launch_one<256, ES, A_MN, B_MN, AF, BF, EpiStore<false>>(g, p, g.max_ctas)
+                     : launch_one<128, ES, A_MN, B_MN, AF, BF, EpiStore<false>>(g, p, g.max_ctas);
+}
+
+}  // namespace mng
+
+using namespace mng;
+
+extern "C" int mng_gemm(const GemmDesc* gp) {
+  const GemmDesc& g = *gp;
+  if (g.M <= 0 || g.N <= 0 || g.K <= 0 || g.batch <= 0) return -10;
+  const int es = g.dtype_a == MNG_BF16 ? 2 : 1;
+  if ((g.dtype_b == MNG_BF16 ? 2 : 1) != es) return -11;
+  const int ld_align = g.out_f32 ? 4 : 8;
+  if (g.epilogue == MNG_EPI_STORE && ((g.ldc % ld_align) || (reinterpret_cast<uintptr_t>(g.out) & 15))) return -12;
+  if (g.epilogue == MNG_EPI_STORE) {
+    if (es == 2) {
+      if (!g.a_mn && !g.b_mn) return launch_store<2, false, false, 1, 1>(g);
+      if (!g.a_mn && g.b_mn) return launch_store<2, false, true, 1, 1>(g);
+      if (g.a_mn && g.b_mn) return launch_store<2, true, true, 1, 1>(g);
+      return -13;
+    }
+    const uint32_t af = g.dtype_a == MNG_E5M2, bf = g.dtype_b == MNG_E5M2;
+    if (!g.a_mn && !g.b_mn && af == 0 && bf == 0) return launch_store<1, false, false, 0, 0>(g);
+    if (!g.a_mn && !g.b_mn && af == 1 && bf == 0) return launch_store<1, false, false, 1, 0>(g);
+    if (!g.a_mn && g.b_mn && af == 0 && bf == 0) return launch_store<1, false, true, 0, 0>(g);
+    if (g.a_mn && g.b_mn && af == 0 && bf == 1) return launch_store<1, true, true, 0, 1>(g);
+    if (g.a_mn && g.b_mn && af == 0 && bf == 0) return launch_store<1, true, true, 0, 0>(g);
+    return -14;
+  }
+  if (g.epilogue == MNG_EPI_RELU2) {
+    if (g.a_mn || g.b_mn || g.batch != 1 || (g.N % 32) || (g.ldc % 16)) return -15;
+    EpiRelu2::Params p{reinterpret_cast<__nv_bfloat16*>(g.out), reinterpret_cast<uint8_t*>(g.out8), g.row_scale, g.col_scale,
+                       g.act_scale, g.amax_bits, g.ldc};
+    if (es == 1) return launch_one<256, 1, false, false, 0, 0, EpiRelu2>(g, p, g.max_ctas);
+    return launch_one<256, 2, false, false, 1, 1, EpiRelu2>(g, p, g.max_ctas);
+  }
+  if (g.epilogue == MNG_EPI_DPRE) {
+    if (g.a_mn || g.b_mn || g.batch != 1 || es != 2 || (g.N % 32) || (g.ldc % 8)) return -16;
+    EpiDpre::Params p{reinterpret_cast<__nv_bfloat16*>(g.out), reinterpret_cast<const __nv_bfloat16*>(g.cin), g.ldc};
+    return launch_one<256, 2, false, false, 1, 1, EpiDpre>(g, p, g.max_ctas);
+  }
+  return -17;
+}

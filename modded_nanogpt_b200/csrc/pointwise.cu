@@ -1,0 +1,268 @@
+// Bandwidth-bound row kernels: RMSNorm forward (with fused row-scaled e4m3 quantisation for the
+// FP8 GEMMs) and backward, row quantisation, tiled transposes.  One warp per row, 16-byte accesses.
+#include "api.h"
+#include "ptx.cuh"
+
+namespace mng {
+
+constexpr int ROW_WARPS = 8;
+
+// cols must be a multiple of 256 (32 lanes x 8 bf16) and <= 256 * MAXV.
+template <int MAXV>
+__global__ void __launch_bounds__(ROW_WARPS * 32)
+rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y, uint8_t* __restrict__ y8,
+                   float* __restrict__ row_scale, float* __restrict__ rstd_out, long long rows, int cols, float eps) {
+  const int lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int nv = cols >> 8;
+  const __nv_bfloat16* xr = x + row * cols;
+  float v[MAXV][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    if (i < nv) {
+      uint4 u = *reinterpret_cast<const uint4*>(xr + (i * 32 + lane) * 8);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        float2 f = __bfloat1622float2(h[t]);
+        v[i][2 * t] = f.x; v[i][2 * t + 1] = f.y;
+        ss += f.x * f.x + f.y * f.y;
+      }
+    }
+  }
+  ss = warp_sum(ss);
+  const float rstd = rsqrtf(ss / cols + eps);
+  if (rstd_out && lane == 0) rstd_out[row] = rstd;
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    if (i < nv) {
+      uint4 w;
+      uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        __nv_bfloat162 b = __floats2bfloat162_rn(v[i][2 * t] * rstd, v[i][2 * t + 1] * rstd);
+        wp[t] = *reinterpret_cast<uint32_t*>(&b);
+        float2 f = __bfloat1622float2(b);          // quantise what the bf16 consumer would see
+        v[i][2 * t] = f.x; v[i][2 * t + 1] = f.y;
+        amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
+      if (y) *reinterpret_cast<uint4*>(y + row * cols + (i * 32 + lane) * 8) = w;
+    }
+  }
+  if (y8) {
+    amax = fmaxf(warp_max(amax), 1e-12f);
+    const float s = amax / 448.f, inv = 448.f / amax;
+    if (lane == 0) row_scale[row] = s;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      if (i < nv) {
+        uint2 w;
+        w.x = pack_e4m3x2(v[i][0] * inv, v[i][1] * inv) | ((uint32_t)pack_e4m3x2(v[i][2] * inv, v[i][3] * inv) << 16);
+        w.y = pack_e4m3x2(v[i][4] * inv, v[i][5] * inv) | ((uint32_t)pack_e4m3x2(v[i][6] * inv, v[i][7] * inv) << 16);
+        *reinterpret_cast<uint2*>(y8 + row * cols + (i * 32 + lane) * 8) = w;
+      }
+    }
+  }
+}
+
+// dx = rstd * (dy - xhat * mean(dy * xhat)),  xhat = x * rstd.   accumulate: dx += ...
+template <int MAXV>
+__global__ void __launch_bounds__(ROW_WARPS * 32)
+rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ dy, const float* __restrict__ rstd_in,
+                   __nv_bfloat16* __restrict__ dx, long long rows, int cols, int accumulate, float eps) {
+  const int lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int nv = cols >> 8;
+  float xv[MAXV][8], gv[MAXV][8];
+  float ss = 0.f, dot = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    if (i < nv) {
+      uint4 u = *reinterpret_cast<const uint4*>(x + row * cols + (i * 32 + lane) * 8);
+      uint4 g = *reinterpret_cast<const uint4*>(dy + row * cols + (i * 32 + lane) * 8);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+      const __nv_bfloat162* k = reinterpret_cast<const __nv_bfloat162*>(&g);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        float2 a = __bfloat1622float2(h[t]), b = __bfloat1622float2(k[t]);
+        xv[i][2 * t] = a.x; xv[i][2 * t + 1] = a.y; gv[i][2 * t] = b.x; gv[i][2 * t + 1] = b.y;
+        ss += a.x * a.x + a.y * a.y;
+        dot += a.x * b.x + a.y * b.y;
+      }
+    }
+  }
+  ss = warp_sum(ss);
+  dot = warp_sum(dot);
+  const float rstd = rstd_in ? rstd_in[row] : rsqrtf(ss / cols + eps);
+  const float c = dot * rstd * rstd * rstd / cols;       // mean(dy*xhat) * rstd, with xhat = x*rstd
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    if (i < nv) {
+      __nv_bfloat16* o = dx + row * cols + (i * 32 + lane) * 8;
+      float r[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) r[t] = gv[i][t] * rstd - xv[i][t] * c;
+      if (accumulate) {
+        uint4 old = *reinterpret_cast<const uint4*>(o);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&old);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          float2 f = __bfloat1622float2(h[t]);
+          r[2 * t] += f.x; r[2 * t + 1] += f.y;
+        }
+      }
+      uint4 w;
+      w.x = pack_bf16x2(r[0], r[1]); w.y = pack_bf16x2(r[2], r[3]); w.z = pack_bf16x2(r[4], r[5]); w.w = pack_bf16x2(r[6], r[7]);
+      *reinterpret_cast<uint4*>(o) = w;
+    }
+  }
+}
+
+template <int MAXV>
+__global__ void __launch_bounds__(ROW_WARPS * 32)
+quant_rows_kernel(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ q, float* __restrict__ scale, long long rows, int cols) {
+  const int lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int nv = cols >> 8;
+  float v[MAXV][8];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    if (i < nv) {
+      uint4 u = *reinterpret_cast<const uint4*>(x + row * cols + (i * 32 + lane) * 8);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        float2 f = __bfloat1622float2(h[t]);
+        v[i][2 * t] = f.x; v[i][2 * t + 1] = f.y;
+        amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
+    }
+  }
+  amax = fmaxf(warp_max(amax), 1e-12f);
+  const float inv = 448.f / amax;
+  if (lane == 0) scale[row] = amax / 448.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    if (i < nv) {
+      uint2 w;
+      w.x = pack_e4m3x2(v[i][0] * inv, v[i][1] * inv) | ((uint32_t)pack_e4m3x2(v[i][2] * inv, v[i][3] * inv) << 16);
+      w.y = pack_e4m3x2(v[i][4] * inv, v[i][5] * inv) | ((uint32_t)pack_e4m3x2(v[i][6] * inv, v[i][7] * inv) << 16);
+      *reinterpret_cast<uint2*>(q + row * cols + (i * 32 + lane) * 8) = w;
+    }
+  }
+}
+
+// 64x64 bf16 tile transpose through padded shared memory; coalesced on both sides.
+__global__ void __launch_bounds__(256)
+transpose_bf16_kernel(const __nv_bfloat16* __restrict__ src, __nv_bfloat16* __restrict__ dst, long long rows, long long cols,
+                      int accumulate) {
+  __shared__ __nv_bfloat16 tile[64][66];
+  const long long r0 = (long long)blockIdx.y * 64, c0 = (long long)blockIdx.x * 64;
+  const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;
+  for (int i = ty; i < 64; i += 4) {
+    const long long r = r0 + i, c = c0 + tx;
+    tile[i][tx] = (r < rows && c < cols) ? src[r * cols + c] : __float2bfloat16(0.f);
+  }
+  __syncthreads();
+  for (int i = ty; i < 64; i += 4) {
+    const long long c = c0 + i, r = r0 + tx;
+    if (c < cols && r < rows) {
+      __nv_bfloat16 v = tile[tx][i];
+      if (accumulate) v = __float2bfloat16(__bfloat162float(v) + __bfloat162float(dst[c * rows + r]));
+      dst[c * rows + r] = v;
+    }
+  }
+}
+
+// Column amax of a [rows, cols] bf16 matrix (atomic max on float bits), then quantise the transpose.
+__global__ void __launch_bounds__(256)
+col_amax_kernel(const __nv_bfloat16* __restrict__ src, unsigned int* __restrict__ amax_bits, long long rows, long long cols) {
+  const long long c = (long long)blockIdx.x * 64 + (threadIdx.x & 63);
+  const int ty = threadIdx.x >> 6;
+  const long long r_begin = (long long)blockIdx.y * 256;
+  float m = 0.f;
+  if (c < cols)
+    for (long long r = r_begin + ty; r < rows && r < r_begin + 256; r += 4) m = fmaxf(m, fabsf(__bfloat162float(src[r * cols + c])));
+  if (c < cols && m > 0.f) atomicMax(amax_bits + c, __float_as_uint(m));
+}
+
+__global__ void __launch_bounds__(256)
+quant_transpose_kernel(const __nv_bfloat16* __restrict__ src, uint8_t* __restrict__ q, const unsigned int* __restrict__ amax_bits,
+                       float* __restrict__ scale, long long rows, long long cols) {
+  __shared__ float tile[64][65];
+  const long long r0 = (long long)blockIdx.y * 64, c0 = (long long)blockIdx.x * 64;
+  const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;
+  for (int i = ty; i < 64; i += 4) {
+    const long long r = r0 + i, c = c0 + tx;
+    tile[i][tx] = (r < rows && c < cols) ? __bfloat162float(src[r * cols + c]) : 0.f;
+  }
+  __syncthreads();
+  for (int i = ty; i < 64; i += 4) {
+    const long long c = c0 + i, r = r0 + tx;
+    if (c < cols && r < rows) {
+      const float amax = fmaxf(__uint_as_float(amax_bits[c]), 1e-12f);
+      if (blockIdx.y == 0 && tx == 0) scale[c] = amax / 448.f;
+      q[c * rows + r] = (uint8_t)(pack_e4m3x2(tile[tx][i] * (448.f / amax), 0.f) & 0xff);
+    }
+  }
+}
+
+}  // namespace mng
+
+using namespace mng;
+
+#define DISPATCH_COLS(KERNEL, ...)                                                            \
+  do {                                                                                        \
+    if (cols % 256 != 0 || cols > 4096) return -1;                                            \
+    const unsigned grid = (unsigned)((rows + ROW_WARPS - 1) / ROW_WARPS);                     \
+    if (cols <= 256) KERNEL<1><<<grid, ROW_WARPS * 32, 0, (cudaStream_t)stream>>>(__VA_ARGS__);        \
+    else if (cols <= 768) KERNEL<3><<<grid, ROW_WARPS * 32, 0, (cudaStream_t)stream>>>(__VA_ARGS__);   \
+    else if (cols <= 1024) KERNEL<4><<<grid, ROW_WARPS * 32, 0, (cudaStream_t)stream>>>(__VA_ARGS__);  \
+    else if (cols <= 3072) KERNEL<12><<<grid, ROW_WARPS * 32, 0, (cudaStream_t)stream>>>(__VA_ARGS__); \
+    else KERNEL<16><<<grid, ROW_WARPS * 32, 0, (cudaStream_t)stream>>>(__VA_ARGS__);                   \
+    return cudaGetLastError() == cudaSuccess ? 0 : -2;                                        \
+  } while (0)
+
+static const float kRmsEps = 0.0078125f;   // torch.finfo(bfloat16).eps: what F.rms_norm(eps=None) uses on bf16 input
+
+extern "C" int mng_rmsnorm_fwd(const void* x, void* y, void* y8, float* row_scale, float* rstd, long long rows, int cols,
+                               void* stream) {
+  if (rows == 0) return 0;
+  DISPATCH_COLS(rmsnorm_fwd_kernel, (const __nv_bfloat16*)x, (__nv_bfloat16*)y, (uint8_t*)y8, row_scale, rstd, rows, cols, kRmsEps);
+}
+
+extern "C" int mng_rmsnorm_bwd(const void* x, const void* dy, const float* rstd, void* dx, long long rows, int cols,
+                               int accumulate, void* stream) {
+  if (rows == 0) return 0;
+  DISPATCH_COLS(rmsnorm_bwd_kernel, (const __nv_bfloat16*)x, (const __nv_bfloat16*)dy, rstd, (__nv_bfloat16*)dx, rows, cols,
+                accumulate, kRmsEps);
+}
+
+extern "C" int mng_quant_rows_e4m3(const void* x, void* q, float* scale, long long rows, int cols, void* stream) {
+  if (rows == 0) return 0;
+  DISPATCH_COLS(quant_rows_kernel, (const __nv_bfloat16*)x, (uint8_t*)q, scale, rows, cols);
+}
+
+extern "C" int mng_transpose_bf16(const void* src, void* dst, long long rows, long long cols, int accumulate, void* stream) {
+  dim3 grid((unsigned)((cols + 63) / 64), (unsigned)((rows + 63) / 64));
+  transpose_bf16_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>((const __nv_bfloat16*)src, (__nv_bfloat16*)dst, rows, cols, accumulate);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+// `amax_scratch` holds `cols` 32-bit words of caller-provided scratch (zeroed here).
+extern "C" int mng_quant_transpose_e4m3(const void* src, void* q, float* scale, unsigned int* amax_scratch, long long rows,
+                                        long long cols, void* stream) {
+  cudaStream_t s = (cudaStream_t)stream;
+  if (cudaMemsetAsync(amax_scratch, 0, sizeof(unsigned int) * cols, s) != cudaSuccess) return -3;
+  dim3 g1((unsigned)((cols + 63) / 64), (unsigned)((rows + 255) / 256));
+  col_amax_kernel<<<g1, 256, 0, s>>>((const __nv_bfloat16*)src, amax_scratch, rows, cols);
+  dim3 g2((unsigned)((cols + 63) / 64), (unsigned)((rows + 63) / 64));
+  quant_transpose_kernel<<<g2, 256, 0, s>>>((const __nv_bfloat16*)src, (uint8_t*)q, amax_scratch, scale, rows, cols);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}

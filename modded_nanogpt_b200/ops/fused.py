@@ -1,0 +1,245 @@
+"""Python face of the sm_100a kernels: tensor plumbing and autograd Functions.
+
+Forward/backward pairs here mirror the reference's fused ops:
+* `relu2_mlp`  <-> `FusedLinearReLUSquareFunction` (`triton_kernels.py:667-729`): FP8 forward with a
+  fused ReLU^2 epilogue, bf16 backward without ever storing the pre-activation;
+* `softcap_ce` <-> `FusedSoftcappedCrossEntropy` (`triton_kernels.py:1208-1292`): FP8 lm_head GEMM,
+  one-pass loss + gradient kernel, FP8 backward GEMMs - here without any transpose copies, because
+  the tcgen05 descriptors read MN-major operands in place;
+* `rms_norm` with an optional fused row-scaled e4m3 copy (removes the global amax pass of
+  `train_gpt.py:1645-1646`).
+"""
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from . import native
+
+EPI_STORE, EPI_RELU2, EPI_DPRE = 0, 1, 2
+NUM_SMS = 148
+
+
+def _C():
+    return native.lib()
+
+
+def check_status(like: Tensor | None = None) -> int:
+    """Reads the device status word (0 = no kernel reported a timed-out wait); synchronises."""
+    like = like if like is not None else torch.empty(1, device="cuda")
+    code = int(_C().status_tensor(like).item())
+    if code:
+        raise RuntimeError(f"a kernel reported error status {code} (bounded wait expired or bad argument)")
+    return code
+
+
+# --------------------------------------------------------------------------------------------------
+# GEMM
+
+
+def gemm(a: Tensor, b: Tensor, *, a_mn: bool = False, b_mn: bool = False, out: Tensor | None = None,
+         out_dtype=torch.bfloat16, bn: int | None = None, alpha: float = 1.0, beta: float = 0.0, cin: Tensor | None = None,
+         alpha_t: Tensor | None = None, row_scale: Tensor | None = None, col_scale: Tensor | None = None,
+         epilogue: int = EPI_STORE, out8: Tensor | None = None, act_scale: Tensor | None = None,
+         amax_bits: Tensor | None = None, max_ctas: int = 0) -> Tensor:
+    """out = epilogue(A @ B^T) on the tcgen05 kernel.  A is [.., M, K] (or [.., K, M] with a_mn),
+    B is [.., N, K] (or [.., K, N] with b_mn); fp32 accumulation."""
+    M = a.shape[-1] if a_mn else a.shape[-2]
+    N = b.shape[-1] if b_mn else b.shape[-2]
+    if out is None:
+        out = torch.empty((*a.shape[:-2], M, N), dtype=out_dtype, device=a.device)
+    if bn is None:
+        batch = a.shape[0] if a.dim() == 3 else 1
+        tiles256 = -(-M // 128) * -(-N // 256) * batch
+        bn = 256 if (tiles256 >= NUM_SMS or N > 4096) and epilogue == EPI_STORE else 128
+        if epilogue != EPI_STORE:
+            bn = 256
+    _C().gemm(a, b, out, a_mn, b_mn, epilogue, bn, alpha, beta, cin, alpha_t, row_scale, col_scale, out8, act_scale,
+              amax_bits, max_ctas)
+    return out
+
+
+# --------------------------------------------------------------------------------------------------
+# RMSNorm
+
+
+class _RmsNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x):
+        xc = x.contiguous()
+        y, _, _, rstd = _C().rmsnorm_fwd(xc, True, False, True)
+        ctx.save_for_backward(xc, rstd)
+        return y.view(x.shape)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, rstd = ctx.saved_tensors
+        return _C().rmsnorm_bwd(x, dy.contiguous().view(x.shape), rstd, None)
+
+
+def rms_norm(x: Tensor) -> Tensor:
+    if x.shape[-1] % 256 != 0 or x.shape[-1] > 4096:
+        from . import reference
+        return reference.rms_norm(x)
+    return _RmsNorm.apply(x)
+
+
+# --------------------------------------------------------------------------------------------------
+# ReLU^2 MLP
+
+
+class MlpFp8State:
+    """e4m3 copies of the MLP bank with one scale per weight row, plus the delayed activation
+    scale of every layer's hidden activations (amax of the previous step x 1.8 / 448)."""
+
+    def __init__(self, bank: Tensor):
+        Lp, _, hid, dim = bank.shape
+        dev = bank.device
+        self.fc8 = torch.empty(Lp, hid, dim, dtype=torch.float8_e4m3fn, device=dev)
+        self.fc_scale = torch.empty(Lp, hid, dtype=torch.float32, device=dev)
+        self.projT8 = torch.empty(Lp, dim, hid, dtype=torch.float8_e4m3fn, device=dev)
+        self.projT_scale = torch.empty(Lp, dim, dtype=torch.float32, device=dev)
+        self.act_scale = torch.ones(Lp, dtype=torch.float32, device=dev)
+        self.amax_bits = torch.zeros(Lp, dtype=torch.int32, device=dev)
+        self._scratch = torch.empty(max(hid, dim), dtype=torch.int32, device=dev)
+
+    def layer(self, i: int):
+        return (self.fc8[i], self.fc_scale[i], self.projT8[i], self.projT_scale[i], self.act_scale[i:i + 1],
+                self.amax_bits[i:i + 1])
+
+
+@torch.no_grad()
+def quantize_mlp_weights(bank: Tensor, state: MlpFp8State | None, used_scales: Tensor, next_scales: Tensor,
+                         bootstrap: bool) -> MlpFp8State:
+    C = _C()
+    if state is None:
+        state = MlpFp8State(bank)
+    Lp, _, hid, dim = bank.shape
+    for l in range(Lp):
+        q, s = C.quant_rows(bank[l, 0])
+        state.fc8[l].copy_(q)
+        state.fc_scale[l].copy_(s)
+        C.quant_transpose(bank[l, 1], state.projT8[l], state.projT_scale[l], state._scratch)
+    # delayed activation scales: amax seen since the last refresh, with headroom (`train_gpt.py:1670-1675`)
+    amax = state.amax_bits.view(torch.float32)
+    seen = amax > 0
+    new = amax.clamp_min(1e-12) * (1.80 / 448.0)
+    state.act_scale.copy_(torch.where(seen, new, state.act_scale))
+    state.amax_bits.zero_()
+    # per-layer maxima of the down-projection scales keep the reference's state_dict buffers meaningful
+    used_scales.copy_(next_scales)
+    next_scales.copy_(state.projT_scale.amax(dim=1) * 1.12)
+    if bootstrap:
+        used_scales.copy_(state.projT_scale.amax(dim=1))
+    return state
+
+
+class _NormRelu2Mlp(torch.autograd.Function):
+    """out = relu(norm(x) @ W1^T)^2 @ W2 with W1, W2 stored (hidden, dim)."""
+
+    @staticmethod
+    def forward(ctx, x, w_fc, w_proj, fp8):
+        C = _C()
+        T, D = x.shape
+        hid = w_fc.shape[0]
+        xc = x.contiguous()
+        post = torch.empty(T, hid, dtype=torch.bfloat16, device=x.device)
+        if fp8 is not None:
+            fc8, fc_scale, projT8, projT_scale, act_scale, amax_bits = fp8
+            y, y8, y_scale, rstd = C.rmsnorm_fwd(xc, True, True, True)
+            post8 = torch.empty(T, hid, dtype=torch.float8_e4m3fn, device=x.device)
+            gemm(y8, fc8, out=post, epilogue=EPI_RELU2, row_scale=y_scale, col_scale=fc_scale, out8=post8,
+                 act_scale=act_scale, amax_bits=amax_bits)
+            out = gemm(post8, projT8, col_scale=projT_scale, alpha_t=act_scale)
+        else:
+            y, _, _, rstd = C.rmsnorm_fwd(xc, True, False, True)
+            gemm(y, w_fc, out=post, epilogue=EPI_RELU2)
+            out = gemm(post, w_proj, b_mn=True)
+        ctx.save_for_backward(xc, rstd, y, post, w_fc, w_proj)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        C = _C()
+        x, rstd, y, post, w_fc, w_proj = ctx.saved_tensors
+        g = g.contiguous()
+        d_proj = gemm(post, g, a_mn=True, b_mn=True)                         # post^T g         (hid, dim)
+        dpre = gemm(g, w_proj, epilogue=EPI_DPRE, cin=post)                  # 2 (g W2^T) sqrt(post)
+        d_fc = gemm(dpre, y, a_mn=True, b_mn=True)                           # dpre^T y         (hid, dim)
+        dy = gemm(dpre, w_fc, b_mn=True)                                     # dpre W1          (T, dim)
+        dx = C.rmsnorm_bwd(x, dy, rstd, None)
+        return dx, d_fc, d_proj, None
+
+
+def norm_relu2_mlp(x: Tensor, w_fc: Tensor, w_proj: Tensor, fp8_state=None) -> Tensor:
+    return _NormRelu2Mlp.apply(x, w_fc, w_proj, fp8_state)
+
+
+def relu2_mlp(x_normed: Tensor, w_fc: Tensor, w_proj: Tensor, fp8_state=None) -> Tensor:
+    """MLP on an already normalised input (used when the caller needs the normed tensor too)."""
+    post = gemm(x_normed.contiguous(), w_fc, epilogue=EPI_RELU2,
+                out=torch.empty(x_normed.shape[0], w_fc.shape[0], dtype=torch.bfloat16, device=x_normed.device))
+    return gemm(post, w_proj, b_mn=True)
+
+
+# --------------------------------------------------------------------------------------------------
+# lm_head + softcapped cross entropy
+
+
+def quant_static_e4m3(x: Tensor, scale: float) -> Tensor:
+    """Saturating e4m3 cast of x/scale (per-tensor static scale)."""
+    return (x.float() * (1.0 / scale)).clamp_(-448.0, 448.0).to(torch.float8_e4m3fn)
+
+
+class _SoftcapCE(torch.autograd.Function):
+    """x [T,D] bf16 (normed), w [D,V] bf16.  FP8 path: static per-tensor scales x_s, w_s and a
+    gradient scale grad_s, as in the reference (`train_gpt.py:1225`)."""
+
+    @staticmethod
+    def forward(ctx, x, w, targets, mtp_weights, prefix_targets, prefix_weight, a, b, c, grad_scale, fp8, scales):
+        C = _C()
+        x_s, w_s, grad_s = scales
+        if fp8:
+            x8 = quant_static_e4m3(x, x_s)
+            w8 = quant_static_e4m3(w, w_s)
+            logits = gemm(x8, w8, b_mn=True, alpha=x_s * w_s)
+            g_s = grad_s * grad_scale
+            losses, dl = C.softcap_ce(logits, targets, mtp_weights, prefix_targets, prefix_weight, True, a, b, c,
+                                      grad_scale / g_s)
+            ctx.save_for_backward(x8, w8, dl)
+            ctx.cfg = (True, x_s, w_s, g_s)
+        else:
+            logits = gemm(x.contiguous(), w, b_mn=True)
+            losses, dl = C.softcap_ce(logits, targets, mtp_weights, prefix_targets, prefix_weight, False, a, b, c, grad_scale)
+            ctx.save_for_backward(x, w, dl)
+            ctx.cfg = (False, 1.0, 1.0, 1.0)
+        return losses
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        xq, wq, dl = ctx.saved_tensors
+        fp8, x_s, w_s, g_s = ctx.cfg
+        # dl already carries grad_scale: the caller reduces the losses with .sum() * grad_scale
+        dx = gemm(dl, wq, alpha=g_s * w_s)                                           # dl W^T          (T, D)
+        dw = gemm(xq, dl, a_mn=True, b_mn=True, alpha=x_s * g_s, out_dtype=torch.float32)   # x^T dl   (D, V)
+        return dx, dw.to(torch.bfloat16), None, None, None, None, None, None, None, None, None, None
+
+
+def softcap_ce(x, w, targets, mtp_weights, prefix_targets, prefix_weight, a, b, c, grad_scale=1.0, fp8=True,
+               scales=(100 / 448, 1.6 / 448, 0.75 / 448)) -> Tensor:
+    if prefix_weight is not None:
+        prefix_weight = prefix_weight.reshape(1).float()
+    return _SoftcapCE.apply(x.contiguous(), w, targets.contiguous(), mtp_weights.float().contiguous(), prefix_targets,
+                            prefix_weight, a, b, c, grad_scale, fp8, scales)
+
+
+# --------------------------------------------------------------------------------------------------
+# attention / DC: tcgen05 kernels are selected here once available for the shape
+
+
+def attention_supported(q: Tensor, window: int) -> bool:
+    return False
+
+
+def dc_supported(q: Tensor, window: int) -> bool:
+    return False
