@@ -90,6 +90,48 @@ int mng_scale_by_norm(void* x_bf16, const float* sumsq, long long mats, long lon
 int mng_normuon_apply(const PeerPtrs* params, long long off, void* mantissa_u16, const void* v_bf16, float* second_mom,
                       float* scale_scratch, long long mats, int rows, int cols, int red_rows, float beta2, float eff_wd,
                       const float* eff_lr_per_mat, void* stream);
+// ---- fused glue (glue.cu) -----------------------------------------------------------------------------
+#define LC_MAX_TERMS 6
+typedef struct {
+  const void* x;            // [rows, cols] bf16
+  const float* scalar;      // device scalar s (null = 1)
+  const void* gate;         // per-row coefficient source g (null = 1): element [row*gate_stride + gate_col]
+  long long gate_stride;
+  int gate_col;
+  int gate_bf16;            // gate dtype: 1 = bf16, 0 = fp32
+  float addc;               // coefficient = addc + s * g(row)
+} LinTerm;
+typedef struct { LinTerm t[LC_MAX_TERMS]; int k; } LinCombArgs;
+typedef struct {
+  void* dx;                 // [rows, cols] bf16 or null
+  void* dgate;              // bf16 buffer (zero-initialised by the caller) or null; written at [row*stride + col]
+  long long dgate_stride;
+  int dgate_col;
+  float* dscalar;           // fp32 accumulator (zeroed by the caller) or null
+} LinGrad;
+typedef struct { LinGrad t[LC_MAX_TERMS]; } LinCombGrads;
+int mng_lincomb_fwd(const LinCombArgs* a, void* out, long long rows, int cols, void* stream);
+int mng_lincomb_bwd(const LinCombArgs* a, const LinCombGrads* g, const void* gout, long long rows, int cols, void* stream);
+
+int mng_qkv_post_fwd(const void* qkv, const float* cos_t, const float* sin_t, const void* ve, const void* vgate,
+                     int vgate_stride, const void* vadd, void* q, void* k, void* v, float* rstd_q, float* rstd_k,
+                     long long T, int H, int paired, int key_offset, void* stream);
+int mng_qkv_post_bwd(const void* qkv, const float* cos_t, const float* sin_t, const float* rstd_q, const float* rstd_k,
+                     const void* dq, const void* dk, const void* dv, const void* ve, const void* vgate, int vgate_stride,
+                     void* d_qkv, void* d_ve, void* d_vgate, int d_vgate_stride, long long T, int H, int paired,
+                     int key_offset, void* stream);
+int mng_xsa_gate_fwd(const void* y, const void* v, const void* alpha, int alpha_stride, const void* gate, int gate_stride,
+                     void* out, long long T, int H, void* stream);
+int mng_xsa_gate_bwd(const void* y, const void* v, const void* alpha, int alpha_stride, const void* gate, int gate_stride,
+                     const void* dout, void* dy, void* dv, void* dalpha, int dalpha_stride, void* dgate, int dgate_stride,
+                     long long T, int H, void* stream);
+
+// ---- DC cross-head mixing (dc.cu) ---------------------------------------------------------------------
+int mng_dc_mix_fwd(const float* S, const void* w1, const int* doc_start, void* P, void* a, long long T, int H, int window,
+                   void* stream);
+int mng_dc_mix_bwd(const float* dM, const void* P, const void* a, const void* w1, const void* w2, void* dS, float* g_w1,
+                   float* g_w2, long long T, int H, float scale, void* stream);
+
 // Barrier across ranks on signal pads (bounded wait; sets *status on expiry).
 int mng_peer_barrier(const PeerPtrs* pads, int rank, uint32_t epoch, uint32_t* status, void* stream);
 

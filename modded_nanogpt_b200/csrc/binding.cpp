@@ -12,6 +12,8 @@ namespace {
 using torch::Tensor;
 
 Tensor g_status;   // one int32 word per device, lazily created
+int64_t g_launches = 0;   // kernels launched by this extension since import
+int64_t launch_count() { return g_launches; }
 
 uint32_t* status_ptr(const Tensor& like) {
   if (!g_status.defined() || g_status.device() != like.device())
@@ -94,6 +96,7 @@ void gemm(const Tensor& a, const Tensor& b, Tensor& out, bool a_mn, bool b_mn, i
   g.stream = cur_stream();
   g.status = status_ptr(a);
   check(mng_gemm(&g), "mng_gemm");
+  g_launches += 1;
 }
 
 std::vector<Tensor> rmsnorm_fwd(const Tensor& x, bool want_y, bool want_fp8, bool want_rstd) {
@@ -112,6 +115,7 @@ std::vector<Tensor> rmsnorm_fwd(const Tensor& x, bool want_y, bool want_fp8, boo
                         want_fp8 ? scale.data_ptr<float>() : nullptr, want_rstd ? rstd.data_ptr<float>() : nullptr, rows, cols,
                         cur_stream()),
         "mng_rmsnorm_fwd");
+  g_launches += 1;
   return {y, y8, scale, rstd};
 }
 
@@ -125,6 +129,7 @@ Tensor rmsnorm_bwd(const Tensor& x, const Tensor& dy, const c10::optional<Tensor
   check(mng_rmsnorm_bwd(x.data_ptr(), dy.data_ptr(), fptr(rstd), dx.data_ptr(), rows, cols,
                         (accum_into.has_value() && accum_into->defined()) ? 1 : 0, cur_stream()),
         "mng_rmsnorm_bwd");
+  g_launches += 1;
   return dx;
 }
 
@@ -136,6 +141,7 @@ std::vector<Tensor> quant_rows(const Tensor& x) {
   Tensor q = torch::empty(x.sizes(), x.options().dtype(torch::kFloat8_e4m3fn));
   Tensor s = torch::empty({rows}, x.options().dtype(torch::kFloat32));
   check(mng_quant_rows_e4m3(x.data_ptr(), q.data_ptr(), s.data_ptr<float>(), rows, cols, cur_stream()), "mng_quant_rows_e4m3");
+  g_launches += 1;
   return {q, s};
 }
 
@@ -145,6 +151,7 @@ void transpose(const Tensor& src, Tensor& dst, bool accumulate) {
   TORCH_CHECK(dst.size(0) == src.size(1) && dst.size(1) == src.size(0));
   c10::cuda::CUDAGuard guard(src.device());
   check(mng_transpose_bf16(src.data_ptr(), dst.data_ptr(), src.size(0), src.size(1), accumulate, cur_stream()), "mng_transpose_bf16");
+  g_launches += 1;
 }
 
 // q [cols, rows] e4m3 and scale [cols] of the transpose of src [rows, cols]; `scratch` is cols int32 words.
@@ -155,6 +162,7 @@ void quant_transpose(const Tensor& src, Tensor& q, Tensor& scale, Tensor& scratc
   check(mng_quant_transpose_e4m3(src.data_ptr(), q.data_ptr(), scale.data_ptr<float>(),
                                  reinterpret_cast<unsigned int*>(scratch.data_ptr()), src.size(0), src.size(1), cur_stream()),
         "mng_quant_transpose_e4m3");
+  g_launches += 2;
 }
 
 std::vector<Tensor> softcap_ce(const Tensor& logits, const Tensor& targets, const Tensor& mtp_weights,
@@ -178,6 +186,7 @@ std::vector<Tensor> softcap_ce(const Tensor& logits, const Tensor& targets, cons
                        losses.data_ptr<float>(), dl.data_ptr(), dlogits_e5m2, rows, vocab, vocab, (float)A, (float)B, (float)C,
                        (float)grad_mul, cur_stream()),
         "mng_softcap_ce");
+  g_launches += 1;
   return {losses, dl};
 }
 
@@ -208,6 +217,7 @@ void adam(const std::vector<int64_t>& grad_ptrs, const std::vector<int64_t>& par
   d.step_size = (float)step_size; d.eff_wd = (float)eff_wd; d.grad_mul = (float)grad_mul;
   TORCH_CHECK(exp_avg.numel() >= n && exp_avg_sq.numel() >= n);
   check(mng_adam(&d, cur_stream()), "mng_adam");
+  g_launches += 1;
 }
 
 void nesterov(const std::vector<int64_t>& grad_ptrs, int64_t self, int64_t off, Tensor& buf, Tensor& out, Tensor& sumsq,
@@ -219,12 +229,14 @@ void nesterov(const std::vector<int64_t>& grad_ptrs, int64_t self, int64_t off, 
   check(mng_nesterov(&g, off, buf.data_ptr<float>(), out.data_ptr(), sumsq.data_ptr<float>(), buf.size(0),
                      buf.size(1) * buf.size(2), (float)momentum, (float)grad_mul, cur_stream()),
         "mng_nesterov");
+  g_launches += 1;
 }
 
 void scale_by_norm(Tensor& x, const Tensor& sumsq) {
   TORCH_CHECK(x.dim() == 3 && x.is_contiguous() && x.scalar_type() == torch::kBFloat16 && sumsq.numel() == x.size(0));
   c10::cuda::CUDAGuard guard(x.device());
   check(mng_scale_by_norm(x.data_ptr(), sumsq.data_ptr<float>(), x.size(0), x.size(1) * x.size(2), cur_stream()), "mng_scale_by_norm");
+  g_launches += 1;
 }
 
 void normuon_apply(const std::vector<int64_t>& param_ptrs, int64_t self, int64_t off, Tensor& mantissa, const Tensor& v,
@@ -239,12 +251,201 @@ void normuon_apply(const std::vector<int64_t>& param_ptrs, int64_t self, int64_t
                           v.size(0), rows, cols, red_rows, (float)beta2, (float)eff_wd, eff_lr_per_mat.data_ptr<float>(),
                           cur_stream()),
         "mng_normuon_apply");
+  g_launches += 2;
 }
 
 void peer_barrier(const std::vector<int64_t>& pad_ptrs, int64_t rank, int64_t epoch, const Tensor& like) {
   c10::cuda::CUDAGuard guard(like.device());
   PeerPtrs p = peers_from(pad_ptrs, rank);
   check(mng_peer_barrier(&p, (int)rank, (uint32_t)epoch, status_ptr(like), cur_stream()), "mng_peer_barrier");
+  g_launches += 1;
+}
+
+using OptT = c10::optional<Tensor>;
+
+LinCombArgs make_lincomb(const std::vector<Tensor>& xs, const std::vector<OptT>& scalars, const std::vector<OptT>& gates,
+                         const std::vector<int64_t>& cols, const std::vector<double>& addc) {
+  const size_t k = xs.size();
+  TORCH_CHECK(k >= 1 && k <= LC_MAX_TERMS && scalars.size() == k && gates.size() == k && cols.size() == k && addc.size() == k);
+  LinCombArgs a{};
+  a.k = (int)k;
+  for (size_t j = 0; j < k; ++j) {
+    TORCH_CHECK(xs[j].is_contiguous() && xs[j].scalar_type() == torch::kBFloat16 && xs[j].sizes() == xs[0].sizes());
+    a.t[j].x = xs[j].data_ptr();
+    if (scalars[j].has_value() && scalars[j]->defined()) {
+      TORCH_CHECK(scalars[j]->scalar_type() == torch::kFloat32 && scalars[j]->numel() == 1);
+      a.t[j].scalar = scalars[j]->data_ptr<float>();
+    }
+    if (gates[j].has_value() && gates[j]->defined()) {
+      const Tensor& g = *gates[j];
+      TORCH_CHECK(g.dim() == 2 && g.stride(1) == 1 && g.size(0) == xs[0].size(0) && cols[j] < g.size(1));
+      TORCH_CHECK(g.scalar_type() == torch::kBFloat16 || g.scalar_type() == torch::kFloat32);
+      a.t[j].gate = g.data_ptr();
+      a.t[j].gate_stride = g.stride(0);
+      a.t[j].gate_col = (int)cols[j];
+      a.t[j].gate_bf16 = g.scalar_type() == torch::kBFloat16;
+    }
+    a.t[j].addc = (float)addc[j];
+  }
+  return a;
+}
+
+Tensor lincomb_fwd(const std::vector<Tensor>& xs, const std::vector<OptT>& scalars, const std::vector<OptT>& gates,
+                   const std::vector<int64_t>& cols, const std::vector<double>& addc) {
+  c10::cuda::CUDAGuard guard(xs[0].device());
+  LinCombArgs a = make_lincomb(xs, scalars, gates, cols, addc);
+  Tensor out = torch::empty_like(xs[0]);
+  const int ncols = (int)xs[0].size(-1);
+  check(mng_lincomb_fwd(&a, out.data_ptr(), xs[0].numel() / ncols, ncols, cur_stream()), "mng_lincomb_fwd");
+  g_launches += 1;
+  return out;
+}
+
+// need_dx[j]: allocate and return dx_j.  dgates[j]: bf16 [rows, C] buffer (zeroed by the caller; may be shared between
+// terms) written at column cols[j].  dscalars[j]: fp32 one-element accumulator (zeroed by the caller).
+std::vector<Tensor> lincomb_bwd(const std::vector<Tensor>& xs, const std::vector<OptT>& scalars, const std::vector<OptT>& gates,
+                                const std::vector<int64_t>& cols, const std::vector<double>& addc, const Tensor& gout,
+                                const std::vector<bool>& need_dx, const std::vector<OptT>& dgates, const std::vector<OptT>& dscalars) {
+  c10::cuda::CUDAGuard guard(xs[0].device());
+  LinCombArgs a = make_lincomb(xs, scalars, gates, cols, addc);
+  TORCH_CHECK(gout.is_contiguous() && gout.scalar_type() == torch::kBFloat16 && gout.numel() == xs[0].numel());
+  LinCombGrads g{};
+  std::vector<Tensor> dxs;
+  for (int j = 0; j < a.k; ++j) {
+    Tensor dx;
+    if (need_dx[j]) {
+      dx = torch::empty_like(xs[j]);
+      g.t[j].dx = dx.data_ptr();
+    }
+    dxs.push_back(dx);
+    if (dgates[j].has_value() && dgates[j]->defined()) {
+      TORCH_CHECK(dgates[j]->scalar_type() == torch::kBFloat16 && dgates[j]->stride(1) == 1);
+      g.t[j].dgate = dgates[j]->data_ptr();
+      g.t[j].dgate_stride = dgates[j]->stride(0);
+      g.t[j].dgate_col = (int)cols[j];
+    }
+    if (dscalars[j].has_value() && dscalars[j]->defined()) g.t[j].dscalar = dscalars[j]->data_ptr<float>();
+  }
+  const int ncols = (int)xs[0].size(-1);
+  check(mng_lincomb_bwd(&a, &g, gout.data_ptr(), xs[0].numel() / ncols, ncols, cur_stream()), "mng_lincomb_bwd");
+  g_launches += 1;
+  return dxs;
+}
+
+const void* optr(const OptT& t) { return (t.has_value() && t->defined()) ? t->data_ptr() : nullptr; }
+
+// qkv [T, 3*H*128] bf16 -> q, k, v [T, H, 128] (+ rstd_q, rstd_k [T*H]).  cos/sin fp32 [positions, 32].
+std::vector<Tensor> qkv_post_fwd(const Tensor& qkv, const Tensor& cos_t, const Tensor& sin_t, const OptT& ve, const OptT& vgate,
+                                 const OptT& vadd, int64_t H, bool paired, bool key_offset) {
+  TORCH_CHECK(qkv.dim() == 2 && qkv.is_contiguous() && qkv.scalar_type() == torch::kBFloat16 && qkv.size(1) == 3 * H * 128);
+  TORCH_CHECK(cos_t.scalar_type() == torch::kFloat32 && cos_t.is_contiguous() && cos_t.size(1) == 32 && sin_t.sizes() == cos_t.sizes());
+  const int64_t T = qkv.size(0);
+  TORCH_CHECK(cos_t.size(0) >= (paired ? 2 * T : T));
+  c10::cuda::CUDAGuard guard(qkv.device());
+  auto o = qkv.options();
+  Tensor q = torch::empty({T, H, 128}, o), k = torch::empty({T, H, 128}, o), v = torch::empty({T, H, 128}, o);
+  Tensor rq = torch::empty({T * H}, o.dtype(torch::kFloat32)), rk = torch::empty({T * H}, o.dtype(torch::kFloat32));
+  int vstride = 0;
+  if (vgate.has_value() && vgate->defined()) {
+    TORCH_CHECK(vgate->scalar_type() == torch::kBFloat16 && vgate->stride(1) == 1 && vgate->size(1) >= H);
+    vstride = (int)vgate->stride(0);
+  }
+  if (ve.has_value() && ve->defined()) TORCH_CHECK(ve->is_contiguous() && ve->numel() == T * H * 128 && ve->scalar_type() == torch::kBFloat16);
+  if (vadd.has_value() && vadd->defined()) TORCH_CHECK(vadd->is_contiguous() && vadd->numel() == T * H * 128 && vadd->scalar_type() == torch::kBFloat16);
+  check(mng_qkv_post_fwd(qkv.data_ptr(), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), optr(ve), optr(vgate), vstride,
+                         optr(vadd), q.data_ptr(), k.data_ptr(), v.data_ptr(), rq.data_ptr<float>(), rk.data_ptr<float>(), T,
+                         (int)H, paired, key_offset, cur_stream()),
+        "mng_qkv_post_fwd");
+  g_launches += 1;
+  return {q, k, v, rq, rk};
+}
+
+// Returns d_qkv, d_ve (or undefined), d_vgate [T, H] bf16 (or undefined).
+std::vector<Tensor> qkv_post_bwd(const Tensor& qkv, const Tensor& cos_t, const Tensor& sin_t, const Tensor& rq, const Tensor& rk,
+                                 const Tensor& dq, const Tensor& dk, const Tensor& dv, const OptT& ve, const OptT& vgate,
+                                 int64_t H, bool paired, bool key_offset, bool need_dve, bool need_dvgate) {
+  const int64_t T = qkv.size(0);
+  TORCH_CHECK(dq.is_contiguous() && dk.is_contiguous() && dv.is_contiguous());
+  c10::cuda::CUDAGuard guard(qkv.device());
+  Tensor dqkv = torch::empty_like(qkv), dve, dvg;
+  const bool has_ve = ve.has_value() && ve->defined();
+  if (has_ve && need_dve) dve = torch::empty({T, H * 128}, qkv.options());
+  if (has_ve && need_dvgate) dvg = torch::empty({T, H}, qkv.options());
+  int vstride = (vgate.has_value() && vgate->defined()) ? (int)vgate->stride(0) : 0;
+  check(mng_qkv_post_bwd(qkv.data_ptr(), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), rq.data_ptr<float>(),
+                         rk.data_ptr<float>(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), optr(ve), optr(vgate), vstride,
+                         dqkv.data_ptr(), dve.defined() ? dve.data_ptr() : nullptr, dvg.defined() ? dvg.data_ptr() : nullptr,
+                         (int)H, T, (int)H, paired, key_offset, cur_stream()),
+        "mng_qkv_post_bwd");
+  g_launches += 1;
+  return {dqkv, dve, dvg};
+}
+
+// alpha / gate: bf16 [T, >=H] views (row stride arbitrary, unit column stride) or None.
+Tensor xsa_gate_fwd(const Tensor& y, const Tensor& v, const OptT& alpha, const OptT& gate) {
+  TORCH_CHECK(y.dim() == 3 && y.size(2) == 128 && y.is_contiguous() && v.is_contiguous() && y.scalar_type() == torch::kBFloat16);
+  c10::cuda::CUDAGuard guard(y.device());
+  Tensor out = torch::empty_like(y);
+  auto st = [](const OptT& t) { return (t.has_value() && t->defined()) ? (int)t->stride(0) : 0; };
+  if (alpha.has_value() && alpha->defined()) TORCH_CHECK(alpha->scalar_type() == torch::kBFloat16 && alpha->stride(1) == 1);
+  if (gate.has_value() && gate->defined()) TORCH_CHECK(gate->scalar_type() == torch::kBFloat16 && gate->stride(1) == 1);
+  check(mng_xsa_gate_fwd(y.data_ptr(), v.data_ptr(), optr(alpha), st(alpha), optr(gate), st(gate), out.data_ptr(), y.size(0),
+                         (int)y.size(1), cur_stream()),
+        "mng_xsa_gate_fwd");
+  g_launches += 1;
+  return out;
+}
+
+// Returns dy, dv (undefined without alpha), dalpha [T,H], dgate [T,H] (undefined when absent).
+std::vector<Tensor> xsa_gate_bwd(const Tensor& y, const Tensor& v, const OptT& alpha, const OptT& gate, const Tensor& dout) {
+  c10::cuda::CUDAGuard guard(y.device());
+  TORCH_CHECK(dout.is_contiguous());
+  const int64_t T = y.size(0), H = y.size(1);
+  const bool ha = alpha.has_value() && alpha->defined(), hg = gate.has_value() && gate->defined();
+  Tensor dy = torch::empty_like(y), dv, da, dg;
+  if (ha) {
+    dv = torch::empty_like(v);
+    da = torch::empty({T, H}, y.options());
+  }
+  if (hg) dg = torch::empty({T, H}, y.options());
+  auto st = [](const OptT& t) { return (t.has_value() && t->defined()) ? (int)t->stride(0) : 0; };
+  check(mng_xsa_gate_bwd(y.data_ptr(), v.data_ptr(), optr(alpha), st(alpha), optr(gate), st(gate), dout.data_ptr(), dy.data_ptr(),
+                         ha ? dv.data_ptr() : nullptr, ha ? da.data_ptr() : nullptr, (int)H, hg ? dg.data_ptr() : nullptr, (int)H,
+                         T, (int)H, cur_stream()),
+        "mng_xsa_gate_bwd");
+  g_launches += 1;
+  return {dy, dv, da, dg};
+}
+
+// S [H, T/128, 128, 256] fp32 -> P (same shape, bf16), a [T/128, 128, 256] bf16
+std::vector<Tensor> dc_mix_fwd(const Tensor& S, const Tensor& w1, const Tensor& doc_start, int64_t window) {
+  TORCH_CHECK(S.dim() == 4 && S.is_contiguous() && S.scalar_type() == torch::kFloat32 && S.size(2) == 128 && S.size(3) == 256);
+  const int64_t H = S.size(0), T = S.size(1) * 128;
+  TORCH_CHECK(w1.is_contiguous() && w1.scalar_type() == torch::kBFloat16 && w1.numel() == T * H);
+  TORCH_CHECK(doc_start.is_contiguous() && doc_start.scalar_type() == torch::kInt32 && doc_start.numel() == T);
+  c10::cuda::CUDAGuard guard(S.device());
+  Tensor P = torch::empty(S.sizes(), S.options().dtype(torch::kBFloat16));
+  Tensor a = torch::empty({S.size(1), 128, 256}, S.options().dtype(torch::kBFloat16));
+  check(mng_dc_mix_fwd(S.data_ptr<float>(), w1.data_ptr(), doc_start.data_ptr<int>(), P.data_ptr(), a.data_ptr(), T, (int)H,
+                       (int)window, cur_stream()),
+        "mng_dc_mix_fwd");
+  g_launches += 1;
+  return {P, a};
+}
+
+// returns dS [H, T/128, 128, 256] bf16, g_w1, g_w2 [T, H] fp32
+std::vector<Tensor> dc_mix_bwd(const Tensor& dM, const Tensor& P, const Tensor& a, const Tensor& w1, const Tensor& w2, double scale) {
+  TORCH_CHECK(dM.is_contiguous() && dM.scalar_type() == torch::kFloat32 && P.is_contiguous() && a.is_contiguous());
+  TORCH_CHECK(w1.is_contiguous() && w2.is_contiguous() && w2.scalar_type() == torch::kBFloat16);
+  const int64_t H = dM.size(0), T = dM.size(1) * 128;
+  c10::cuda::CUDAGuard guard(dM.device());
+  Tensor dS = torch::empty(dM.sizes(), dM.options().dtype(torch::kBFloat16));
+  Tensor g1 = torch::empty({T, H}, dM.options()), g2 = torch::empty({T, H}, dM.options());
+  check(mng_dc_mix_bwd(dM.data_ptr<float>(), P.data_ptr(), a.data_ptr(), w1.data_ptr(), w2.data_ptr(), dS.data_ptr(),
+                       g1.data_ptr<float>(), g2.data_ptr<float>(), T, (int)H, (float)scale, cur_stream()),
+        "mng_dc_mix_bwd");
+  g_launches += 1;
+  return {dS, g1, g2};
 }
 
 Tensor status_tensor(const Tensor& like) {
@@ -267,5 +468,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("scale_by_norm", &scale_by_norm);
   m.def("normuon_apply", &normuon_apply);
   m.def("peer_barrier", &peer_barrier);
+  m.def("lincomb_fwd", &lincomb_fwd);
+  m.def("lincomb_bwd", &lincomb_bwd);
+  m.def("qkv_post_fwd", &qkv_post_fwd);
+  m.def("qkv_post_bwd", &qkv_post_bwd);
+  m.def("xsa_gate_fwd", &xsa_gate_fwd);
+  m.def("xsa_gate_bwd", &xsa_gate_bwd);
+  m.def("dc_mix_fwd", &dc_mix_fwd);
+  m.def("dc_mix_bwd", &dc_mix_bwd);
   m.def("status_tensor", &status_tensor);
+  m.def("launch_count", &launch_count);
 }

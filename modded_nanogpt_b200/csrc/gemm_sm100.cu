@@ -24,7 +24,9 @@ struct EpiStore {
     long long ld, bstride;      // elements
     float alpha, beta;
   };
-  __device__ static void apply(const Params& p, const float (&acc)[32], int b, int row, int col0, int M, int N) {
+  struct State {};
+  __device__ static void finish(const Params&, State&) {}
+  __device__ static void apply(const Params& p, State&, const float (&acc)[32], int b, int row, int col0, int M, int N) {
     if (row >= M) return;
     float a = p.alpha;
     if (p.alpha_ptr) a *= *p.alpha_ptr;
@@ -106,7 +108,13 @@ struct EpiRelu2 {
     unsigned int* amax_bits;    // device scalar, float bits (values are >= 0 so integer max works)
     long long ld;
   };
-  __device__ static void apply(const Params& p, const float (&acc)[32], int b, int row, int col0, int M, int N) {
+  struct State { float mx = 0.f; };
+  // one atomic per epilogue warp for the whole kernel (a per-chunk atomic on one address serialises)
+  __device__ static void finish(const Params& p, State& st) {
+    const float m = warp_max(st.mx);
+    if (p.post8 && (threadIdx.x & 31) == 0 && m > 0.f) atomicMax(p.amax_bits, __float_as_uint(m));
+  }
+  __device__ static void apply(const Params& p, State& st, const float (&acc)[32], int b, int row, int col0, int M, int N) {
     // N is a multiple of 32 for this epilogue (checked on the host).  Rows past M stay in the warp
     // (the amax reduction below is a warp collective) with their stores predicated off.
     const bool live = row < M;
@@ -146,8 +154,7 @@ struct EpiRelu2 {
         }
         *reinterpret_cast<uint4*>(o8 + j) = make_uint4(w[0], w[1], w[2], w[3]);
       }
-      mx = warp_max(mx);
-      if ((threadIdx.x & 31) == 0 && mx > 0.f) atomicMax(p.amax_bits, __float_as_uint(mx));
+      st.mx = fmaxf(st.mx, mx);
     }
   }
 };
@@ -159,7 +166,9 @@ struct EpiDpre {
     const __nv_bfloat16* post;
     long long ld;
   };
-  __device__ static void apply(const Params& p, const float (&acc)[32], int b, int row, int col0, int M, int N) {
+  struct State {};
+  __device__ static void finish(const Params&, State&) {}
+  __device__ static void apply(const Params& p, State&, const float (&acc)[32], int b, int row, int col0, int M, int N) {
     if (row >= M) return;
     const long long off = (long long)row * p.ld + col0;
 #pragma unroll
@@ -233,6 +242,12 @@ static int cached_map(CUtensorMap* out, const void* ptr, int es, long long inner
   std::lock_guard<std::mutex> g(mu);
   auto it = cache.find(k);
   if (it == cache.end()) {
+    // Encoding needs a current driver context; a thread that has not yet run any runtime call (an
+    // autograd worker whose first op is one of ours) has none until the runtime binds the primary one.
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaSetDevice(dev);
+    cudaFree(nullptr);
     CUtensorMap m;
     int rc = make_tensor_map(&m, ptr, es, inner, outer, batch, ld, bs, bi, bo);
     if (rc) return rc;

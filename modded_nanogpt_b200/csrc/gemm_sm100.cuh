@@ -7,8 +7,8 @@
 //   shared-memory ring, one elected thread issues tcgen05.mma, accumulators live in TMEM and are
 //   double buffered so the epilogue of tile i overlaps the main loop of tile i+1;
 // * CTA tile 128 x BN (BN = 128 or 256), K step = 128 bytes of K per operand row;
-// * warp 0 = TMA producer, warp 1 = MMA issuer (+ TMEM allocation), warps 2..5 = epilogue (each owns
-//   the 32-lane TMEM sub-partition `warp_id % 4`);
+// * warp 0 = TMA producer, warp 1 = MMA issuer (+ TMEM allocation), warps 2..9 = epilogue (warp w reads
+//   the 32-lane TMEM sub-partition `w % 4`; warps 2..5 take the left half of the tile's columns, 6..9 the right);
 // * epilogues are functors applied to 32-column register fragments (see epilogues in gemm_sm100.cu);
 // * no cluster launch, no multicast loads; every mbarrier wait is bounded.
 #pragma once
@@ -17,7 +17,8 @@
 namespace mng {
 
 constexpr int GEMM_BM = 128;
-constexpr int GEMM_THREADS = 192;
+constexpr int GEMM_THREADS = 320;
+constexpr int GEMM_EPI_WARPS = 8;
 constexpr int GEMM_STAGE_K_BYTES = 128;   // bytes of K per row and stage (one swizzle span)
 
 struct GemmShape {
@@ -35,9 +36,11 @@ struct GemmSmem {
 };
 
 // Epilogue contract:
-//   struct Epi { struct Params {...};
-//     __device__ static void apply(const Params&, const float (&acc)[32], int batch, int row, int col0,
-//                                  int M, int N); }
+//   struct Epi { struct Params {...}; struct State {...};
+//     __device__ static void apply(const Params&, State&, const float (&acc)[32], int batch, int row, int col0,
+//                                  int M, int N);
+//     __device__ static void finish(const Params&, State&);   // once per epilogue thread, after its last tile
+//   }
 // `acc[j]` is element (row, col0 + j) of the tile product; rows/cols beyond M/N must be skipped.
 
 template <int BN, int ES, bool A_MN, bool B_MN, uint32_t A_FMT, uint32_t B_FMT, class Epi>
@@ -80,7 +83,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_cons
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&tfull_bar[s], 1);
-      mbar_init(&tempty_bar[s], 4);                     // one arrival per epilogue warp
+      mbar_init(&tempty_bar[s], GEMM_EPI_WARPS);        // one arrival per epilogue warp
     }
     *abort_flag = 0;
     mbar_fence_init();
@@ -178,8 +181,10 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_cons
   } else {
     // ------------------------------ epilogue warps ----------------------------------------------
     const int q = warp & 3;                             // TMEM sub-partition of this warp
+    const int c_begin = ((warp - 2) >> 2) * (BN / 64);  // first 32-column chunk of this warp's half
     int acc = 0;
     uint32_t acc_phase = 0;
+    typename Epi::State est{};                         // per-thread state carried across tiles (e.g. a running max)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int b = tile / (tiles_m * tiles_n);
       const int r = tile - b * tiles_m * tiles_n;
@@ -193,14 +198,14 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_cons
       const int row = m0 + q * 32 + lane;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = c_begin; c < c_begin + BN / 64; ++c) {
         uint32_t v[32];
         tmem_ld32(taddr + c * 32, v);
         tmem_ld_wait();
         float f[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
-        if (n0 + c * 32 < shape.N) Epi::apply(ep, f, b, row, n0 + c * 32, shape.M, shape.N);
+        if (n0 + c * 32 < shape.N) Epi::apply(ep, est, f, b, row, n0 + c * 32, shape.M, shape.N);
       }
       tc_fence_before();
       __syncwarp();
@@ -208,6 +213,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_cons
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    Epi::finish(ep, est);
   }
 
   // ------------------------------ common exit ---------------------------------------------------

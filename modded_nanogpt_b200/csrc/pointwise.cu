@@ -229,7 +229,7 @@ using namespace mng;
     return cudaGetLastError() == cudaSuccess ? 0 : -2;                                        \
   } while (0)
 
-static const float kRmsEps = 0.0078125f;   // torch.finfo(bfloat16).eps: what F.rms_norm(eps=None) uses on bf16 input
+static const float kRmsEps = 1.1920929e-07f;   // F.rms_norm(eps=None) uses the eps of the fp32 computation dtype, also for bf16 input
 
 extern "C" int mng_rmsnorm_fwd(const void* x, void* y, void* y8, float* row_scale, float* rstd, long long rows, int cols,
                                void* stream) {

@@ -163,6 +163,8 @@ class TokenLoader:
         self.pos = 0
         self._pin = self.device.type == "cuda"
         self._stage = {}
+        self.count_bytes = False
+        self.bytes_copied = 0
         tokens = read_shard(self.files[0], pin=self._pin)
         if align_to_bos:
             self.shard = Shard(tokens, world_size)
@@ -250,6 +252,8 @@ class TokenLoader:
         dev = self.device
         to = (lambda t: t.to(dev, non_blocking=True)) if dev.type == "cuda" else (lambda t: t.clone())
         nbytes = sum(st[k].numel() * st[k].element_size() for k in ("inp", "tgt", "cu", "bg"))
+        if self.count_bytes and dev.type == "cuda":
+            self.bytes_copied += nbytes
         return Batch(to(st["inp"]), to(st["tgt"]), to(st["cu"]), to(st["bg"]), st["bg"].numpy().copy(), nbytes)
 
     __next__ = next_batch

@@ -278,10 +278,12 @@ class GPT(nn.Module):
         out = F.linear(h, self.mudd_gate_w2[gid, :n].type_as(x)) + self.mudd_gate_b2[gid, :n].type_as(x)
         return out * self._mudd_gate_scale.type_as(x)
 
-    def _mudd(self, x: Tensor, mid: int, n: int):
+    def _mudd_raw(self, x: Tensor, mid: int, n: int) -> Tensor:
         h = F.gelu(F.linear(x, self.mudd_w1[mid].type_as(x)))
-        out = (F.linear(h, self.mudd_w2[mid, :n].type_as(x)) + self.mudd_b2[mid, :n].type_as(x)) * self._mudd_scale
-        return out.split(1, dim=-1)
+        return (F.linear(h, self.mudd_w2[mid, :n].type_as(x)) + self.mudd_b2[mid, :n].type_as(x)) * self._mudd_scale
+
+    def _mudd(self, x: Tensor, mid: int, n: int):
+        return self._mudd_raw(x, mid, n).split(1, dim=-1)
 
     def _attention(self, pl: LayerPlan, x: Tensor, w_qkvo: Tensor, sa_lambdas: Tensor, seqlens: Tensor,
                    window: int, max_len: int, aux_v, xsa_alpha, attn_gate, dc_w):
@@ -327,12 +329,16 @@ class GPT(nn.Module):
         state = None
         if training_fp8 and self._fp8_state is not None:
             state = self._fp8_state.layer(i)
-        return ops.relu2_mlp(ops.rms_norm(x), w_fc, w_proj, state)
+        return ops.norm_relu2_mlp(x, w_fc, w_proj, state)
 
     # ----------------------------------------------------------------------------------
     def forward(self, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, bigram_input_seq: Tensor,
                 schedule_cfg: ForwardScheduleConfig) -> Tensor:
         assert input_seq.ndim == 1
+        if input_seq.is_cuda:
+            from .gpt_fused import forward_fused, fused_supported
+            if fused_supported(self, input_seq):
+                return forward_fused(self, input_seq, target_seq, seqlens, bigram_input_seq, schedule_cfg)
         cfg, L, H, Dh, D, V = self.cfg, self.num_layers, self.num_heads, self.head_dim, self.model_dim, self.vocab_size
         T = input_seq.size(0)
         ws = {False: schedule_cfg.ws_short, True: schedule_cfg.ws_long}

@@ -1,0 +1,163 @@
+"""CUDA execution path of `GPT.forward`: the same math as the op-by-op forward in `gpt.py`, with
+every residual / gate / norm / rotary step routed through the fused sm_100a kernels
+(`ops.glue`, `ops.fused`).  Selected automatically for bf16 CUDA models with head_dim 128 and
+model_dim a multiple of 256; `ops.set_backend("reference")` switches it off for A/B tests."""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+from torch import Tensor
+
+from ..ops import functional as ops
+from ..ops import fused
+from ..ops.glue import Term, lincomb, qkv_post, xsa_gate
+
+
+def fused_supported(model, x: Tensor) -> bool:
+    from .. import ops as ops_pkg
+    return (x.is_cuda and ops_pkg.get_backend() != "reference" and model.head_dim == 128 and model.model_dim % 256 == 0
+            and model.model_dim <= 1024 and model.lm_head.weight.dtype == torch.bfloat16
+            and (model.cfg.bigram_dim in (0, model.model_dim)) and ops_pkg.use_kernel("glue", x))
+
+
+def _rope_tables(yarn, n: int, device):
+    """fp32 cos/sin [n, 32] of the 32 distinct rotary frequencies, values rounded to bf16 like the
+    reference's tables (`train_gpt.py:1013-1032`)."""
+    cache = getattr(yarn, "_t32", None)
+    if cache is None or cache[0] != yarn._version or cache[1].size(0) < n or cache[1].device != device:
+        t = torch.arange(n, dtype=torch.float32, device=device)
+        theta = torch.outer(t, yarn.angular_freq.to(device)[0:yarn.head_dim // 2:2])
+        cache = (yarn._version, theta.cos().bfloat16().float().contiguous(), theta.sin().bfloat16().float().contiguous())
+        yarn._t32 = cache
+    return cache[1], cache[2]
+
+
+def forward_fused(m, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, bigram_input_seq: Tensor, sc) -> Tensor:
+    cfg, L, H, Dh, D, V = m.cfg, m.num_layers, m.num_heads, m.head_dim, m.model_dim, m.vocab_size
+    T = input_seq.size(0)
+    ws = {False: sc.ws_short, True: sc.ws_long}
+    max_len = sc.train_max_seq_len if m.training else m.eval_seq_len
+    training_fp8 = m.training and m.use_fp8
+    track1 = m.track1
+
+    sa_lambdas = m.scalars[:2 * L].view(L, 2)
+    smear_lambda, skip_lambda = m.scalars[2 * L], m.scalars[2 * L + 1]
+    qk_all, vo_all = m.attn_layer_weights()
+    resid, post = m.resid_lambdas, m.post_lambdas
+
+    ids = input_seq.long()
+    x = F.embedding(ids, m.embed.weight)
+    x0_bigram = None
+    if cfg.bigram_vocab_size:
+        sign_idx = torch.zeros_like(ids)
+        sign_idx[1:] = (ids[:-1] ^ ids[1:]) % m.bigram_sign_table.shape[0]
+        x0_bigram = F.embedding(bigram_input_seq.long(), m.bigram_embed.weight) * m.bigram_sign_table[sign_idx]
+    ve = None
+    if cfg.num_value_embeds:
+        # one gather over the flat table (ids offset per table): a single embedding backward into one
+        # [n*V, D] gradient instead of n full-size zero-filled select_backward tensors
+        n = cfg.num_value_embeds
+        offs = torch.arange(n, device=ids.device)[:, None] * V
+        ve = F.embedding((ids[None, :] + offs).reshape(-1), m.value_embeds).view(n, T, D).unbind(0)
+
+    # smear: x[t] += smear_lambda * sigmoid(W x[t, :12]) * x[t-1]
+    g = torch.zeros(T, 1, dtype=x.dtype, device=x.device)
+    g[1:] = smear_lambda * torch.sigmoid(F.linear(x[1:, :12], m.smear_gate.weight))
+    x_prev = torch.cat([x[:1], x[:-1]])
+    x = lincomb([Term(x), Term(x_prev, gate=g, col=0)])
+    x = x0 = fused.rms_norm(x)
+
+    cos_t, sin_t = _rope_tables(m.yarn, 2 * T, x.device)
+    cos_p, sin_p = _rope_tables(m.yarn_paired_head, 2 * T, x.device)
+
+    pre = pg = None
+    lay0 = lay1 = None
+    if track1:
+        pre = m._gate_mlp(x0, 0)
+        lay0, lay1 = m.gate_layouts
+        x = lincomb([Term(x0), Term(x0_bigram, gate=pre, col=lay0["inject"][0] + 1)])
+    cache = {0: x}
+    normed7 = None
+
+    def gate_of(i):
+        return (pre, lay0) if i < m.post_gate_layer else (pg, lay1)
+
+    for pl in m.plan:
+        i, mu = pl.index, None
+        if track1 and i == m.post_gate_layer:
+            pg = m._gate_mlp(x, 1)
+
+        if not pl.has_attn:
+            sk = torch.sigmoid(skip_lambda).reshape(1)
+            x = lincomb([Term(x), Term(cache[3], scalar=sk, gate=pg, col=lay1["skip"])])
+        else:
+            w_qkvo = torch.cat([qk_all[pl.attn_slot], vo_all[pl.attn_slot]], dim=0)
+            if track1 and 7 in cache:
+                if normed7 is None:
+                    normed7 = fused.rms_norm(cache[7])
+                attn_in = normed7
+            else:
+                attn_in = fused.rms_norm(x)
+            ve_t = vgate = vadd = None
+            if track1 and pl.last:
+                cache[9] = x
+                mu = m._mudd_raw(x, 0, 14)                                    # [T, 14]
+                vadd = lincomb([Term(cache[0], gate=mu, col=0), Term(cache[7], gate=mu, col=1), Term(x, gate=mu, col=2)])
+                x = lincomb([Term(x, gate=mu, col=5, addc=1.0), Term(cache[0], gate=mu, col=3), Term(cache[7], gate=mu, col=4)])
+                vgate = mu[:, 6:8].repeat_interleave(H // 2, dim=-1).contiguous()
+                ve_t = ve[pl.ve_slot]
+            elif pl.ve_slot >= 0:
+                ve_t = ve[pl.ve_slot]
+                gate_in = torch.cat([attn_in[:, :6], ve_t[:, :6]], dim=-1)
+                vgate = (2 * torch.sigmoid(F.linear(gate_in, m.ve_gate_bank[pl.ve_slot]))).contiguous()
+            qkv = F.linear(attn_in, sa_lambdas[i, 0] * w_qkvo[:3 * D])
+            yarn = m.yarn_paired_head if pl.paired else m.yarn
+            ct, st = (cos_p, sin_p) if pl.paired else (cos_t, sin_t)
+            q, k, v = qkv_post(qkv, ct, st, ve_t, vgate, vadd, H, pl.paired, pl.long_window and not pl.paired)
+            if pl.paired:
+                y = ops.attention(q.view(2 * T, H // 2, Dh), k.view(2 * T, H // 2, Dh), v.view(2 * T, H // 2, Dh),
+                                  2 * seqlens, ws[pl.long_window], yarn.attn_scale, 2 * max_len).view(T, H, Dh)
+            else:
+                y = ops.attention(q, k, v, seqlens, ws[pl.long_window], yarn.attn_scale, max_len)
+            gt, lay = gate_of(i) if track1 else (None, None)
+            if track1 and pl.dc and not pl.paired:
+                o = lay1["dc"]
+                w1 = F.rms_norm(pg[:, o:o + H].float(), (H,), eps=1e-6).to(x.dtype).contiguous()
+                w2 = pg[:, o + H:o + 2 * H].contiguous()
+                y = ops.dc_correction(y, q, k, v, w1, w2, seqlens, yarn.attn_scale, cfg.dc_window)
+            if track1:
+                alpha = gt[:, lay["xsa"][i]:lay["xsa"][i] + H] if (pl.xsa and not pl.paired) else None
+                agate = gt[:, lay["attn"][i]:lay["attn"][i] + H] if pl.attn_gate else None
+                y = xsa_gate(y, v, alpha, agate)
+            attn_out = F.linear(y.reshape(T, D), sa_lambdas[i, 1] * w_qkvo[3 * D:])
+            if mu is not None:
+                x = lincomb([Term(x, gate=mu, col=8), Term(attn_out, gate=mu, col=9), Term(cache[0], gate=mu, col=10),
+                             Term(x0_bigram, gate=mu, col=11)])
+            elif track1:
+                o = lay["inject"][i]
+                terms = [Term(x, scalar=resid[i, 0]), Term(attn_out, scalar=post[i, 0]), Term(x0, gate=gt, col=o)]
+                if i != 0:
+                    terms.append(Term(x0_bigram, gate=gt, col=o + 1))
+                x = lincomb(terms)
+            else:
+                x = lincomb([Term(x, scalar=resid[i, 0]), Term(attn_out, scalar=post[i, 0])])
+
+        h = m._mlp(i, x, training_fp8)
+        if mu is not None:
+            x = lincomb([Term(x, gate=mu, col=12), Term(h, gate=mu, col=13)])
+        else:
+            x = lincomb([Term(x, scalar=resid[i, 1]), Term(h, scalar=post[i, 1])])
+        if pl.cache:
+            cache[i] = x
+
+    if track1:
+        mu = m._mudd_raw(x, 1, 5)
+        x = lincomb([Term(x), Term(cache[0], gate=mu, col=0), Term(cache[7], gate=mu, col=1), Term(cache[9], gate=mu, col=2),
+                     Term(ve[0], gate=mu, col=3), Term(cache[3], gate=mu, col=4)])
+    x = fused.rms_norm(x)
+
+    if m.training:
+        prefix_targets = m.prefix_table[target_seq]
+        return ops.softcap_ce(x, m.lm_head.weight, target_seq, sc.mtp_weights, prefix_targets, sc.prefix_weight,
+                              cfg.softcap_a, cfg.softcap_b, cfg.softcap_c, grad_scale=m.grad_scale, fp8=m.use_fp8)
+    return ops.softcap_ce_eval(x, m.lm_head.weight, target_seq, cfg.softcap_a, cfg.softcap_b, cfg.softcap_c)

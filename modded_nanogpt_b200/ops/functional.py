@@ -30,9 +30,9 @@ def attention(q: Tensor, k: Tensor, v: Tensor, cu_seqlens: Tensor, window: int, 
 
 def dc_correction(base, q, k, v, w1, w2, cu_seqlens, scale, window=112) -> Tensor:
     if use_kernel("dc", q) and q.dtype == torch.bfloat16:
-        from . import fused
-        if fused.dc_supported(q, window):
-            return fused.dc_correction(base, q, k, v, w1, w2, cu_seqlens, scale, window)
+        from . import dc
+        if dc.supported(q, window):
+            return dc.dc_correction(base, q, k, v, w1, w2, cu_seqlens, scale, window)
     return ref.dc_correction(base, q, k, v, w1, w2, cu_seqlens, scale, window)
 
 
@@ -43,6 +43,14 @@ def relu2_mlp(x: Tensor, w_fc: Tensor, w_proj: Tensor, fp8_state=None) -> Tensor
         from . import fused
         return fused.relu2_mlp(x, w_fc, w_proj, fp8_state)
     return ref.relu2_mlp(x, w_fc, w_proj)
+
+
+def norm_relu2_mlp(x: Tensor, w_fc: Tensor, w_proj: Tensor, fp8_state=None) -> Tensor:
+    """relu(norm(x) w_fc^T)^2 w_proj with the RMSNorm (and, for FP8, the row quantisation) fused in."""
+    if use_kernel("mlp", x) and x.dtype == torch.bfloat16 and x.shape[-1] % 256 == 0:
+        from . import fused
+        return fused.norm_relu2_mlp(x, w_fc, w_proj, fp8_state)
+    return ref.relu2_mlp(ref.rms_norm(x), w_fc, w_proj)
 
 
 def softcap_ce(x, w, targets, mtp_weights, prefix_targets, prefix_weight, a, b, c, grad_scale: float = 1.0,

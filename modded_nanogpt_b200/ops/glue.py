@@ -1,0 +1,143 @@
+"""Autograd wrappers of the fused glue kernels (csrc/glue.cu).
+
+`lincomb`   out = sum_j (addc_j + s_j * g_j[t]) * x_j[t, :] - every residual / skip / MUDD mix of
+            `train_gpt.py:1547-1680` is one call instead of a chain of broadcast multiplies and adds;
+            its backward produces all input gradients, the per-token coefficient gradients and the
+            scalar-parameter gradients in one pass.
+`qkv_post`  QK RMSNorm + rotary + key offset + value-embedding add (`train_gpt.py:1103-1136`).
+`xsa_gate`  gated XSA and the per-head attention gate (`train_gpt.py:1150-1159`).
+"""
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from .native import lib
+
+
+class Term:
+    """One summand of `lincomb`: x * (addc + scalar * gate[:, col])."""
+    __slots__ = ("x", "scalar", "gate", "col", "addc")
+
+    def __init__(self, x: Tensor, scalar: Tensor | None = None, gate: Tensor | None = None, col: int = 0, addc: float = 0.0):
+        self.x, self.scalar, self.gate, self.col, self.addc = x, scalar, gate, col, addc
+
+
+class _LinComb(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, meta, *tensors):
+        k, sidx, gidx, cols, addc = meta
+        xs = [t.contiguous() for t in tensors[:k]]
+        scalars = [tensors[i] if i >= 0 else None for i in sidx]
+        gates = [tensors[i] if i >= 0 else None for i in gidx]
+        out = lib().lincomb_fwd(xs, scalars, gates, cols, addc)
+        ctx.meta = meta
+        ctx.save_for_backward(*xs, *tensors[k:])
+        return out
+
+    @staticmethod
+    def backward(ctx, gout):
+        k, sidx, gidx, cols, addc = ctx.meta
+        tensors = ctx.saved_tensors
+        xs = list(tensors[:k])
+        scalars = [tensors[i] if i >= 0 else None for i in sidx]
+        gates = [tensors[i] if i >= 0 else None for i in gidx]
+        need = ctx.needs_input_grad[1:]
+        grads: list = [None] * len(tensors)
+        dgate_bufs, dscal_bufs = {}, {}
+        dgates, dscalars = [], []
+        for j in range(k):
+            gi, si = gidx[j], sidx[j]
+            if gi >= 0 and need[gi]:
+                if gi not in dgate_bufs:
+                    dgate_bufs[gi] = torch.zeros_like(tensors[gi], dtype=torch.bfloat16)
+                dgates.append(dgate_bufs[gi])
+            else:
+                dgates.append(None)
+            if si >= 0 and need[si]:
+                if si not in dscal_bufs:
+                    dscal_bufs[si] = torch.zeros(1, dtype=torch.float32, device=gout.device)
+                dscalars.append(dscal_bufs[si])
+            else:
+                dscalars.append(None)
+        dxs = lib().lincomb_bwd(xs, scalars, gates, cols, addc, gout.contiguous(), [bool(n) for n in need[:k]], dgates, dscalars)
+        for j in range(k):
+            grads[j] = dxs[j]
+        for gi, buf in dgate_bufs.items():
+            grads[gi] = buf if tensors[gi].dtype == torch.bfloat16 else buf.to(tensors[gi].dtype)
+        for si, buf in dscal_bufs.items():
+            grads[si] = buf.view(tensors[si].shape)
+        return (None, *grads)
+
+
+def lincomb(terms: list[Term]) -> Tensor:
+    k = len(terms)
+    extra, index = [], {}
+
+    def slot(t):
+        if t is None:
+            return -1
+        key = id(t)
+        if key not in index:
+            index[key] = k + len(extra)
+            extra.append(t)
+        return index[key]
+
+    sidx = [slot(t.scalar) for t in terms]
+    gidx = [slot(t.gate) for t in terms]
+    meta = (k, sidx, gidx, [int(t.col) for t in terms], [float(t.addc) for t in terms])
+    return _LinComb.apply(meta, *[t.x for t in terms], *extra)
+
+
+class _QkvPost(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, cos_t, sin_t, ve, vgate, vadd, H, paired, key_offset):
+        qkv = qkv.contiguous()
+        if ve is not None:
+            ve = ve.contiguous()
+        if vadd is not None:
+            vadd = vadd.contiguous()
+        q, k, v, rq, rk = lib().qkv_post_fwd(qkv, cos_t, sin_t, ve, vgate, vadd, H, paired, key_offset)
+        ctx.save_for_backward(qkv, cos_t, sin_t, rq, rk, ve, vgate)
+        ctx.cfg = (H, paired, key_offset, vadd is not None)
+        return q, k, v
+
+    @staticmethod
+    def backward(ctx, dq, dk, dv):
+        qkv, cos_t, sin_t, rq, rk, ve, vgate = ctx.saved_tensors
+        H, paired, key_offset, has_vadd = ctx.cfg
+        dv = dv.contiguous()
+        need_dve = ve is not None and ctx.needs_input_grad[3]
+        need_dvg = vgate is not None and ctx.needs_input_grad[4]
+        dqkv, dve, dvg = lib().qkv_post_bwd(qkv, cos_t, sin_t, rq, rk, dq.contiguous(), dk.contiguous(), dv, ve, vgate, H,
+                                            paired, key_offset, need_dve, need_dvg)
+        dvadd = dv.view(qkv.shape[0], -1) if has_vadd else None
+        return dqkv, None, None, dve, dvg, dvadd, None, None, None
+
+
+def qkv_post(qkv: Tensor, cos_t: Tensor, sin_t: Tensor, ve: Tensor | None, vgate: Tensor | None, vadd: Tensor | None,
+             H: int, paired: bool, key_offset: bool):
+    """qkv [T, 3*H*128] -> q, k, v [T, H, 128].  v = v + vgate[t,h]*ve[t,h,:] + vadd[t,h,:]."""
+    return _QkvPost.apply(qkv, cos_t, sin_t, ve, vgate, vadd, H, paired, key_offset)
+
+
+class _XsaGate(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, y, v, alpha, gate):
+        y, v = y.contiguous(), v.contiguous()
+        out = lib().xsa_gate_fwd(y, v, alpha, gate)
+        ctx.save_for_backward(y, v, alpha, gate)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        y, v, alpha, gate = ctx.saved_tensors
+        dy, dv, da, dg = lib().xsa_gate_bwd(y, v, alpha, gate, dout.contiguous())
+        return dy, dv, da, dg
+
+
+def xsa_gate(y: Tensor, v: Tensor, alpha: Tensor | None, gate: Tensor | None) -> Tensor:
+    """y, v [T, H, 128]; alpha, gate: bf16 [T, H] (possibly column slices of a wider gate tensor)."""
+    if alpha is None and gate is None:
+        return y
+    return _XsaGate.apply(y, v, alpha, gate)

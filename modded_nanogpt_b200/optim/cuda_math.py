@@ -1,0 +1,118 @@
+"""Per-shard optimizer math on the sm_100a kernels.
+
+`CudaMath` has the interface of `TorchMath` (normuon_direction / normuon_apply / adam /
+transpose_add / transpose_copy).  Polar Express runs as batched tcgen05 GEMMs:
+tall matrices iterate on A = X^T X (both operands read MN-major in place, no transposes),
+wide ones on A = X X^T; B = b*A + c*A@A and X' = a*X + X@B (or B@X) use the GEMM's fused
+alpha/beta epilogue, so one iteration is three launches (`train_gpt.py:202-253` needs a
+Triton kernel per product plus cuBLAS baddbmm).
+
+When `grad_ptrs` / `param_ptrs` (peer addresses over NVLink) are given, the first kernel sums
+the gradient shard straight out of every rank's gradient buffer (reduce-scatter fused into the
+momentum update) and the last kernel stores the new weights into every rank's parameter tensor
+(all-gather fused into the weight update).
+"""
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from ..ops import fused
+from ..ops import reference as ref
+from ..ops.native import lib
+from .normuon_adam import ParamConfig, TorchMath
+
+
+class CudaMath(TorchMath):
+    def __init__(self, rank: int = 0):
+        super().__init__(torch.bfloat16)
+        self.rank = rank
+        self._scratch: dict = {}
+
+    def _buf(self, key, shape, dtype, device):
+        t = self._scratch.get(key)
+        if t is None or t.shape != torch.Size(shape) or t.dtype != dtype:
+            t = torch.empty(shape, dtype=dtype, device=device)
+            self._scratch[key] = t
+        return t
+
+    # ------------------------------------------------------------------------------------------
+    def polar_express(self, X: Tensor) -> Tensor:
+        """X: [mats, rows, cols] bf16, already normalised.  Returns the orthogonalised X (bf16)."""
+        mats, rows, cols = X.shape
+        tall = rows > cols
+        n = cols if tall else rows
+        A = self._buf(("A", mats, n), (mats, n, n), torch.bfloat16, X.device)
+        B = self._buf(("B", mats, n), (mats, n, n), torch.bfloat16, X.device)
+        Y = self._buf(("Y", mats, rows, cols), (mats, rows, cols), torch.bfloat16, X.device)
+        for a, b, c in ref.POLAR_EXPRESS_COEFFS:
+            if tall:
+                fused.gemm(X, X, a_mn=True, b_mn=True, out=A)                       # A = X^T X
+            else:
+                fused.gemm(X, X, out=A)                                             # A = X X^T
+            fused.gemm(A, A, b_mn=True, out=B, alpha=c, beta=b, cin=A)              # B = b A + c A A
+            if tall:
+                fused.gemm(X, B, b_mn=True, out=Y, alpha=1.0, beta=a, cin=X)        # X' = a X + X B
+            else:
+                fused.gemm(B, X, b_mn=True, out=Y, alpha=1.0, beta=a, cin=X)        # X' = a X + B X
+            X, Y = Y, X
+        return X
+
+    def normuon_direction(self, grad_chunk: Tensor, state: dict, cfg: ParamConfig, grad_ptrs=None, off: int = 0,
+                          grad_mul: float = 1.0) -> Tensor:
+        C = lib()
+        buf = state["momentum_buffer"]
+        shape = buf.shape
+        X = self._buf(("X", cfg.label), shape, torch.bfloat16, buf.device)
+        ss = self._buf(("ss", cfg.label), (shape[0],), torch.float32, buf.device)
+        if grad_ptrs is None:
+            grad_chunk = grad_chunk.contiguous()
+            grad_ptrs, off = [grad_chunk.data_ptr()], 0
+        C.nesterov(grad_ptrs, self.rank, off, buf, X, ss, float(cfg.momentum), grad_mul)
+        C.scale_by_norm(X, ss)
+        return self.polar_express(X)
+
+    def normuon_apply(self, p_slice: Tensor, state: dict, v: Tensor, cfg: ParamConfig, param_ptrs=None, off: int = 0) -> None:
+        C = lib()
+        mats, rows, cols = v.shape
+        red_rows = rows >= cols
+        eff_wd = cfg.wd_mul * cfg.weight_decay * cfg.lr
+        mul = cfg.per_matrix_lr_mul or [1.0] * mats
+        key = ("lr", cfg.label)
+        lrs_host = [cfg.lr_mul * m * cfg.lr for m in mul]
+        lrs = self._buf(key, (mats,), torch.float32, v.device)
+        lrs.copy_(torch.tensor(lrs_host, dtype=torch.float32), non_blocking=True)
+        scratch = self._buf(("sc", cfg.label), (mats * max(rows, cols),), torch.float32, v.device)
+        if param_ptrs is None:
+            assert p_slice.is_contiguous()
+            param_ptrs, off = [p_slice.data_ptr()], 0
+        C.normuon_apply(param_ptrs, self.rank, off, state["mantissa"], v.contiguous(), state["second_momentum_buffer"],
+                        scratch, red_rows, float(cfg.beta2), float(eff_wd), lrs)
+
+    def adam(self, p_slice: Tensor, grad: Tensor, state: dict, cfg: ParamConfig, step_size: float, eff_wd: float,
+             grad_ptrs=None, param_ptrs=None, off: int = 0, grad_mul: float = 1.0) -> None:
+        n = p_slice.numel()
+        is_f32 = p_slice.dtype == torch.float32
+        vec = 4 if is_f32 else 8
+        ok = (p_slice.is_cuda and n % vec == 0 and p_slice.is_contiguous()
+              and (grad_ptrs is not None or (grad.is_contiguous() and grad.dtype == p_slice.dtype))
+              and p_slice.dtype in (torch.float32, torch.bfloat16) and p_slice.data_ptr() % 16 == 0)
+        if not ok:
+            return super().adam(p_slice, grad, state, cfg, step_size, eff_wd)
+        if grad_ptrs is None:
+            grad_ptrs, param_ptrs, off = [grad.data_ptr()], [p_slice.data_ptr()], 0
+        b1, b2 = cfg.adam_betas
+        lib().adam(grad_ptrs, param_ptrs, self.rank, off, state["exp_avg"], state["exp_avg_sq"], n, is_f32, b1, b2, cfg.eps,
+                   step_size, eff_wd, grad_mul)
+
+    def transpose_add(self, src: Tensor, dst: Tensor) -> None:
+        if src.dtype == torch.bfloat16 and src.is_contiguous() and dst.is_contiguous():
+            lib().transpose(src, dst, True)
+        else:
+            super().transpose_add(src, dst)
+
+    def transpose_copy(self, src: Tensor, dst: Tensor) -> None:
+        if src.dtype == torch.bfloat16 and src.is_contiguous() and dst.is_contiguous():
+            lib().transpose(src, dst, False)
+        else:
+            super().transpose_copy(src, dst)

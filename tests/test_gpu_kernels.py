@@ -120,7 +120,7 @@ def test_rmsnorm_fwd_bwd_and_quant(fused):
     x = (torch.randn(1000, 768, device="cuda") * 3).to(BF).requires_grad_(True)
     y = fused.rms_norm(x)
     xr = x.detach().float().requires_grad_(True)
-    eps = torch.finfo(BF).eps
+    eps = torch.finfo(torch.float32).eps
     yr = xr * torch.rsqrt(xr.square().mean(-1, keepdim=True) + eps)
     assert _rel(y, yr) < 4e-3
     dy = torch.randn_like(y)
@@ -197,7 +197,7 @@ def test_fused_mlp_matches_reference(fused):
         g = torch.randn_like(out)
         gx, g1, g2 = torch.autograd.grad(out, (x, w1, w2), g)
         xr, w1r, w2r = (t.detach().float().requires_grad_(True) for t in (x, w1, w2))
-        eps = torch.finfo(BF).eps
+        eps = torch.finfo(torch.float32).eps
         yr = xr * torch.rsqrt(xr.square().mean(-1, keepdim=True) + eps)
         outr = ref.relu2_mlp(yr, w1r, w2r)
         gxr, g1r, g2r = torch.autograd.grad(outr, (xr, w1r, w2r), g.float())
