@@ -266,3 +266,61 @@ extern "C" int mng_quant_transpose_e4m3(const void* src, void* q, float* scale, 
   quant_transpose_kernel<<<g2, 256, 0, s>>>((const __nv_bfloat16*)src, (uint8_t*)q, amax_scratch, scale, rows, cols);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
+
+// ---------------------------------------------------------------------------------------------------
+// Allocation-free variant of mng_quant_transpose_e4m3 (see noalloc.h): the column-amax scratch lives
+// in this file-scope device array instead of caller memory.
+#include "noalloc.h"
+
+#include <mutex>
+
+static __device__ __align__(256) unsigned int g_static_amax_scratch[MNG_STATIC_SCRATCH_COLS];
+
+namespace {
+constexpr int kMaxDevices = 64;
+void* g_static_scratch_addr[kMaxDevices] = {};   // device address of the array, per device ordinal
+std::mutex g_static_scratch_mu;
+
+// `g_static_amax_scratch` named in host code is only a host-side handle; the address a kernel can use
+// has to be asked for, once per device, while that device is current.
+int static_scratch_ptr(unsigned int** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return MNG_ERR_SYMBOL;
+  std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+  if (g_static_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_static_amax_scratch) != cudaSuccess || p == nullptr) return MNG_ERR_SYMBOL;
+    g_static_scratch_addr[dev] = p;
+  }
+  *out = static_cast<unsigned int*>(g_static_scratch_addr[dev]);
+  return MNG_OK;
+}
+}  // namespace
+
+extern "C" int mng_quant_transpose_e4m3_static(const void* src, void* q, float* scale, long long rows, long long cols,
+                                               void* stream) {
+  if (rows <= 0 || cols <= 0) return MNG_ERR_BAD_SHAPE;
+  if (cols > MNG_STATIC_SCRATCH_COLS) return MNG_ERR_TOO_LARGE;
+  unsigned int* scratch = nullptr;
+  const int rc = static_scratch_ptr(&scratch);
+  if (rc != MNG_OK) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  // the array still holds the previous call's maxima: clear the words this call will use
+  if (cudaMemsetAsync(scratch, 0, sizeof(unsigned int) * cols, s) != cudaSuccess) return MNG_ERR_LAUNCH;
+  dim3 g1((unsigned)((cols + 63) / 64), (unsigned)((rows + 255) / 256));
+  mng::col_amax_kernel<<<g1, 256, 0, s>>>((const __nv_bfloat16*)src, scratch, rows, cols);
+  dim3 g2((unsigned)((cols + 63) / 64), (unsigned)((rows + 63) / 64));
+  mng::quant_transpose_kernel<<<g2, 256, 0, s>>>((const __nv_bfloat16*)src, (uint8_t*)q, scratch, scale, rows, cols);
+  return cudaGetLastError() == cudaSuccess ? MNG_OK : MNG_ERR_LAUNCH;
+}
+
+extern "C" const char* mng_static_strerror(int code) {
+  switch (code) {
+    case MNG_OK: return "ok";
+    case MNG_ERR_TOO_LARGE: return "cols exceeds MNG_STATIC_SCRATCH_COLS (65536): the built-in scratch array is too small";
+    case MNG_ERR_SYMBOL: return "could not resolve the device address of the built-in scratch array on the current device";
+    case MNG_ERR_BAD_SHAPE: return "rows and cols must be positive";
+    case MNG_ERR_LAUNCH: return "memset or kernel launch failed";
+    default: return "unknown code";
+  }
+}
