@@ -273,6 +273,8 @@ class NorMuonAndAdam:
                 self._pending[label] = self.coll.launch_fused_reduce(label, p.grad, c, self.state[label])
             else:
                 self._launch_reduce(label, p.grad)
+        if fused:
+            self.coll.reduce_barrier()      # all ranks' gradients are final before any peer reads them
 
         # ---- phase 2: updates + gathers ------------------------------------------------
         gathers, lm_gather = [], None
@@ -304,6 +306,8 @@ class NorMuonAndAdam:
                     gathers.append(g)
 
         # ---- phase 3 -------------------------------------------------------------------
+        if fused:
+            self.coll.gather_barrier()      # peer stores of the new weights have landed everywhere
         if lm_gather is not None:
             lm_gather.wait()
         if do_adam and tied:
@@ -314,7 +318,10 @@ class NorMuonAndAdam:
         for label, p in self.params.items():
             if self.cfgs[label].optim == "adam" and not do_adam:
                 continue
-            p.grad = None
+            if fused and p.grad is not None:
+                self.coll.clear_grad(p)     # gradients live in peer-mapped memory: keep the buffer, zero it
+            else:
+                p.grad = None
 
     def adam_scalars(self, label: str):
         """Advance the step count and return (step_size, eff_wd) for this update."""

@@ -1,0 +1,129 @@
+"""Fused collectives over NVLink peer memory.
+
+Every parameter and its gradient live in one symmetric-memory arena (same offsets on every rank,
+peer-mapped through `torch.distributed._symmetric_memory`).  The optimizer kernels then do the
+communication themselves (`csrc/optim.cu`):
+
+* gradient reduce-scatter (NorMuon banks, sharded Adam tables) and all-reduce (replicated Adam
+  parameters): the update kernel reads the shard from every rank's gradient buffer with plain peer
+  loads, sums in fp32 and scales by 1/world - no separate reduction pass, no staging buffer;
+* parameter all-gather: the kernel that computes the new weights stores them into every rank's
+  parameter tensor with peer stores;
+* ordering: one `peer_barrier` kernel (release/acquire flags in the arena's signal pad, bounded
+  spin that reports through the status word) after backward and one after the updates.
+
+This replaces `reduce_scatter_tensor` / `all_reduce` / `all_gather_into_tensor` of
+`train_gpt.py:588-642` for every parameter whose shard is 16-byte aligned; the handful of tiny
+parameters that are not fall back to NCCL through the base class.  Loads and stores are ordinary
+global accesses on peer pointers: no TMA multicast, no library kernel is handed a peer pointer.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from ..ops.native import lib
+from .collectives import TorchCollectives, _Done
+
+PAD_BYTES = 4096
+
+
+def _align(n: int, a: int = 256) -> int:
+    return -(-n // a) * a
+
+
+class NvlinkCollectives(TorchCollectives):
+    fused = True
+
+    def __init__(self, model, env, math):
+        super().__init__()
+        import torch.distributed._symmetric_memory as symm
+        assert self.world_size <= 8
+        self.math = math
+        self.device = env.device
+        layout, off = {}, PAD_BYTES
+        params = [(getattr(p, "label", n), p) for n, p in model.named_parameters()]
+        for label, p in params:
+            nb = p.numel() * p.element_size()
+            layout[label] = (off, off + _align(nb), nb)
+            off += 2 * _align(nb)
+        self.arena = symm.empty(off, dtype=torch.uint8, device=env.device)
+        self.handle = symm.rendezvous(self.arena, dist.group.WORLD.group_name)
+        self.arena.zero_()
+        self.base_ptrs = [int(x) for x in self.handle.buffer_ptrs]
+        assert len(self.base_ptrs) == self.world_size
+        self.offsets = {}
+        for label, p in params:
+            po, go, nb = layout[label]
+            pv = self.arena[po:po + nb].view(p.dtype).view(p.shape)
+            gv = self.arena[go:go + nb].view(p.dtype).view(p.shape)
+            pv.copy_(p.data)
+            p.data = pv
+            p.grad = gv
+            self.offsets[label] = (po, go)
+        self.epoch = 0
+        torch.cuda.synchronize()
+        dist.barrier()
+
+    # ------------------------------------------------------------------------------------------
+    def _ptrs(self, label: str, which: int):
+        off = self.offsets[label][which]
+        return [b + off for b in self.base_ptrs]
+
+    def peer_barrier(self):
+        self.epoch += 1
+        lib().peer_barrier(self.base_ptrs, self.rank, self.epoch, self.arena)
+
+    def handles(self, cfg) -> bool:
+        if cfg.label not in self.offsets:
+            return False
+        if cfg.optim == "normuon":
+            return True
+        po, _ = self.offsets[cfg.label]
+        # shard length in elements must keep 16-byte vectors aligned
+        return cfg.label in self._adam_ok
+
+    def prepare(self, optimizer):
+        """Decide per Adam parameter whether its shard can use the vectorised fused kernel."""
+        self._adam_ok = set()
+        for label, c in optimizer.cfgs.items():
+            if c.optim != "adam" or label not in self.offsets:
+                continue
+            p = optimizer.params[label]
+            vec = 4 if p.dtype == torch.float32 else 8
+            n = p.numel() // self.world_size if c.comms.startswith("sharded") else p.numel()
+            if n % vec == 0 and p.dtype in (torch.float32, torch.bfloat16):
+                self._adam_ok.add(label)
+
+    def clear_grad(self, p):
+        p.grad.zero_()
+
+    # -- called by NorMuonAndAdam.step ---------------------------------------------------------------
+    def launch_fused_reduce(self, label, grad, cfg, state):
+        return (None, None)           # nothing to launch: the update kernel reads the peers directly
+
+    def reduce_barrier(self):
+        self.peer_barrier()           # every rank's backward (and tied-embedding transpose-add) is complete
+
+    def gather_barrier(self):
+        self.peer_barrier()           # every rank's peer stores have landed
+
+    def fused_update_and_gather(self, label, _grad, cfg, state, optimizer, do_adam):
+        W, r = self.world_size, self.rank
+        gptrs, pptrs = self._ptrs(label, 1), self._ptrs(label, 0)
+        p = optimizer.params[label]
+        if cfg.optim == "normuon":
+            per_chunk = p.numel() // W
+            v = self.math.normuon_direction(None, state, cfg, grad_ptrs=gptrs, off=r * per_chunk, grad_mul=1.0 / W)
+            self.math.normuon_apply(None, state, v, cfg, param_ptrs=pptrs, off=r * per_chunk)
+            return None
+        step_size, eff_wd = optimizer.adam_scalars(label)
+        if cfg.comms.startswith("sharded"):
+            n = p.numel() // W
+            shard = p.data.view(-1)[r * n:(r + 1) * n]
+            self.math.adam(shard, None, state, cfg, step_size, eff_wd, grad_ptrs=gptrs, param_ptrs=pptrs, off=r * n,
+                           grad_mul=1.0 / W)
+        else:       # replicated: all ranks read all gradients and apply the same update to their own copy
+            self.math.adam(p.data.view(-1), None, state, cfg, step_size, eff_wd, grad_ptrs=gptrs,
+                           param_ptrs=[pptrs[r]], off=0, grad_mul=1.0 / W)
+        return None

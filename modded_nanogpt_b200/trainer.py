@@ -70,7 +70,10 @@ class TrainingManager:
         dev = next(model.parameters()).device
         self.sparse = None
         self.row_tracker = None
-        if (hasattr(model, "bigram_embed") and env.world_size >= sparse_min_world and env.world_size > 1
+        # with the fused NVLink path every rank reads its bigram shard straight from the peers' dense
+        # gradients, so the host-driven sparse exchange is only used on the NCCL / gloo path
+        if (hasattr(model, "bigram_embed") and not getattr(collectives, "fused", False)
+                and env.world_size >= sparse_min_world and env.world_size > 1
                 and env.grad_accum_steps == 1):
             n = model.bigram_embed.weight.shape[0]
             self.sparse = SparseRowExchange(n, env.rank, env.world_size, dev)
@@ -81,6 +84,8 @@ class TrainingManager:
             normuon_defaults=dict(lr=hp.muon_lr, momentum=hp.muon_momentum, beta2=hp.muon_beta2, weight_decay=hp.muon_wd),
             collectives=collectives or TorchCollectives(), math=math, sparse_exchange=self.sparse,
             rank=env.rank, world_size=env.world_size)
+        if hasattr(self.optimizer.coll, "prepare"):
+            self.optimizer.coll.prepare(self.optimizer)
         self.split_step = schedule.split_step
         self.device = dev
         self.reset()
@@ -290,7 +295,12 @@ class Trainer:
             m.step_optimizers(step)
             self.model.quantize_mlp_fp8(bootstrap_down=True)
         self.log.print0("Resetting Model", console=True)
-        self.model.zero_grad(set_to_none=True)
+        if getattr(m.optimizer.coll, "fused", False):
+            for p in self.model.parameters():       # gradients live in peer-mapped memory: keep the buffers
+                if p.grad is not None:
+                    p.grad.zero_()
+        else:
+            self.model.zero_grad(set_to_none=True)
         self.model.load_state_dict(init["model"])
         m.reset(init["optimizer"])
         self.model.quantize_mlp_fp8(bootstrap_down=True)
