@@ -42,7 +42,16 @@ def parse():
 
 def reference_arm(args):
     from baseline.run_reference import run_reference
-    print(json.dumps(run_reference(args)), flush=True)
+    try:
+        out = run_reference(args)
+    except Exception as e:  # noqa: BLE001 - the reference arm must never take the driver down
+        import traceback
+        traceback.print_exc()
+        out = {"impl": "reference", "unavailable": f"reference run failed: {type(e).__name__}: {str(e)[:300]}"}
+        if int(os.environ.get("RANK", "0")) != 0:
+            out = {}
+    if out:
+        print(json.dumps(out), flush=True)
 
 
 def main():

@@ -279,7 +279,8 @@ class Trainer:
         self.train_loader = self.make_train_loader()
         val_loader = self.make_val_loader()
         trans = m.get_transition_steps()
-        steps = sorted({0, 1} | {s + o for s in trans for o in (-2, -1, 0, 1) if s + o >= 2})
+        last = self.schedule.total_steps - 1
+        steps = sorted({0, min(1, last)} | {s + o for s in trans for o in (-2, -1, 0, 1) if 2 <= s + o <= last})
         self.log.print0(f"Sampling steps {steps} for warmup", console=True)
         for step in steps:
             m.advance_schedule(step)

@@ -57,8 +57,13 @@ def save_checkpoint(trainer, path: str | None = None, compiled_prefix: bool = Tr
     d = path or checkpoint_dir(trainer)
     os.makedirs(d, exist_ok=True)
     m = trainer.manager
+    # Adam parameters are stepped every other step, so after an even step their gradients are still
+    # pending: they are part of the training state
+    pending = {l: p.grad.detach().cpu().clone() for l, p in m.optimizer.params.items()
+               if p.grad is not None and bool(p.grad.ne(0).any())}
     shard = dict(step=step, optimizer=m.optimizer.state_dict(), rank=env.rank, world_size=env.world_size,
-                 loader=trainer.train_loader.state_dict() if trainer.train_loader is not None else None)
+                 loader=trainer.train_loader.state_dict() if trainer.train_loader is not None else None,
+                 pending_grads=pending)
     torch.save(shard, os.path.join(d, f"optim_step{step:06d}_rank{env.rank}.pt"))
     main = os.path.join(d, f"state_step{step:06d}.pt")
     if env.master:
@@ -81,10 +86,10 @@ def save_checkpoint(trainer, path: str | None = None, compiled_prefix: bool = Tr
 def load_checkpoint(trainer, main_path: str) -> int:
     """Restores model, optimizer shard of this rank, loader cursor, rotary and schedule state.
     Returns the step to continue from."""
-    env = trainer.env
     log = torch.load(main_path, map_location="cpu", weights_only=False)
     if not isinstance(log, dict) or "model" not in log or "step" not in log:
         raise ValueError(f"{main_path}: not a checkpoint of this framework or of the reference")
+    env = trainer.env
     step = int(log["step"])
     load_model_state(trainer.model, log["model"])
     m = trainer.manager
@@ -93,6 +98,12 @@ def load_checkpoint(trainer, main_path: str) -> int:
     if os.path.exists(shard_path) and log.get("world_size", env.world_size) == env.world_size:
         shard = torch.load(shard_path, map_location="cpu", weights_only=False)
         m.optimizer.load_state_dict(shard["optimizer"])
+        for l, g in shard.get("pending_grads", {}).items():
+            p = m.optimizer.params[l]
+            if p.grad is None:
+                p.grad = g.to(p.device, p.dtype)
+            else:
+                p.grad.copy_(g)
         if shard.get("loader") is not None:
             if trainer.train_loader is None:
                 trainer.train_loader = trainer.make_train_loader()
