@@ -132,6 +132,10 @@ int mng_dc_mix_fwd(const float* S, const void* w1, const int* doc_start, void* P
 int mng_dc_mix_bwd(const float* dM, const void* P, const void* a, const void* w1, const void* w2, void* dS, float* g_w1,
                    float* g_w2, long long T, int H, float scale, void* stream);
 
+// ---- embedding backward (embed.cu): grad[sorted_ids[j], :] += g[perm[j], :], accumulated in place (bf16) ----
+int mng_embed_bwd(const void* g, const long long* sorted_ids, const long long* perm, void* grad, long long n, int D,
+                  void* stream);
+
 // Barrier across ranks on signal pads (bounded wait; sets *status on expiry).
 int mng_peer_barrier(const PeerPtrs* pads, int rank, uint32_t epoch, uint32_t* status, void* stream);
 

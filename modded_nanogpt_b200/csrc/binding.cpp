@@ -448,6 +448,20 @@ std::vector<Tensor> dc_mix_bwd(const Tensor& dM, const Tensor& P, const Tensor& 
   return {dS, g1, g2};
 }
 
+// grad[sorted_ids[j], :] += g[perm[j], :]   (grad: bf16 [V, D] updated in place)
+void embed_bwd(const Tensor& g, const Tensor& sorted_ids, const Tensor& perm, Tensor& grad) {
+  TORCH_CHECK(g.dim() == 2 && g.is_contiguous() && g.scalar_type() == torch::kBFloat16);
+  TORCH_CHECK(grad.dim() == 2 && grad.is_contiguous() && grad.scalar_type() == torch::kBFloat16 && grad.size(1) == g.size(1));
+  TORCH_CHECK(sorted_ids.scalar_type() == torch::kInt64 && perm.scalar_type() == torch::kInt64 && sorted_ids.is_contiguous() &&
+              perm.is_contiguous() && sorted_ids.numel() == g.size(0) && perm.numel() == g.size(0));
+  c10::cuda::CUDAGuard guard(g.device());
+  check(mng_embed_bwd(g.data_ptr(), reinterpret_cast<const long long*>(sorted_ids.data_ptr<int64_t>()),
+                      reinterpret_cast<const long long*>(perm.data_ptr<int64_t>()), grad.data_ptr(), g.size(0), (int)g.size(1),
+                      cur_stream()),
+        "mng_embed_bwd");
+  g_launches += 1;
+}
+
 Tensor status_tensor(const Tensor& like) {
   status_ptr(like);
   return g_status;
@@ -474,6 +488,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qkv_post_bwd", &qkv_post_bwd);
   m.def("xsa_gate_fwd", &xsa_gate_fwd);
   m.def("xsa_gate_bwd", &xsa_gate_bwd);
+  m.def("embed_bwd", &embed_bwd);
   m.def("dc_mix_fwd", &dc_mix_fwd);
   m.def("dc_mix_bwd", &dc_mix_bwd);
   m.def("status_tensor", &status_tensor);

@@ -13,7 +13,6 @@
 
 namespace mng {
 
-constexpr int CE_THREADS = 256;
 constexpr int CE_MAX_PREDICT = 8;
 
 __device__ __forceinline__ float fast_sigmoid(float u) {
@@ -22,15 +21,19 @@ __device__ __forceinline__ float fast_sigmoid(float u) {
   return 0.5f + 0.5f * t;
 }
 
-template <bool OUT_E5M2>
-__global__ void __launch_bounds__(CE_THREADS, 2)
+// CACHE_E: also park exp(z - A) (bf16) next to the sigmoids so the gradient sweep needs no second
+// exponential: 2 instead of 3 special-function evaluations per logit, which is what bounds this kernel
+// once the logits stream at HBM speed.  Needs 4*vocab bytes of shared memory (one 1024-thread CTA per SM).
+template <bool OUT_E5M2, bool CACHE_E, int CE_THREADS>
+__global__ void __launch_bounds__(CE_THREADS, CACHE_E ? 1 : 2)
 softcap_ce_kernel(const __nv_bfloat16* __restrict__ logits, const long long* __restrict__ targets,
                   const float* __restrict__ mtp_weights, int n_predict, const long long* __restrict__ prefix_targets,
                   const float* __restrict__ prefix_weight_ptr, float* __restrict__ losses, void* __restrict__ dlogits,
                   long long rows, int vocab, long long ld, float A, float B, float C, float grad_mul) {
   extern __shared__ __nv_bfloat16 sig[];
+  __nv_bfloat16* ex = sig + vocab;                 // only touched when CACHE_E
   __shared__ float red[CE_THREADS / 32];
-  __shared__ float s_lse;
+  __shared__ float s_lse, s_inv;
   const long long row = blockIdx.x;
   const __nv_bfloat16* lrow = logits + row * ld;
   const float inv_c = 1.f / C, b_over_c = B / C;
@@ -40,17 +43,21 @@ softcap_ce_kernel(const __nv_bfloat16* __restrict__ logits, const long long* __r
   for (int i = threadIdx.x; i < nvec; i += CE_THREADS) {
     uint4 u = *reinterpret_cast<const uint4*>(lrow + i * 8);
     const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-    uint4 w;
+    uint4 w, we;
     uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+    uint32_t* ep = reinterpret_cast<uint32_t*>(&we);
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
       float2 f = __bfloat1622float2(h[t]);
       __nv_bfloat162 s2 = __floats2bfloat162_rn(fast_sigmoid(f.x * inv_c + b_over_c), fast_sigmoid(f.y * inv_c + b_over_c));
       wp[t] = *reinterpret_cast<uint32_t*>(&s2);
       float2 s = __bfloat1622float2(s2);
-      part += __expf(A * s.x - A) + __expf(A * s.y - A);
+      const float e0 = __expf(A * s.x - A), e1 = __expf(A * s.y - A);
+      part += e0 + e1;
+      if constexpr (CACHE_E) ep[t] = pack_bf16x2(e0, e1);
     }
     *reinterpret_cast<uint4*>(sig + i * 8) = w;
+    if constexpr (CACHE_E) *reinterpret_cast<uint4*>(ex + i * 8) = we;
   }
   part = warp_sum(part);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = part;
@@ -60,9 +67,10 @@ softcap_ce_kernel(const __nv_bfloat16* __restrict__ logits, const long long* __r
 #pragma unroll
     for (int i = 0; i < CE_THREADS / 32; ++i) tot += red[i];
     s_lse = A + __logf(tot);
+    s_inv = 1.f / tot;
   }
   __syncthreads();
-  const float lse = s_lse;
+  const float lse = s_lse, inv_tot = s_inv;
 
   const float prefix_weight = prefix_weight_ptr ? prefix_weight_ptr[0] : 0.f;
   const long long ptgt = prefix_targets ? prefix_targets[row] : -1;
@@ -88,11 +96,23 @@ softcap_ce_kernel(const __nv_bfloat16* __restrict__ logits, const long long* __r
     uint4 u = *reinterpret_cast<const uint4*>(sig + i * 8);
     const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
     float g[8];
+    if constexpr (CACHE_E) {
+      uint4 ue = *reinterpret_cast<const uint4*>(ex + i * 8);
+      const __nv_bfloat162* he = reinterpret_cast<const __nv_bfloat162*>(&ue);
+      const float c = gscale * S_w * inv_tot;
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      float2 s = __bfloat1622float2(h[t]);
-      g[2 * t] = gscale * S_w * __expf(A * s.x - lse) * s.x * (1.f - s.x);
-      g[2 * t + 1] = gscale * S_w * __expf(A * s.y - lse) * s.y * (1.f - s.y);
+      for (int t = 0; t < 4; ++t) {
+        float2 s = __bfloat1622float2(h[t]), e = __bfloat1622float2(he[t]);
+        g[2 * t] = c * e.x * s.x * (1.f - s.x);
+        g[2 * t + 1] = c * e.y * s.y * (1.f - s.y);
+      }
+    } else {
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        float2 s = __bfloat1622float2(h[t]);
+        g[2 * t] = gscale * S_w * __expf(A * s.x - lse) * s.x * (1.f - s.x);
+        g[2 * t + 1] = gscale * S_w * __expf(A * s.y - lse) * s.y * (1.f - s.y);
+      }
     }
     if constexpr (OUT_E5M2) {
       uint2 w;
@@ -146,21 +166,26 @@ extern "C" int mng_softcap_ce(const void* logits, const long long* targets, cons
                               float grad_mul, void* stream) {
   if (rows == 0) return 0;
   if (vocab % 8 || ld % 8 || n_predict > CE_MAX_PREDICT || n_predict < 1) return -1;
-  const size_t smem = (size_t)vocab * 2;
-  if (smem > 200 * 1024) return -2;
-  cudaError_t e;
+  const size_t smem1 = (size_t)vocab * 2, smem2 = (size_t)vocab * 4;
+  const bool cache = smem2 <= 220 * 1024;
+  if (!cache && smem1 > 200 * 1024) return -2;
+  cudaStream_t st = (cudaStream_t)stream;
+#define CE_LAUNCH(E5, CACHE, TH, SMEM)                                                                              \
+  do {                                                                                                              \
+    static bool set = false;                                                                                        \
+    auto kern = softcap_ce_kernel<E5, CACHE, TH>;                                                                   \
+    if (!set) {                                                                                                     \
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024) != cudaSuccess) return -3; \
+      set = true;                                                                                                   \
+    }                                                                                                               \
+    kern<<<(unsigned)rows, TH, SMEM, st>>>((const __nv_bfloat16*)logits, targets, mtp_weights, n_predict, prefix_targets, \
+                                           prefix_weight, losses, dlogits, rows, vocab, ld, A, B, C, grad_mul);       \
+  } while (0)
   if (dlogits_is_e5m2) {
-    static bool set = false;
-    if (!set) { e = cudaFuncSetAttribute(softcap_ce_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); if (e) return -3; set = true; }
-    softcap_ce_kernel<true><<<(unsigned)rows, CE_THREADS, smem, (cudaStream_t)stream>>>(
-        (const __nv_bfloat16*)logits, targets, mtp_weights, n_predict, prefix_targets, prefix_weight, losses, dlogits, rows, vocab,
-        ld, A, B, C, grad_mul);
+    if (cache) CE_LAUNCH(true, true, 1024, smem2); else CE_LAUNCH(true, false, 256, smem1);
   } else {
-    static bool set = false;
-    if (!set) { e = cudaFuncSetAttribute(softcap_ce_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); if (e) return -3; set = true; }
-    softcap_ce_kernel<false><<<(unsigned)rows, CE_THREADS, smem, (cudaStream_t)stream>>>(
-        (const __nv_bfloat16*)logits, targets, mtp_weights, n_predict, prefix_targets, prefix_weight, losses, dlogits, rows, vocab,
-        ld, A, B, C, grad_mul);
+    if (cache) CE_LAUNCH(false, true, 1024, smem2); else CE_LAUNCH(false, false, 256, smem1);
   }
+#undef CE_LAUNCH
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }

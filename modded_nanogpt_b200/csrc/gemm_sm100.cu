@@ -11,6 +11,23 @@
 namespace mng {
 
 // ================================== epilogues =====================================================
+// Each functor turns a 32-column fp32 fragment (one row per lane) into output bytes, staged through the
+// warp's ChunkIO buffer so that global loads and stores are coalesced.  A chunk whose columns are not
+// all inside N (only possible when N % 32 != 0) takes the element-wise slow path.
+
+__device__ __forceinline__ uint4 pack_bf16x8(const float* v) {
+  uint4 w;
+  w.x = pack_bf16x2(v[0], v[1]); w.y = pack_bf16x2(v[2], v[3]); w.z = pack_bf16x2(v[4], v[5]); w.w = pack_bf16x2(v[6], v[7]);
+  return w;
+}
+__device__ __forceinline__ void unpack_bf16x8(uint4 c, float* f) {
+  const __nv_bfloat162* c2 = reinterpret_cast<const __nv_bfloat162*>(&c);
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    float2 x = __bfloat1622float2(c2[t]);
+    f[2 * t] = x.x; f[2 * t + 1] = x.y;
+  }
+}
 
 // out = alpha * acc * row_scale[m] * col_scale[n] + beta * Cin[m,n]   (bf16 or fp32 output)
 template <bool OUT_F32>
@@ -26,11 +43,15 @@ struct EpiStore {
   };
   struct State {};
   __device__ static void finish(const Params&, State&) {}
-  __device__ static void apply(const Params& p, State&, const float (&acc)[32], int b, int row, int col0, int M, int N) {
-    if (row >= M) return;
+  __device__ static void apply(const Params& p, State&, ChunkIO& io, const float (&acc)[32], int b, long long row0, int col0,
+                               int M, int N) {
+    constexpr int ESZ = OUT_F32 ? 4 : 2;
+    constexpr int B = 32 * ESZ;
+    const long long row = row0 + io.lane;
+    const bool live = row < M;
     float a = p.alpha;
     if (p.alpha_ptr) a *= *p.alpha_ptr;
-    if (p.row_scale) a *= p.row_scale[(long long)b * M + row];
+    if (p.row_scale && live) a *= p.row_scale[(long long)b * M + row];
     float v[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = acc[j] * a;
@@ -39,58 +60,45 @@ struct EpiStore {
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] *= (col0 + j < N) ? cs[j] : 0.f;
     }
-    const long long off = (long long)b * p.bstride + (long long)row * p.ld + col0;
-    const bool full = (col0 + 32 <= N);
-    if constexpr (OUT_F32) {
-      float* o = reinterpret_cast<float*>(p.out) + off;
+    const long long base = (long long)b * p.bstride;                       // elements
+    if (col0 + 32 <= N) {
+      uint8_t* outb = reinterpret_cast<uint8_t*>(p.out) + base * ESZ;
       if (p.beta != 0.f) {
-        const float* ci = reinterpret_cast<const float*>(p.cin) + off;
-        if (full) {
+        io.load_rows<B>(reinterpret_cast<const uint8_t*>(p.cin) + base * ESZ, p.ld * ESZ, row0, (long long)col0 * ESZ, M);
 #pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            float4 c = *reinterpret_cast<const float4*>(ci + j);
-            v[j] += p.beta * c.x; v[j + 1] += p.beta * c.y; v[j + 2] += p.beta * c.z; v[j + 3] += p.beta * c.w;
+        for (int j = 0; j < B / 16; ++j) {
+          uint4 c = io.get<B>(j);
+          if constexpr (OUT_F32) {
+            const float* f = reinterpret_cast<const float*>(&c);
+#pragma unroll
+            for (int t = 0; t < 4; ++t) v[4 * j + t] += p.beta * f[t];
+          } else {
+            float f[8];
+            unpack_bf16x8(c, f);
+#pragma unroll
+            for (int t = 0; t < 8; ++t) v[8 * j + t] += p.beta * f[t];
           }
+        }
+        __syncwarp();
+      }
+#pragma unroll
+      for (int j = 0; j < B / 16; ++j) {
+        if constexpr (OUT_F32) io.put<B>(j, make_uint4(__float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]),
+                                                       __float_as_uint(v[4 * j + 2]), __float_as_uint(v[4 * j + 3])));
+        else io.put<B>(j, pack_bf16x8(v + 8 * j));
+      }
+      io.store_rows<B>(outb, p.ld * ESZ, row0, (long long)col0 * ESZ, M);
+    } else if (live) {                                                     // ragged last chunk
+      const long long off = base + row * p.ld + col0;
+      for (int j = 0; j < 32; ++j) {
+        if (col0 + j >= N) break;
+        if constexpr (OUT_F32) {
+          float* o = reinterpret_cast<float*>(p.out) + off;
+          o[j] = v[j] + (p.beta != 0.f ? p.beta * (reinterpret_cast<const float*>(p.cin) + off)[j] : 0.f);
         } else {
-          for (int j = 0; j < 32; ++j) if (col0 + j < N) v[j] += p.beta * ci[j];
+          __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + off;
+          o[j] = __float2bfloat16(v[j] + (p.beta != 0.f ? p.beta * __bfloat162float((reinterpret_cast<const __nv_bfloat16*>(p.cin) + off)[j]) : 0.f));
         }
-      }
-      if (full) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-      } else {
-        for (int j = 0; j < 32; ++j) if (col0 + j < N) o[j] = v[j];
-      }
-    } else {
-      __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + off;
-      if (p.beta != 0.f) {
-        const __nv_bfloat16* ci = reinterpret_cast<const __nv_bfloat16*>(p.cin) + off;
-        if (full) {
-#pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            uint4 c = *reinterpret_cast<const uint4*>(ci + j);
-            const __nv_bfloat162* c2 = reinterpret_cast<const __nv_bfloat162*>(&c);
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              float2 f = __bfloat1622float2(c2[t]);
-              v[j + 2 * t] += p.beta * f.x;
-              v[j + 2 * t + 1] += p.beta * f.y;
-            }
-          }
-        } else {
-          for (int j = 0; j < 32; ++j) if (col0 + j < N) v[j] += p.beta * __bfloat162float(ci[j]);
-        }
-      }
-      if (full) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 8) {
-          uint4 w;
-          w.x = pack_bf16x2(v[j], v[j + 1]); w.y = pack_bf16x2(v[j + 2], v[j + 3]);
-          w.z = pack_bf16x2(v[j + 4], v[j + 5]); w.w = pack_bf16x2(v[j + 6], v[j + 7]);
-          *reinterpret_cast<uint4*>(o + j) = w;
-        }
-      } else {
-        for (int j = 0; j < 32; ++j) if (col0 + j < N) o[j] = __float2bfloat16(v[j]);
       }
     }
   }
@@ -98,6 +106,7 @@ struct EpiStore {
 
 // MLP up projection: pre = acc * row_scale[m] * col_scale[n] rounded to bf16; post = relu(pre)^2 in
 // bf16 (store); e4m3 copy min(post / act_scale, 448) (store); running max of post -> amax (atomic).
+// N is a multiple of 32 for this epilogue (checked on the host).
 struct EpiRelu2 {
   struct Params {
     __nv_bfloat16* post;
@@ -114,12 +123,11 @@ struct EpiRelu2 {
     const float m = warp_max(st.mx);
     if (p.post8 && (threadIdx.x & 31) == 0 && m > 0.f) atomicMax(p.amax_bits, __float_as_uint(m));
   }
-  __device__ static void apply(const Params& p, State& st, const float (&acc)[32], int b, int row, int col0, int M, int N) {
-    // N is a multiple of 32 for this epilogue (checked on the host).  Rows past M stay in the warp
-    // (the amax reduction below is a warp collective) with their stores predicated off.
+  __device__ static void apply(const Params& p, State& st, ChunkIO& io, const float (&acc)[32], int b, long long row0,
+                               int col0, int M, int N) {
+    const long long row = row0 + io.lane;
     const bool live = row < M;
-    if (!live) row = M - 1;
-    const float rs = p.row_scale ? p.row_scale[row] : 1.f;
+    const float rs = (p.row_scale && live) ? p.row_scale[row] : 1.f;
     float post[32];
     float mx = 0.f;
 #pragma unroll
@@ -131,30 +139,25 @@ struct EpiRelu2 {
       post[j] = q;
       mx = fmaxf(mx, q);
     }
-    if (!live) mx = 0.f;
-    __nv_bfloat16* o = p.post + (long long)row * p.ld + col0;
 #pragma unroll
-    for (int j = 0; live && j < 32; j += 8) {
-      uint4 w;
-      w.x = pack_bf16x2(post[j], post[j + 1]); w.y = pack_bf16x2(post[j + 2], post[j + 3]);
-      w.z = pack_bf16x2(post[j + 4], post[j + 5]); w.w = pack_bf16x2(post[j + 6], post[j + 7]);
-      *reinterpret_cast<uint4*>(o + j) = w;
-    }
+    for (int j = 0; j < 4; ++j) io.put<64>(j, pack_bf16x8(post + 8 * j));
+    io.store_rows<64>(p.post, p.ld * 2, row0, (long long)col0 * 2, M);
     if (p.post8) {
       const float inv = 1.f / *p.act_scale;
-      uint8_t* o8 = p.post8 + (long long)row * p.ld + col0;
 #pragma unroll
-      for (int j = 0; live && j < 32; j += 16) {
+      for (int j = 0; j < 2; ++j) {
         uint32_t w[4];
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
-          uint32_t lo = pack_e4m3x2(post[j + 4 * t] * inv, post[j + 4 * t + 1] * inv);
-          uint32_t hi = pack_e4m3x2(post[j + 4 * t + 2] * inv, post[j + 4 * t + 3] * inv);
+          const float* s = post + 16 * j + 4 * t;
+          uint32_t lo = pack_e4m3x2(s[0] * inv, s[1] * inv);
+          uint32_t hi = pack_e4m3x2(s[2] * inv, s[3] * inv);
           w[t] = lo | (hi << 16);
         }
-        *reinterpret_cast<uint4*>(o8 + j) = make_uint4(w[0], w[1], w[2], w[3]);
+        io.put<32>(j, make_uint4(w[0], w[1], w[2], w[3]));
       }
-      st.mx = fmaxf(st.mx, mx);
+      io.store_rows<32>(p.post8, p.ld, row0, col0, M);
+      if (live) st.mx = fmaxf(st.mx, mx);
     }
   }
 };
@@ -168,25 +171,21 @@ struct EpiDpre {
   };
   struct State {};
   __device__ static void finish(const Params&, State&) {}
-  __device__ static void apply(const Params& p, State&, const float (&acc)[32], int b, int row, int col0, int M, int N) {
-    if (row >= M) return;
-    const long long off = (long long)row * p.ld + col0;
+  __device__ static void apply(const Params& p, State&, ChunkIO& io, const float (&acc)[32], int b, long long row0, int col0,
+                               int M, int N) {
+    io.load_rows<64>(p.post, p.ld * 2, row0, (long long)col0 * 2, M);
+    float o[32];
 #pragma unroll
-    for (int j = 0; j < 32; j += 8) {
-      uint4 c = *reinterpret_cast<const uint4*>(p.post + off + j);
-      const __nv_bfloat162* c2 = reinterpret_cast<const __nv_bfloat162*>(&c);
-      float o[8];
+    for (int j = 0; j < 4; ++j) {
+      float f[8];
+      unpack_bf16x8(io.get<64>(j), f);
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        float2 f = __bfloat1622float2(c2[t]);
-        o[2 * t] = 2.f * __bfloat162float(__float2bfloat16(acc[j + 2 * t])) * sqrtf(f.x);
-        o[2 * t + 1] = 2.f * __bfloat162float(__float2bfloat16(acc[j + 2 * t + 1])) * sqrtf(f.y);
-      }
-      uint4 w;
-      w.x = pack_bf16x2(o[0], o[1]); w.y = pack_bf16x2(o[2], o[3]);
-      w.z = pack_bf16x2(o[4], o[5]); w.w = pack_bf16x2(o[6], o[7]);
-      *reinterpret_cast<uint4*>(p.out + off + j) = w;
+      for (int t = 0; t < 8; ++t) o[8 * j + t] = 2.f * __bfloat162float(__float2bfloat16(acc[8 * j + t])) * sqrtf(f[t]);
     }
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 4; ++j) io.put<64>(j, pack_bf16x8(o + 8 * j));
+    io.store_rows<64>(p.out, p.ld * 2, row0, (long long)col0 * 2, M);
   }
 };
 

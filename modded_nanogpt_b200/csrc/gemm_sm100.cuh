@@ -32,16 +32,71 @@ struct GemmSmem {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (BN == 256) ? 4 : 6;
   static constexpr int BAR_BYTES = 1024;
-  static constexpr int TOTAL = STAGES * STAGE_BYTES + BAR_BYTES + 1024;   // + alignment slack
+  static constexpr int STG_BYTES = 4096;                                  // epilogue staging per warp
+  static constexpr int TOTAL = STAGES * STAGE_BYTES + BAR_BYTES + 8 * STG_BYTES + 1024;   // + alignment slack
+};
+
+// Per-warp staging buffer that turns the "one thread = one row" fragments of tcgen05.ld into
+// coalesced global traffic.  A warp holds 32 rows x B bytes (B = 32, 64 or 128: 32 columns of 1-, 2-
+// or 4-byte elements) as 16-byte chunks with an XOR swizzle that keeps both access patterns free of
+// bank conflicts: thread r writes/reads its own row; then B/16 adjacent lanes cover one row, so a warp
+// store instruction writes 512 contiguous-per-row bytes (full 32-byte sectors) instead of 32 scattered
+// 16-byte pieces.  All methods are warp collectives (every lane must call them).
+struct ChunkIO {
+  uint8_t* stg;      // 4 KB of shared memory owned by this warp
+  int lane;
+  template <int B>
+  __device__ __forceinline__ static int swz(int j, int row) {
+    if constexpr (B == 128) return j ^ (row & 7);
+    else if constexpr (B == 64) return j ^ ((row >> 1) & 3);
+    else return j ^ ((row >> 2) & 1);
+  }
+  template <int B>
+  __device__ __forceinline__ void put(int j, uint4 v) {                 // chunk j of this lane's row
+    *reinterpret_cast<uint4*>(stg + lane * B + swz<B>(j, lane) * 16) = v;
+  }
+  template <int B>
+  __device__ __forceinline__ uint4 get(int j) const {
+    return *reinterpret_cast<const uint4*>(stg + lane * B + swz<B>(j, lane) * 16);
+  }
+  // rows [row0, row0+32) x bytes [col_byte0, col_byte0+B) of a row-major array with row pitch ld_bytes
+  template <int B>
+  __device__ __forceinline__ void store_rows(void* gbase, long long ld_bytes, long long row0, long long col_byte0, int M) {
+    constexpr int LPR = B / 16, RPI = 32 / LPR;
+    __syncwarp();
+#pragma unroll
+    for (int it = 0; it < 32 / RPI; ++it) {
+      const int row = it * RPI + lane / LPR, j = lane % LPR;
+      const uint4 v = *reinterpret_cast<const uint4*>(stg + row * B + swz<B>(j, row) * 16);
+      if (row0 + row < M)
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(gbase) + (row0 + row) * ld_bytes + col_byte0 + j * 16) = v;
+    }
+    __syncwarp();
+  }
+  template <int B>
+  __device__ __forceinline__ void load_rows(const void* gbase, long long ld_bytes, long long row0, long long col_byte0, int M) {
+    constexpr int LPR = B / 16, RPI = 32 / LPR;
+    __syncwarp();
+#pragma unroll
+    for (int it = 0; it < 32 / RPI; ++it) {
+      const int row = it * RPI + lane / LPR, j = lane % LPR;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (row0 + row < M)
+        v = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(gbase) + (row0 + row) * ld_bytes + col_byte0 + j * 16);
+      *reinterpret_cast<uint4*>(stg + row * B + swz<B>(j, row) * 16) = v;
+    }
+    __syncwarp();
+  }
 };
 
 // Epilogue contract:
 //   struct Epi { struct Params {...}; struct State {...};
-//     __device__ static void apply(const Params&, State&, const float (&acc)[32], int batch, int row, int col0,
-//                                  int M, int N);
+//     __device__ static void apply(const Params&, State&, ChunkIO&, const float (&acc)[32], int batch,
+//                                  long long row0, int col0, int M, int N);
 //     __device__ static void finish(const Params&, State&);   // once per epilogue thread, after its last tile
 //   }
-// `acc[j]` is element (row, col0 + j) of the tile product; rows/cols beyond M/N must be skipped.
+// `acc[j]` is element (row0 + lane, col0 + j) of the tile product.  `apply` is called by all 32 lanes of
+// the warp (it uses warp-collective staging); rows/cols beyond M/N must not be written.
 
 template <int BN, int ES, bool A_MN, bool B_MN, uint32_t A_FMT, uint32_t B_FMT, class Epi>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
@@ -185,6 +240,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_cons
     int acc = 0;
     uint32_t acc_phase = 0;
     typename Epi::State est{};                         // per-thread state carried across tiles (e.g. a running max)
+    ChunkIO io{bars + SM::BAR_BYTES + (warp - 2) * SM::STG_BYTES, lane};
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int b = tile / (tiles_m * tiles_n);
       const int r = tile - b * tiles_m * tiles_n;
@@ -195,7 +251,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_cons
         break;
       }
       tc_fence_after();
-      const int row = m0 + q * 32 + lane;
+      const long long row0 = m0 + q * 32;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
 #pragma unroll 1
       for (int c = c_begin; c < c_begin + BN / 64; ++c) {
@@ -205,7 +261,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_cons
         float f[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
-        if (n0 + c * 32 < shape.N) Epi::apply(ep, est, f, b, row, n0 + c * 32, shape.M, shape.N);
+        if (n0 + c * 32 < shape.N) Epi::apply(ep, est, io, f, b, row0, n0 + c * 32, shape.M, shape.N);
       }
       tc_fence_before();
       __syncwarp();

@@ -10,7 +10,7 @@ from torch import Tensor
 
 from ..ops import functional as ops
 from ..ops import fused
-from ..ops.glue import Term, lincomb, qkv_post, xsa_gate
+from ..ops.glue import Term, embed_direct, lincomb, qkv_post, xsa_gate
 
 
 def fused_supported(model, x: Tensor) -> bool:
@@ -44,21 +44,35 @@ def forward_fused(m, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, big
     smear_lambda, skip_lambda = m.scalars[2 * L], m.scalars[2 * L + 1]
     qk_all, vo_all = m.attn_layer_weights()
     resid, post = m.resid_lambdas, m.post_lambdas
+    # Training: the weight-gradient GEMMs accumulate straight into slices of the bank gradients (no
+    # per-layer select/stack of full-bank tensors), so the bank gradients must exist up front.
+    direct = m.training and torch.is_grad_enabled()
+    qk_g = vo_g = None
+    if direct:
+        tables = [m.embed.weight] + ([m.value_embeds] if cfg.num_value_embeds else []) + (
+            [m.bigram_embed.weight] if cfg.bigram_vocab_size else [])
+        for p in (m.qk_bank, m.vo_bank, m.mlp_bank, *tables):
+            if p.grad is None:
+                p.grad = torch.zeros_like(p)
+        A = m._num_attn_layers
+        qk_g = m.qk_bank.grad[:m._num_qk_groups].view(A, 2 * D, D)
+        vo_g = m.vo_bank.grad[:2 * A].view(A, 2 * D, D)
 
     ids = input_seq.long()
-    x = F.embedding(ids, m.embed.weight)
+    gather = (lambda i, w: embed_direct(i, w, w.grad)) if direct else F.embedding
+    x = gather(ids, m.embed.weight)
     x0_bigram = None
     if cfg.bigram_vocab_size:
         sign_idx = torch.zeros_like(ids)
         sign_idx[1:] = (ids[:-1] ^ ids[1:]) % m.bigram_sign_table.shape[0]
-        x0_bigram = F.embedding(bigram_input_seq.long(), m.bigram_embed.weight) * m.bigram_sign_table[sign_idx]
+        x0_bigram = gather(bigram_input_seq.long(), m.bigram_embed.weight) * m.bigram_sign_table[sign_idx]
     ve = None
     if cfg.num_value_embeds:
         # one gather over the flat table (ids offset per table): a single embedding backward into one
         # [n*V, D] gradient instead of n full-size zero-filled select_backward tensors
         n = cfg.num_value_embeds
         offs = torch.arange(n, device=ids.device)[:, None] * V
-        ve = F.embedding((ids[None, :] + offs).reshape(-1), m.value_embeds).view(n, T, D).unbind(0)
+        ve = gather((ids[None, :] + offs).reshape(-1), m.value_embeds).view(n, T, D).unbind(0)
 
     # smear: x[t] += smear_lambda * sigmoid(W x[t, :12]) * x[t-1]
     g = torch.zeros(T, 1, dtype=x.dtype, device=x.device)
@@ -91,7 +105,7 @@ def forward_fused(m, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, big
             sk = torch.sigmoid(skip_lambda).reshape(1)
             x = lincomb([Term(x), Term(cache[3], scalar=sk, gate=pg, col=lay1["skip"])])
         else:
-            w_qkvo = torch.cat([qk_all[pl.attn_slot], vo_all[pl.attn_slot]], dim=0)
+            sl = pl.attn_slot
             if track1 and 7 in cache:
                 if normed7 is None:
                     normed7 = fused.rms_norm(cache[7])
@@ -110,7 +124,10 @@ def forward_fused(m, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, big
                 ve_t = ve[pl.ve_slot]
                 gate_in = torch.cat([attn_in[:, :6], ve_t[:, :6]], dim=-1)
                 vgate = (2 * torch.sigmoid(F.linear(gate_in, m.ve_gate_bank[pl.ve_slot]))).contiguous()
-            qkv = F.linear(attn_in, sa_lambdas[i, 0] * w_qkvo[:3 * D])
+            if direct:
+                qkv = fused.bank_linear(attn_in, sa_lambdas[i, 0], [qk_all[sl], vo_all[sl][:D]], [qk_g[sl], vo_g[sl][:D]])
+            else:
+                qkv = F.linear(attn_in, sa_lambdas[i, 0] * torch.cat([qk_all[sl], vo_all[sl][:D]], dim=0))
             yarn = m.yarn_paired_head if pl.paired else m.yarn
             ct, st = (cos_p, sin_p) if pl.paired else (cos_t, sin_t)
             q, k, v = qkv_post(qkv, ct, st, ve_t, vgate, vadd, H, pl.paired, pl.long_window and not pl.paired)
@@ -129,7 +146,10 @@ def forward_fused(m, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, big
                 alpha = gt[:, lay["xsa"][i]:lay["xsa"][i] + H] if (pl.xsa and not pl.paired) else None
                 agate = gt[:, lay["attn"][i]:lay["attn"][i] + H] if pl.attn_gate else None
                 y = xsa_gate(y, v, alpha, agate)
-            attn_out = F.linear(y.reshape(T, D), sa_lambdas[i, 1] * w_qkvo[3 * D:])
+            if direct:
+                attn_out = fused.bank_linear(y.reshape(T, D), sa_lambdas[i, 1], [vo_all[sl][D:]], [vo_g[sl][D:]])
+            else:
+                attn_out = F.linear(y.reshape(T, D), sa_lambdas[i, 1] * vo_all[sl][D:])
             if mu is not None:
                 x = lincomb([Term(x, gate=mu, col=8), Term(attn_out, gate=mu, col=9), Term(cache[0], gate=mu, col=10),
                              Term(x0_bigram, gate=mu, col=11)])
@@ -142,7 +162,11 @@ def forward_fused(m, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, big
             else:
                 x = lincomb([Term(x, scalar=resid[i, 0]), Term(attn_out, scalar=post[i, 0])])
 
-        h = m._mlp(i, x, training_fp8)
+        if direct:
+            st = m._fp8_state.layer(i) if (training_fp8 and m._fp8_state is not None) else None
+            h = fused.norm_relu2_mlp(x, m.mlp_bank[i, 0], m.mlp_bank[i, 1], st, (m.mlp_bank.grad[i, 0], m.mlp_bank.grad[i, 1]))
+        else:
+            h = m._mlp(i, x, training_fp8)
         if mu is not None:
             x = lincomb([Term(x, gate=mu, col=12), Term(h, gate=mu, col=13)])
         else:

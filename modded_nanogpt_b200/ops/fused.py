@@ -138,9 +138,10 @@ class _NormRelu2Mlp(torch.autograd.Function):
     """out = relu(norm(x) @ W1^T)^2 @ W2 with W1, W2 stored (hidden, dim)."""
 
     @staticmethod
-    def forward(ctx, x, w_fc, w_proj, fp8):
+    def forward(ctx, x, w_fc, w_proj, fp8, g_fc=None, g_proj=None):
         C = _C()
         T, D = x.shape
+        ctx.grad_views = (g_fc, g_proj)
         hid = w_fc.shape[0]
         xc = x.contiguous()
         post = torch.empty(T, hid, dtype=torch.bfloat16, device=x.device)
@@ -163,16 +164,57 @@ class _NormRelu2Mlp(torch.autograd.Function):
         C = _C()
         x, rstd, y, post, w_fc, w_proj = ctx.saved_tensors
         g = g.contiguous()
-        d_proj = gemm(post, g, a_mn=True, b_mn=True)                         # post^T g         (hid, dim)
+        g_fc, g_proj = ctx.grad_views
+        # weight gradients: either returned to autograd, or accumulated by the GEMM epilogue (beta = 1)
+        # straight into the caller's slices of the parameter-bank gradient
+        acc = dict(beta=1.0) if g_fc is not None else {}
+        d_proj = gemm(post, g, a_mn=True, b_mn=True, out=g_proj, cin=g_proj, **acc)      # post^T g      (hid, dim)
         dpre = gemm(g, w_proj, epilogue=EPI_DPRE, cin=post)                  # 2 (g W2^T) sqrt(post)
-        d_fc = gemm(dpre, y, a_mn=True, b_mn=True)                           # dpre^T y         (hid, dim)
+        d_fc = gemm(dpre, y, a_mn=True, b_mn=True, out=g_fc, cin=g_fc, **acc)            # dpre^T y      (hid, dim)
         dy = gemm(dpre, w_fc, b_mn=True)                                     # dpre W1          (T, dim)
         dx = C.rmsnorm_bwd(x, dy, rstd, None)
-        return dx, d_fc, d_proj, None
+        if g_fc is not None:
+            return dx, None, None, None, None, None
+        return dx, d_fc, d_proj, None, None, None
 
 
-def norm_relu2_mlp(x: Tensor, w_fc: Tensor, w_proj: Tensor, fp8_state=None) -> Tensor:
+def norm_relu2_mlp(x: Tensor, w_fc: Tensor, w_proj: Tensor, fp8_state=None, grad_views=None) -> Tensor:
+    """`grad_views = (g_fc, g_proj)`: slices of the bank gradient the weight gradients are accumulated
+    into by the backward GEMMs (the weights then receive no autograd gradient)."""
+    if grad_views is not None:
+        return _NormRelu2Mlp.apply(x, w_fc.detach(), w_proj.detach(), fp8_state, grad_views[0], grad_views[1])
     return _NormRelu2Mlp.apply(x, w_fc, w_proj, fp8_state)
+
+
+class _BankLinear(torch.autograd.Function):
+    """y = x @ (lam * W)^T for a weight W assembled from parameter-bank slices.  The backward adds
+    lam * dy^T x into the given slices of the bank gradients and returns d lam = <dy^T x, W>."""
+
+    @staticmethod
+    def forward(ctx, x, lam, w, *grad_views):
+        w_eff = (lam * w).contiguous()
+        ctx.save_for_backward(x, lam, w, w_eff)
+        ctx.grad_views = grad_views
+        return x @ w_eff.t()
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, lam, w, w_eff = ctx.saved_tensors
+        dy = dy.reshape(-1, dy.shape[-1])
+        dx = dy @ w_eff
+        dw = dy.t() @ x.reshape(-1, x.shape[-1])                              # unscaled: (N, K)
+        dlam = (dw.float() * w.float()).sum().to(lam.dtype).reshape(lam.shape)
+        r = 0
+        for gv in ctx.grad_views:
+            n = gv.shape[0]
+            gv.addcmul_(dw[r:r + n], lam)
+            r += n
+        return (dx.view(x.shape), dlam, None) + (None,) * len(ctx.grad_views)
+
+
+def bank_linear(x: Tensor, lam: Tensor, w_parts: list, grad_views: list) -> Tensor:
+    w = torch.cat([p.detach() for p in w_parts], dim=0) if len(w_parts) > 1 else w_parts[0].detach()
+    return _BankLinear.apply(x, lam, w, *grad_views)
 
 
 def relu2_mlp(x_normed: Tensor, w_fc: Tensor, w_proj: Tensor, fp8_state=None) -> Tensor:

@@ -141,3 +141,28 @@ def xsa_gate(y: Tensor, v: Tensor, alpha: Tensor | None, gate: Tensor | None) ->
     if alpha is None and gate is None:
         return y
     return _XsaGate.apply(y, v, alpha, gate)
+
+
+class _EmbedDirect(torch.autograd.Function):
+    """Row gather whose backward adds the row gradients straight into `grad_buf` (the parameter's
+    persistent .grad, bf16 [V, D]) with the sorted segmented-sum kernel; the weight itself receives
+    no autograd gradient."""
+
+    @staticmethod
+    def forward(ctx, ids, weight, grad_buf):
+        ctx.save_for_backward(ids)
+        ctx.grad_buf = grad_buf
+        return torch.nn.functional.embedding(ids, weight)
+
+    @staticmethod
+    def backward(ctx, g):
+        (ids,) = ctx.saved_tensors
+        sorted_ids, perm = torch.sort(ids.reshape(-1))
+        g2 = g.reshape(-1, g.shape[-1]).contiguous()
+        lib().embed_bwd(g2, sorted_ids, perm, ctx.grad_buf)
+        return None, None, None
+
+
+def embed_direct(ids: Tensor, weight: Tensor, grad_buf: Tensor) -> Tensor:
+    """weight[ids] with gradient accumulation into grad_buf.  The dummy leaf keeps the op in the graph."""
+    return _EmbedDirect.apply(ids, weight.detach().requires_grad_(True), grad_buf)
