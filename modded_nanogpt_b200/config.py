@@ -248,3 +248,45 @@ def tiny_stages(batch_tokens: int = 4 * 256 * 2, seq_len: int = 256) -> list[Tra
 
 def scaled(hp: Hyperparameters, **kw) -> Hyperparameters:
     return replace(hp, **kw)
+
+
+# --------------------------------------------------------------------------------------
+# Track 2 (train_gpt_medium.py:1610-1640, 1402-1433)
+
+TRACK2_BS = (131072, 262144, 393216, 524288) + (524288,) * 8
+TRACK2_WS = (3, 7, 11, 13, 15, 17, 19, 21, 23, 23, 23, 23)
+
+
+def track2_stages() -> list[TrainingStage]:
+    lr = [1.0, 1.52, 1.73] + [2.0] * 9
+    stages = []
+    for k in range(12):
+        if k == 0:
+            mtp = ([1.0, 0.5, 0.25], [1.0, 0.5, 0.0])
+        elif k == 1:
+            mtp = ([1.0, 0.5], [1.0, 0.0])
+        else:
+            mtp = ([1.0], [1.0])
+        stages.append(TrainingStage(duration=1 / 12, train_max_seq_len=4096, batch_size=TRACK2_BS[k],
+                                    window_sizes=(min(11, TRACK2_WS[k] // 2), TRACK2_WS[k]), lr_mul=lr[k],
+                                    mtp_weights_start=mtp[0], mtp_weights_end=mtp[1]))
+    stages.append(TrainingStage(train_max_seq_len=4096, batch_size=32 * 2048 * 8, window_sizes=(11, 23), lr_mul=0.1,
+                                mtp_weights_start=[1.0], mtp_weights_end=[1.0]))
+    return stages
+
+
+def track2_hyperparameters(**kw) -> Hyperparameters:
+    base = dict(num_scheduled_iterations=4700, num_extension_iterations=40, cooldown_frac=0.70, adam_lr=0.004, adam_eps=1e-8,
+                muon_lr=0.015, muon_beta2=0.95)
+    base.update(kw)
+    return Hyperparameters(**base)
+
+
+def track2_schedule(hp: Hyperparameters | None = None) -> TrainingSchedule:
+    hp = hp or track2_hyperparameters()
+    s = TrainingSchedule(track2_stages(), hp.num_scheduled_iterations, hp.num_extension_iterations,
+                         cooldown_frac=hp.cooldown_frac, ws_post_yarn_ext=27, final_lr_frac=0.1)
+    import math
+    s.split_step = math.ceil(2 / 3 / 4 * hp.num_scheduled_iterations) | 1
+    s.yarn_max_ws = 13          # rotary rescaling only follows the first few window changes
+    return s

@@ -65,8 +65,8 @@ class TrainingManager:
                  collectives=None, math=None, sparse_min_world: int = 8):
         self.model, self.schedule, self.hp, self.env = model, schedule, hp, env
         self.block_size = hp.block_size
-        self.param_table = track1_param_table()
-        self.work_order = list(TRACK1_WORK_ORDER)
+        self.param_table = model.param_table() if hasattr(model, "param_table") else track1_param_table()
+        self.work_order = list(getattr(model, "WORK_ORDER", TRACK1_WORK_ORDER))
         dev = next(model.parameters()).device
         self.sparse = None
         self.row_tracker = None
@@ -108,8 +108,9 @@ class TrainingManager:
     def advance_schedule(self, step: int):
         stage, _ = self.schedule.lookup(step)
         self.ws_short, new_long = stage.window_sizes
-        if new_long != self.ws_long:
-            for y in (self.model.yarn, self.model.yarn_paired_head):
+        cap = getattr(self.schedule, "yarn_max_ws", None)
+        if new_long != self.ws_long and (cap is None or new_long <= cap):
+            for y in {id(self.model.yarn): self.model.yarn, id(self.model.yarn_paired_head): self.model.yarn_paired_head}.values():
                 y.apply(self.ws_long * self.block_size, new_long * self.block_size)
         if stage.batch_size != self.batch_size or stage.train_max_seq_len != self.train_max_seq_len:
             self.train_loader_send_args = (stage.batch_size, stage.train_max_seq_len, self.env.grad_accum_steps)
@@ -140,7 +141,8 @@ class TrainingManager:
         self.batch_size, self.train_max_seq_len = stage.batch_size, stage.train_max_seq_len
         self.train_loader_send_args = None
         self.model.yarn.reset()
-        self.model.yarn_paired_head.reset()
+        if self.model.yarn_paired_head is not self.model.yarn:
+            self.model.yarn_paired_head.reset()
         if self.row_tracker is not None:
             self.row_tracker.mask.fill(0)
 
@@ -197,7 +199,7 @@ class Trainer:
         self.train_loader = None
         self.step = 0
         self.training_time_ms = 0.0
-        self._bigram_vocab = model_cfg.bigram_vocab_size
+        self._bigram_vocab = getattr(getattr(self.model, "cfg", None), "bigram_vocab_size", 0)
         self.model.train()
 
     # -- data ----------------------------------------------------------------------------
