@@ -25,6 +25,7 @@ from .optim.normuon_adam import NorMuonAndAdam
 from .parallel.collectives import TorchCollectives
 from .parallel.sparse_comms import RowTracker, SparseRowExchange
 from .runtime.dist import DistEnv, broadcast_model
+from .runtime.health import monitor_from_env
 from .utils.logging import RunLogger
 
 
@@ -199,6 +200,7 @@ class Trainer:
         self.train_loader = None
         self.step = 0
         self.training_time_ms = 0.0
+        self.health = monitor_from_env(env)
         self._bigram_vocab = getattr(getattr(self.model, "cfg", None), "bigram_vocab_size", 0)
         self.model.train()
 
@@ -225,6 +227,14 @@ class Trainer:
     def train_step(self, step: int | None = None) -> torch.Tensor:
         """Returns the (detached, device) sum-loss of the step's micro-batches."""
         step = self.step if step is None else step
+        if self.health is not None:
+            # peers that failed or stalled are noticed here, on the host, before any kernel that waits on them
+            self.health.pre_step(step)
+            with self.health.guard():
+                return self._train_step(step)
+        return self._train_step(step)
+
+    def _train_step(self, step: int) -> torch.Tensor:
         if self.train_loader is None:
             self.train_loader = self.make_train_loader()
         self.manager.advance_schedule(step)
