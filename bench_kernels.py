@@ -1,0 +1,117 @@
+"""Micro-benchmarks of the hand-written kernels, one case per invocation (CUDA-event timing after warm-up).
+
+    python bench_kernels.py --list
+    python bench_kernels.py --case gemm_bf16_o --rows 49152 --bn 256 --iters 10
+
+Every case works on operands larger than the L2 cache at the default --rows.  The same command line
+(with a small --iters) is what the committed profiler summaries under profiles/ were captured from."""
+import argparse
+import json
+
+import torch
+
+BF, F8, F8B = torch.bfloat16, torch.float8_e4m3fn, torch.float8_e5m2
+V, D, H = 50304, 768, 3072
+
+
+def build_case(name, T, bn, fused):
+    dev = "cuda"
+    r = lambda *s: torch.randn(*s, device=dev)
+    fl = 2 * T * D * H
+    if name == "gemm_bf16_up":          # [T,768] x [3072,768]^T
+        a, b = r(T, D).to(BF), r(H, D).to(BF)
+        return (lambda: fused.gemm(a, b, bn=bn)), fl, T * H * 2
+    if name == "gemm_bf16_dpre":        # same product, epilogue 2*acc*sqrt(post) reading the saved activations
+        a, b, post = r(T, D).to(BF), r(H, D).to(BF), r(T, H).abs().to(BF)
+        return (lambda: fused.gemm(a, b, epilogue=fused.EPI_DPRE, cin=post, bn=bn)), fl, T * H * 4
+    if name == "gemm_bf16_down":        # [T,3072] x [768,3072]^T
+        a, b = r(T, H).to(BF), r(D, H).to(BF)
+        return (lambda: fused.gemm(a, b, bn=bn)), fl, T * D * 2
+    if name == "gemm_bf16_dw":          # [T,3072]^T x [T,768] -> [3072,768] fp32, both operands MN-major
+        a, b = r(T, H).to(BF), r(T, D).to(BF)
+        return (lambda: fused.gemm(a, b, a_mn=True, b_mn=True, bn=bn, out_dtype=torch.float32)), fl, H * D * 4
+    if name == "gemm_fp8_relu2":        # fp8 up projection with relu^2, bf16 + e4m3 outputs and running max
+        a, b = r(T, D).to(F8), r(H, D).to(F8)
+        rs, cs = torch.ones(T, device=dev), torch.ones(H, device=dev)
+        act, amax = torch.tensor([0.02], device=dev), torch.zeros(1, dtype=torch.int32, device=dev)
+        o, o8 = torch.empty(T, H, dtype=BF, device=dev), torch.empty(T, H, dtype=F8, device=dev)
+        return (lambda: fused.gemm(a, b, out=o, epilogue=fused.EPI_RELU2, row_scale=rs, col_scale=cs, out8=o8,
+                                   act_scale=act, amax_bits=amax, bn=bn)), fl, T * H * 3
+    if name == "gemm_fp8_down":
+        a, b = r(T, H).to(F8), r(D, H).to(F8)
+        return (lambda: fused.gemm(a, b, bn=bn)), fl, T * D * 2
+    if name == "gemm_bf16_qkv":
+        a, b = r(T, D).to(BF), r(3 * D, D).to(BF)
+        return (lambda: fused.gemm(a, b, bn=bn)), 2 * T * D * 3 * D, T * 3 * D * 2
+    if name == "gemm_bf16_o":
+        a, b = r(T, D).to(BF), r(D, D).to(BF)
+        return (lambda: fused.gemm(a, b, bn=bn)), 2 * T * D * D, T * D * 2
+    if name == "gemm_bf16_o_null":      # same product, accumulators drained but not stored (load + MMA pipeline only)
+        a, b = r(T, D).to(BF), r(D, D).to(BF)
+        o = torch.empty(T, D, dtype=BF, device=dev)
+        return (lambda: fused.gemm(a, b, out=o, bn=bn, epilogue=3)), 2 * T * D * D, 0
+    if name == "gemm_bf16_up_null":
+        a, b = r(T, D).to(BF), r(H, D).to(BF)
+        o = torch.empty(T, H, dtype=BF, device=dev)
+        return (lambda: fused.gemm(a, b, out=o, bn=bn, epilogue=3)), fl, 0
+    if name == "gemm_fp8_logits":       # [T,768] x [768,V] (B MN-major) -> bf16 logits
+        a, b = r(T, D).to(F8), r(D, V).to(F8)
+        o = torch.empty(T, V, dtype=BF, device=dev)
+        return (lambda: fused.gemm(a, b, b_mn=True, out=o, bn=bn)), 2 * T * D * V, T * V * 2
+    if name == "gemm_fp8_lmhead_dx":    # e5m2 [T,V] x e4m3 [768,V]^T
+        a, b = torch.randn(T, V, device=dev, dtype=BF).to(F8B), r(D, V).to(F8)
+        return (lambda: fused.gemm(a, b, bn=bn)), 2 * T * D * V, T * D * 2
+    if name == "gemm_fp8_lmhead_dw":    # e4m3 [T,768]^T x e5m2 [T,V] -> fp32 [768,V]
+        a, b = r(T, D).to(F8), torch.randn(T, V, device=dev, dtype=BF).to(F8B)
+        o = torch.empty(D, V, dtype=torch.float32, device=dev)
+        return (lambda: fused.gemm(a, b, a_mn=True, b_mn=True, out=o, bn=bn)), 2 * T * D * V, D * V * 4
+    if name in ("softcap_ce_e5m2", "softcap_ce_bf16"):
+        from modded_nanogpt_b200.ops import native
+        lib = native.lib()
+        e5 = name.endswith("e5m2")
+        logits = torch.randn(T, V, device=dev, dtype=BF) * 3
+        tg, pt = torch.randint(0, V, (T,), device=dev), torch.randint(-1, V, (T,), device=dev)
+        w, pw = torch.tensor([1.0, 0.5, 0.25], device=dev), torch.tensor([0.3], device=dev)
+        return (lambda: lib.softcap_ce(logits, tg, w, pt, pw, e5, 23.0, 5.0, 7.5, 1.0)), 0, T * V * (3 if e5 else 4)
+    raise SystemExit(f"unknown case {name}")
+
+
+CASES = ["gemm_bf16_up", "gemm_bf16_dpre", "gemm_bf16_down", "gemm_bf16_dw", "gemm_fp8_relu2", "gemm_fp8_down", "gemm_bf16_qkv",
+         "gemm_bf16_o", "gemm_bf16_o_null", "gemm_bf16_up_null", "gemm_fp8_logits", "gemm_fp8_lmhead_dx", "gemm_fp8_lmhead_dw", "softcap_ce_e5m2", "softcap_ce_bf16"]
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--case", default="all")
+    ap.add_argument("--rows", type=int, default=49152)
+    ap.add_argument("--bn", type=int, default=0, help="GEMM tile: 128, 256, 512 (CTA pair); 0 = the wrapper's choice")
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--list", action="store_true")
+    a = ap.parse_args()
+    if a.list:
+        print("\n".join(CASES))
+        return
+    from modded_nanogpt_b200.ops import fused
+    for name in (CASES if a.case == "all" else a.case.split(",")):
+        torch.manual_seed(0)
+        fn, flops, out_bytes = build_case(name, a.rows, a.bn or None, fused)
+        for _ in range(a.warmup):
+            fn()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(a.iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / a.iters
+        fused.check_status()
+        print(json.dumps(dict(case=name, rows=a.rows, bn=a.bn, us=round(ms * 1e3, 1), tflops=round(flops / ms / 1e9, 1),
+                              out_gbs=round(out_bytes / ms / 1e6, 1))), flush=True)
+        del fn
+        torch.cuda.empty_cache()
+
+
+if __name__ == "__main__":
+    main()

@@ -9,7 +9,7 @@ extern "C" {
 #endif
 
 enum { MNG_BF16 = 0, MNG_E4M3 = 1, MNG_E5M2 = 2 };
-enum { MNG_EPI_STORE = 0, MNG_EPI_RELU2 = 1, MNG_EPI_DPRE = 2 };
+enum { MNG_EPI_STORE = 0, MNG_EPI_RELU2 = 1, MNG_EPI_DPRE = 2, MNG_EPI_NULL = 3 /* no output: profiling aid */ };
 
 // D[b] = epi(A[b] (MxK) * B[b]^T (NxK)).  a_mn / b_mn: operand is stored [K, rows] instead of [rows, K].
 typedef struct {
@@ -21,7 +21,7 @@ typedef struct {
   long long lda, ldb;                 // row stride of the stored arrays, in elements
   long long a_bstride, b_bstride;     // batch strides in elements
   int epilogue;
-  int bn;                             // CTA tile width: 128 or 256
+  int bn;                             // CTA tile width: 128 or 256; 512 = 256 x 256 tile on a pair of CTAs (cta_group::2)
   int out_f32;
   void* out;
   long long ldc, c_bstride;

@@ -156,6 +156,172 @@ softcap_ce_kernel(const __nv_bfloat16* __restrict__ logits, const long long* __r
   }
 }
 
+// ---------------------------------------------------------------------------------------------------
+// Streaming variant: persistent 512-thread CTAs, two per SM, each walking rows blockIdx.x, +gridDim.x, ...
+// A row of logits arrives in shared memory by one bulk async copy (cp.async.bulk, completion on an
+// mbarrier) and is rewritten in place: raw logit -> bf16(exp(z-A) * s * (1-s)), the only per-column
+// quantity the gradient sweep needs; the sigmoids at the (at most n_predict+1) target columns are
+// recomputed from global memory while the copy is in flight.  The two CTAs of an SM run out of phase, so
+// one CTA's copy and store-heavy gradient sweep overlap the other's special-function-heavy first sweep.
+// One row buffer of vocab*2 bytes per CTA.  Needs vocab % 16 == 0 and 16-byte aligned rows.
+__device__ __forceinline__ void bulk_load_1d(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               :
+               : "r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+constexpr int CE_STREAM_THREADS = 512;
+
+template <bool OUT_E5M2>
+__global__ void __launch_bounds__(CE_STREAM_THREADS, 2)
+softcap_ce_stream_kernel(const __nv_bfloat16* __restrict__ logits, const long long* __restrict__ targets,
+                         const float* __restrict__ mtp_weights, int n_predict,
+                         const long long* __restrict__ prefix_targets, const float* __restrict__ prefix_weight_ptr,
+                         float* __restrict__ losses, void* __restrict__ dlogits, long long rows, int vocab, long long ld,
+                         float A, float B, float C, float grad_mul) {
+  constexpr int TH = CE_STREAM_THREADS;
+  extern __shared__ __align__(128) unsigned char ce_smem[];
+  __nv_bfloat16* const buf = reinterpret_cast<__nv_bfloat16*>(ce_smem);
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ float red[TH / 32];
+  __shared__ uint32_t s_abort;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const uint32_t bytes = (uint32_t)vocab * 2u;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    s_abort = 0;
+    mbar_fence_init();
+  }
+  __syncthreads();
+  const float half_inv_c = 0.5f / C, half_b_over_c = 0.5f * B / C;
+  const float k2 = A * 1.4426950408889634f;            // exp(A*s - A) = exp2(k2*s - k2)
+  const float gscale = grad_mul * (A / C);
+  const float prefix_weight = prefix_weight_ptr ? prefix_weight_ptr[0] : 0.f;
+  float w_sum = 0.f;
+  for (int k = 0; k < n_predict; ++k) w_sum += mtp_weights[k];
+  const int nvec = vocab >> 3;
+
+  int it = 0;
+  for (long long row = blockIdx.x; row < rows; row += gridDim.x, ++it) {
+    const __nv_bfloat16* lrow = logits + row * ld;
+    if (tid == 0) {
+      fence_proxy_async_smem();                         // the buffer was last touched by generic-proxy accesses
+      mbar_expect_tx(&bar, bytes);
+      bulk_load_1d(buf, lrow, bytes, &bar);
+    }
+    // this thread's target column (threads 0..n_predict): logit straight from global memory
+    long long tgt = -1;
+    bool tvalid = false;
+    float tw = 0.f, ts = 0.f, hit = 0.f;
+    const long long ptgt = prefix_targets ? prefix_targets[row] : -1;
+    const bool pvalid = ptgt >= 0 && ptgt < vocab;
+    if (tid <= n_predict) {
+      if (tid < n_predict) {
+        if (row + tid < rows) tgt = targets[row + tid];
+        tw = mtp_weights[tid];
+      } else {
+        tgt = pvalid ? ptgt : -1;
+        tw = prefix_weight;
+      }
+      tvalid = tgt >= 0 && tgt < vocab;
+      if (tvalid) {
+        float t;
+        asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(__bfloat162float(lrow[tgt]) * half_inv_c + half_b_over_c));
+        ts = 0.5f + 0.5f * t;
+        for (int k = 0; k < n_predict; ++k)
+          if (row + k < rows && targets[row + k] == tgt) hit += mtp_weights[k];
+        if (pvalid && ptgt == tgt) hit += prefix_weight;
+      }
+    }
+    if (!mbar_wait(&bar, (uint32_t)it & 1u, &s_abort)) s_abort = 1;
+    __syncthreads();
+    if (s_abort) {                                      // the copy never landed: mark what is left and leave
+      for (long long r = row; r < rows; r += gridDim.x)
+        if (tid == 0) losses[r] = __int_as_float(0x7fc00000);
+      break;
+    }
+
+    float part = 0.f;
+#pragma unroll 2
+    for (int i = tid; i < nvec; i += TH) {
+      uint4 u = *reinterpret_cast<const uint4*>(buf + i * 8);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+      uint4 w;
+      uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float2 f = __bfloat1622float2(h[t]);
+        float t0, t1;
+        asm("tanh.approx.f32 %0, %1;" : "=f"(t0) : "f"(f.x * half_inv_c + half_b_over_c));
+        asm("tanh.approx.f32 %0, %1;" : "=f"(t1) : "f"(f.y * half_inv_c + half_b_over_c));
+        const float s0 = 0.5f + 0.5f * t0, s1 = 0.5f + 0.5f * t1;
+        const float e0 = exp2f(k2 * s0 - k2), e1 = exp2f(k2 * s1 - k2);
+        part += e0 + e1;
+        wp[t] = pack_bf16x2(e0 * s0 * (0.5f - 0.5f * t0), e1 * s1 * (0.5f - 0.5f * t1));
+      }
+      *reinterpret_cast<uint4*>(buf + i * 8) = w;
+    }
+    part = warp_sum(part);
+    if (lane == 0) red[tid >> 5] = part;
+    __syncthreads();
+    const float tot = warp_sum(lane < TH / 32 ? red[lane] : 0.f);
+    const float lse = A + __logf(tot), inv_tot = 1.f / tot;
+    const float S_w = w_sum + (pvalid ? prefix_weight : 0.f);
+
+    if (tid < 32) {                                     // loss: the target threads all sit in warp 0
+      float l = tvalid ? tw * (lse - A * ts) : 0.f;
+      l = warp_sum(l);
+      if (tid == 0) losses[row] = l;
+    }
+
+    const float c = gscale * S_w * inv_tot;
+    if constexpr (OUT_E5M2) {
+      uint8_t* drow = reinterpret_cast<uint8_t*>(dlogits) + row * ld;
+#pragma unroll 2
+      for (int i = tid; i < (vocab >> 4); i += TH) {
+        const uint4 u0 = *reinterpret_cast<const uint4*>(buf + i * 16);
+        const uint4 u1 = *reinterpret_cast<const uint4*>(buf + i * 16 + 8);
+        const __nv_bfloat162* h0 = reinterpret_cast<const __nv_bfloat162*>(&u0);
+        const __nv_bfloat162* h1 = reinterpret_cast<const __nv_bfloat162*>(&u1);
+        uint32_t o[4];
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const float2 a = __bfloat1622float2(h0[2 * t]), b = __bfloat1622float2(h0[2 * t + 1]);
+          o[t] = pack_e5m2x2(c * a.x, c * a.y) | ((uint32_t)pack_e5m2x2(c * b.x, c * b.y) << 16);
+          const float2 d = __bfloat1622float2(h1[2 * t]), e = __bfloat1622float2(h1[2 * t + 1]);
+          o[2 + t] = pack_e5m2x2(c * d.x, c * d.y) | ((uint32_t)pack_e5m2x2(c * e.x, c * e.y) << 16);
+        }
+        *reinterpret_cast<uint4*>(drow + i * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    } else {
+      __nv_bfloat16* drow = reinterpret_cast<__nv_bfloat16*>(dlogits) + row * ld;
+#pragma unroll 2
+      for (int i = tid; i < nvec; i += TH) {
+        const uint4 u = *reinterpret_cast<const uint4*>(buf + i * 8);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+        uint4 w;
+        uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const float2 a = __bfloat1622float2(h[t]);
+          wp[t] = pack_bf16x2(c * a.x, c * a.y);
+        }
+        *reinterpret_cast<uint4*>(drow + i * 8) = w;
+      }
+    }
+    __syncthreads();                                    // sweep done: the buffer is free, fix-ups may follow
+
+    if (tid <= n_predict && tvalid) {                   // target columns: same value from every thread that hits one
+      const float gv = gscale * (S_w * exp2f(k2 * ts - k2) * inv_tot - hit) * ts * (1.f - ts);
+      if constexpr (OUT_E5M2)
+        reinterpret_cast<uint8_t*>(dlogits)[row * ld + tgt] = (uint8_t)(pack_e5m2x2(gv, 0.f) & 0xff);
+      else
+        reinterpret_cast<__nv_bfloat16*>(dlogits)[row * ld + tgt] = __float2bfloat16(gv);
+    }
+  }
+}
+
 }  // namespace mng
 
 using namespace mng;
@@ -166,10 +332,32 @@ extern "C" int mng_softcap_ce(const void* logits, const long long* targets, cons
                               float grad_mul, void* stream) {
   if (rows == 0) return 0;
   if (vocab % 8 || ld % 8 || n_predict > CE_MAX_PREDICT || n_predict < 1) return -1;
+  cudaStream_t st = (cudaStream_t)stream;
   const size_t smem1 = (size_t)vocab * 2, smem2 = (size_t)vocab * 4;
+  if (vocab % 16 == 0 && (ld * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(dlogits) & 15) == 0 && smem1 <= 110 * 1024) {
+    static int sms = 0;
+    if (sms == 0) {
+      int dev = 0;
+      if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return -5;
+      if (cudaFuncSetAttribute(softcap_ce_stream_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 110 * 1024) != cudaSuccess ||
+          cudaFuncSetAttribute(softcap_ce_stream_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 110 * 1024) != cudaSuccess)
+        return -3;
+    }
+    const unsigned grid = (unsigned)(rows < 2 * sms ? rows : 2 * sms);
+    if (dlogits_is_e5m2)
+      softcap_ce_stream_kernel<true><<<grid, CE_STREAM_THREADS, smem1, st>>>((const __nv_bfloat16*)logits, targets, mtp_weights, n_predict,
+                                                                prefix_targets, prefix_weight, losses, dlogits, rows, vocab, ld,
+                                                                A, B, C, grad_mul);
+    else
+      softcap_ce_stream_kernel<false><<<grid, CE_STREAM_THREADS, smem1, st>>>((const __nv_bfloat16*)logits, targets, mtp_weights, n_predict,
+                                                                 prefix_targets, prefix_weight, losses, dlogits, rows, vocab, ld,
+                                                                 A, B, C, grad_mul);
+    return cudaGetLastError() == cudaSuccess ? 0 : -4;
+  }
   const bool cache = smem2 <= 220 * 1024;
   if (!cache && smem1 > 200 * 1024) return -2;
-  cudaStream_t st = (cudaStream_t)stream;
 #define CE_LAUNCH(E5, CACHE, TH, SMEM)                                                                              \
   do {                                                                                                              \
     static bool set = false;                                                                                        \

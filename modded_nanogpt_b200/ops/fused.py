@@ -11,6 +11,8 @@ Forward/backward pairs here mirror the reference's fused ops:
 """
 from __future__ import annotations
 
+import os
+
 import torch
 from torch import Tensor
 
@@ -18,6 +20,7 @@ from . import native
 
 EPI_STORE, EPI_RELU2, EPI_DPRE = 0, 1, 2
 NUM_SMS = 148
+PAIR_GEMM = os.environ.get("MNG_GEMM_PAIR", "1") != "0"
 
 
 def _C():
@@ -54,6 +57,10 @@ def gemm(a: Tensor, b: Tensor, *, a_mn: bool = False, b_mn: bool = False, out: T
         bn = 256 if (tiles256 >= NUM_SMS or N > 4096) and epilogue == EPI_STORE else 128
         if epilogue != EPI_STORE:
             bn = 256
+        # CTA pairs (256 x 256 tiles, TMA output path) once there is at least one tile per pair of SMs;
+        # the C side falls back to the 128 x 256 kernel for outputs it cannot describe by a tensor map
+        if PAIR_GEMM and out.dtype == torch.bfloat16 and -(-M // 256) * -(-N // 256) * batch >= NUM_SMS // 2:
+            bn = 512
     _C().gemm(a, b, out, a_mn, b_mn, epilogue, bn, alpha, beta, cin, alpha_t, row_scale, col_scale, out8, act_scale,
               amax_bits, max_ctas)
     return out
