@@ -110,7 +110,8 @@ def main():
         env.barrier()
         torch.cuda.synchronize()
         sampler = ClockSampler(env.local_rank).start() if env.master else None
-        launches0 = native.lib().launch_count()
+        replayed = lambda: tr.graphs.replayed_launches if tr.graphs is not None else 0
+        launches0 = native.lib().launch_count() + replayed()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0 = time.perf_counter()
         e0.record()
@@ -121,7 +122,7 @@ def main():
         wall = time.perf_counter() - t0
         clocks = sampler.stop() if sampler else None
         ms = max_over_ranks(e0.elapsed_time(e1))
-        return ms, max_over_ranks(wall * 1e3), native.lib().launch_count() - launches0, clocks, out
+        return ms, max_over_ranks(wall * 1e3), native.lib().launch_count() + replayed() - launches0, clocks, out
 
     # ---- region 1: device-resident inputs ------------------------------------------------------
     staged = [[tr.train_loader.next_batch() for _ in range(env.grad_accum_steps)] for _ in range(K)]

@@ -374,10 +374,16 @@ static int cached_map(CUtensorMap* out, const void* ptr, int es, long long inner
   if (it == cache.end()) {
     // Encoding needs a current driver context; a thread that has not yet run any runtime call (an
     // autograd worker whose first op is one of ours) has none until the runtime binds the primary one.
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaSetDevice(dev);
-    cudaFree(nullptr);
+    // Done once per thread, so that later misses (new activation addresses while a stream capture
+    // is recording) make no runtime call that a capture forbids.
+    static thread_local bool ctx_bound = false;
+    if (!ctx_bound) {
+      int dev = 0;
+      cudaGetDevice(&dev);
+      cudaSetDevice(dev);
+      cudaFree(nullptr);
+      ctx_bound = true;
+    }
     CUtensorMap m;
     int rc = make_tensor_map(&m, ptr, es, inner, outer, batch, ld, bs, bi, bo);
     if (rc) return rc;

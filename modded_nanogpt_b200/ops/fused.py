@@ -270,8 +270,8 @@ class _SoftcapCE(torch.autograd.Function):
         fp8, x_s, w_s, g_s = ctx.cfg
         # dl already carries grad_scale: the caller reduces the losses with .sum() * grad_scale
         dx = gemm(dl, wq, alpha=g_s * w_s)                                           # dl W^T          (T, D)
-        dw = gemm(xq, dl, a_mn=True, b_mn=True, alpha=x_s * g_s, out_dtype=torch.float32)   # x^T dl   (D, V)
-        return dx, dw.to(torch.bfloat16), None, None, None, None, None, None, None, None, None, None
+        dw = gemm(xq, dl, a_mn=True, b_mn=True, alpha=x_s * g_s)                     # x^T dl          (D, V)
+        return dx, dw, None, None, None, None, None, None, None, None, None, None
 
 
 def softcap_ce(x, w, targets, mtp_weights, prefix_targets, prefix_weight, a, b, c, grad_scale=1.0, fp8=True,

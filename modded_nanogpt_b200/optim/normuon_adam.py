@@ -117,6 +117,7 @@ class NorMuonAndAdam:
         self._init_state()
         self._pending: dict[str, tuple] = {}
         self.split_embed = False
+        self.keep_grads = False     # zero gradients in place after a step instead of dropping the tensors
 
     # reference-compatible views -------------------------------------------------------
     @property
@@ -320,6 +321,8 @@ class NorMuonAndAdam:
                 continue
             if fused and p.grad is not None:
                 self.coll.clear_grad(p)     # gradients live in peer-mapped memory: keep the buffer, zero it
+            elif self.keep_grads and p.grad is not None:
+                p.grad.zero_()              # a captured CUDA graph accumulates into this very tensor
             else:
                 p.grad = None
 

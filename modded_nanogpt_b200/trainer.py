@@ -201,6 +201,13 @@ class Trainer:
         self.step = 0
         self.training_time_ms = 0.0
         self.health = monitor_from_env(env)
+        if use_cuda_graphs is None:
+            use_cuda_graphs = env.device.type == "cuda" and os.environ.get("MNG_CUDA_GRAPHS", "1") != "0"
+        self.graphs = None
+        if use_cuda_graphs and env.device.type == "cuda":
+            from .runtime.graphs import MicroStepGraphs
+            self.graphs = MicroStepGraphs(self)
+            self.manager.optimizer.keep_grads = True
         self._bigram_vocab = getattr(getattr(self.model, "cfg", None), "bigram_vocab_size", 0)
         self.model.train()
 
@@ -218,6 +225,9 @@ class Trainer:
     def micro_step(self, batch, step: int) -> torch.Tensor:
         m = self.manager
         m.sparse_index_update(step, batch.bigram_cpu)
+        if self.graphs is not None and self.model.training:
+            m.sparse_index_share(step)
+            return self.graphs.run(batch, m.get_forward_args())
         losses = self.model(batch.inputs, batch.targets, batch.cum_seqlens, batch.bigram_inputs, m.get_forward_args())
         loss = losses.sum() * self.env.grad_scale
         m.sparse_index_share(step)
@@ -308,13 +318,15 @@ class Trainer:
             m.step_optimizers(step)
             self.model.quantize_mlp_fp8(bootstrap_down=True)
         self.log.print0("Resetting Model", console=True)
-        if getattr(m.optimizer.coll, "fused", False):
-            for p in self.model.parameters():       # gradients live in peer-mapped memory: keep the buffers
+        if getattr(m.optimizer.coll, "fused", False) or m.optimizer.keep_grads:
+            for p in self.model.parameters():       # gradients live in peer-mapped memory / captured graphs: keep the buffers
                 if p.grad is not None:
                     p.grad.zero_()
         else:
             self.model.zero_grad(set_to_none=True)
         self.model.load_state_dict(init["model"])
+        if self.graphs is not None:
+            self.graphs.entries.clear()             # recapture after the reset: cheap, and immune to reallocated state
         m.reset(init["optimizer"])
         self.model.quantize_mlp_fp8(bootstrap_down=True)
         self.model.train()
