@@ -73,11 +73,35 @@ def build_case(name, T, bn, fused):
         tg, pt = torch.randint(0, V, (T,), device=dev), torch.randint(-1, V, (T,), device=dev)
         w, pw = torch.tensor([1.0, 0.5, 0.25], device=dev), torch.tensor([0.3], device=dev)
         return (lambda: lib.softcap_ce(logits, tg, w, pt, pw, e5, 23.0, 5.0, 7.5, 1.0)), 0, T * V * (3 if e5 else 4)
+    if name.startswith("attn_"):            # attn_{ours|fa2}_{short|long|paired}: packed documents, sliding window
+        _, impl, kind = name.split("_")
+        Tq, Hh, window = (2 * T, 3, 2 * 640) if kind == "paired" else (T, 6, 640 if kind == "short" else 1408)
+        g = torch.Generator(device=dev).manual_seed(0)
+        q, k, v = (torch.randn(Tq, Hh, 128, device=dev, generator=g).to(BF) for _ in range(3))
+        lens = torch.exp(torch.randn(4 * Tq // 600, generator=torch.Generator().manual_seed(0)) + 6.4).clamp(2, 2048).long()
+        if kind == "paired":
+            lens = lens * 2
+        starts = torch.cat([torch.zeros(1, dtype=torch.long), lens.cumsum(0)])
+        starts = starts[starts < Tq]
+        cu = torch.full((max(len(starts) + 1, 64),), Tq, dtype=torch.int32)
+        cu[:len(starts)] = starts.int()
+        cu = cu.to(dev)
+        pos = torch.arange(Tq, device=dev)
+        ds = fused.doc_starts(cu, Tq)
+        flops = 4 * 128 * Hh * int((pos - torch.maximum(ds.long(), pos - window) + 1).sum())
+        max_len = 4096
+        if impl == "ours":
+            lib = fused._C()
+            return (lambda: lib.attn_fwd(q, k, v, ds, window, 0.12)), flops, Tq * Hh * 256
+        from flash_attn import flash_attn_varlen_func
+        return (lambda: flash_attn_varlen_func(q, k, v, cu_seqlens_q=cu, cu_seqlens_k=cu, max_seqlen_q=max_len, max_seqlen_k=max_len,
+                                               causal=True, softmax_scale=0.12, window_size=(window, 0))), flops, Tq * Hh * 256
     raise SystemExit(f"unknown case {name}")
 
 
 CASES = ["gemm_bf16_up", "gemm_bf16_dpre", "gemm_bf16_down", "gemm_bf16_dw", "gemm_fp8_relu2", "gemm_fp8_down", "gemm_bf16_qkv",
-         "gemm_bf16_o", "gemm_bf16_o_null", "gemm_bf16_up_null", "gemm_fp8_logits", "gemm_fp8_lmhead_dx", "gemm_fp8_lmhead_dw", "softcap_ce_e5m2", "softcap_ce_bf16"]
+         "gemm_bf16_o", "gemm_bf16_o_null", "gemm_bf16_up_null", "gemm_fp8_logits", "gemm_fp8_lmhead_dx", "gemm_fp8_lmhead_dw", "softcap_ce_e5m2", "softcap_ce_bf16",
+         "attn_ours_short", "attn_fa2_short", "attn_ours_long", "attn_fa2_long", "attn_ours_paired", "attn_fa2_paired"]
 
 
 def main():

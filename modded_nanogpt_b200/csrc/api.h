@@ -136,6 +136,12 @@ int mng_dc_mix_bwd(const float* dM, const void* P, const void* a, const void* w1
 int mng_embed_bwd(const void* g, const long long* sorted_ids, const long long* perm, void* grad, long long n, int D,
                   void* stream);
 
+// ---- attention forward (attn_sm100.cu) ------------------------------------------------------------------
+// q, k, v: [T, H, 128] bf16 with token stride `row_stride` elements (heads contiguous); doc_start[i] = first token of
+// i's document; keys j with max(doc_start[i], i - window) <= j <= i.  out [T, H, 128] bf16 contiguous, lse [H, T] fp32.
+int mng_attn_fwd(const void* q, const void* k, const void* v, const int* doc_start, void* out, float* lse, int T, int H,
+                 long long row_stride, int window, float scale, void* stream, uint32_t* status);
+
 // Barrier across ranks on signal pads (bounded wait; sets *status on expiry).
 int mng_peer_barrier(const PeerPtrs* pads, int rank, uint32_t epoch, uint32_t* status, void* stream);
 

@@ -1,0 +1,328 @@
+// Causal, document-masked sliding-window attention forward for sm_100a (head dim 128, bf16).
+//
+//   o[i,h,:] = softmax_j( scale * q[i,h,:].k[j,h,:] ) v[j,h,:]   over keys j of i's document with i-window <= j <= i
+//   lse[h,i] = log sum_j exp(scale * q.k)                         (natural log; what a flash-attention backward expects)
+//
+// Same contract as the reference's `flash_attn_varlen_func(..., causal=True, window_size=(W, 0))` call
+// (`train_gpt.py:1139-1141`) on one packed sequence; documents are given as `doc_start[i]` = index of the
+// first token of the document that holds token i.
+//
+// One CTA = 128 queries of one head, 192 threads, two CTAs per SM (96 KB of shared memory and 256 TMEM
+// columns each), so that one CTA's softmax overlaps the other's MMAs:
+//   warp 0    TMA producer: Q tile once, then K and V tiles of 128 keys (single buffers, refilled as soon as
+//             the MMA that read them has completed);
+//   warp 1    tcgen05 issuer: S = Q K^T (both operands K-major from shared memory) into TMEM columns [0,128);
+//             O += P V with P read from TMEM (bf16, aliasing S) and V MN-major from shared memory, into [128,256);
+//   warps 2-5 softmax: thread = query row.  Two passes over the S tile in TMEM (row maximum, then
+//             exponentials): p = exp2(s*c - m), bf16 P written back over S, row sums in fp32.  The running
+//             maximum only moves when it grows by more than 8 (factor 256), so the O accumulator is rescaled
+//             rarely; the final division by the row sum makes the result exact either way.
+// Key blocks run from max(doc_start[q0], q0 - window) to the tile's last query: blocks before the window or
+// the document never load.  Every mbarrier wait is bounded.
+#include "api.h"
+#include "ptx.cuh"
+
+#include <mutex>
+
+namespace mng {
+
+constexpr int ATT_THREADS = 192;
+constexpr int ATT_TILE_BYTES = 128 * 128 * 2;     // 128 rows x 128 dims bf16 = two 16 KB boxes
+constexpr int ATT_SMEM = 3 * ATT_TILE_BYTES + 1024 /*barriers*/ + 1024 /*alignment*/;
+
+struct AttnParams {
+  const int* doc_start;
+  __nv_bfloat16* out;
+  float* lse;
+  int T, H, window;
+  float scale_log2;       // softmax scale * log2(e)
+};
+
+__global__ void __launch_bounds__(ATT_THREADS, 2)
+attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                const __grid_constant__ CUtensorMap tv, AttnParams p, uint32_t* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = smem + ATT_TILE_BYTES;
+  uint8_t* sV = smem + 2 * ATT_TILE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 3 * ATT_TILE_BYTES);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = bars + 2;
+  uint64_t* v_full = bars + 3;
+  uint64_t* v_empty = bars + 4;
+  uint64_t* s_full = bars + 5;
+  uint64_t* p_ready = bars + 6;
+  uint64_t* o_done = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  volatile uint32_t* abort_flag = tmem_slot + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y;
+  const int q0 = (gridDim.x - 1 - blockIdx.x) * 128;       // late (long-history) tiles first
+  const int q_last = min(q0 + 127, p.T - 1);
+  const int kv_lo = max(p.doc_start[q0], q0 - p.window);
+  const int nb = (q_last - kv_lo) / 128 + 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(k_full, 1);
+    mbar_init(k_empty, 1);
+    mbar_init(v_full, 1);
+    mbar_init(v_empty, 1);
+    mbar_init(s_full, 1);
+    mbar_init(p_ready, 4);
+    mbar_init(o_done, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+    tma_prefetch_desc(&tq);
+    tma_prefetch_desc(&tk);
+    tma_prefetch_desc(&tv);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_S = *tmem_slot;
+  const uint32_t tmem_O = tmem_S + 128;
+#define ATT_FAIL(code)                                                          \
+  do {                                                                          \
+    if (*abort_flag == 0) { *abort_flag = (code); atomicCAS(status, 0u, (code)); } \
+  } while (0)
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_expect_tx(q_full, ATT_TILE_BYTES);
+      tma_load_3d(sQ, &tq, q_full, 0, h, q0);
+      tma_load_3d(sQ + 16384, &tq, q_full, 64, h, q0);
+      for (int j = 0; j < nb; ++j) {
+        const int kb = kv_lo + j * 128;
+        if (!mbar_wait(k_empty, (j & 1) ^ 1, abort_flag)) { ATT_FAIL(ERR_WAIT_SMEM_EMPTY); break; }
+        mbar_expect_tx(k_full, ATT_TILE_BYTES);
+        tma_load_3d(sK, &tk, k_full, 0, h, kb);
+        tma_load_3d(sK + 16384, &tk, k_full, 64, h, kb);
+        if (!mbar_wait(v_empty, (j & 1) ^ 1, abort_flag)) { ATT_FAIL(ERR_WAIT_SMEM_EMPTY); break; }
+        mbar_expect_tx(v_full, ATT_TILE_BYTES);
+        tma_load_3d(sV, &tv, v_full, 0, h, kb);
+        tma_load_3d(sV + 16384, &tv, v_full, 64, h, kb);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t IDESC_S = make_idesc(1, 1, 0, 0, 128, 128);
+      constexpr uint32_t IDESC_PV = make_idesc(1, 1, 0, 1, 128, 128);
+      const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV);
+      bool ok = mbar_wait(q_full, 0, abort_flag);
+      if (!ok) ATT_FAIL(ERR_WAIT_TMA_FULL);
+      for (int j = 0; ok && j < nb; ++j) {
+        if (!mbar_wait(k_full, j & 1, abort_flag)) { ATT_FAIL(ERR_WAIT_TMA_FULL); break; }
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
+          umma_f16(tmem_S, make_smem_desc(aQ + off, 16, 1024), make_smem_desc(aK + off, 16, 1024), IDESC_S, k != 0);
+        }
+        umma_commit(k_empty);
+        umma_commit(s_full);
+        if (!mbar_wait(p_ready, j & 1, abort_flag)) { ATT_FAIL(ERR_WAIT_TMEM_EMPTY); break; }
+        if (!mbar_wait(v_full, j & 1, abort_flag)) { ATT_FAIL(ERR_WAIT_TMA_FULL); break; }
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k)                          // 16 keys per MMA: 8 TMEM columns of packed bf16
+          umma_f16_ts(tmem_O, tmem_S + k * 8, make_smem_desc(aV + k * 2048, 16384, 1024), IDESC_PV, (j | k) != 0);
+        umma_commit(v_empty);
+        umma_commit(o_done);
+      }
+    }
+  } else {
+    const int sub = warp & 3;                                // TMEM sub-partition of this warp
+    const int r = sub * 32 + lane;
+    const int i = q0 + r;
+    const bool row_ok = i < p.T;
+    const int lo_i = row_ok ? max(p.doc_start[i], i - p.window) : 0;
+    const int hi_i = row_ok ? i : -1;
+    const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
+    const float c = p.scale_log2;
+    float m_used = -INFINITY, l = 0.f;
+    bool alive = true;
+    for (int j = 0; j < nb; ++j) {
+      const int kb = kv_lo + j * 128;
+      if (!mbar_wait(s_full, j & 1, abort_flag)) { ATT_FAIL(ERR_WAIT_TMEM_FULL); alive = false; break; }
+      tc_fence_after();
+      const bool full = kb >= lo_i && kb + 127 <= hi_i;      // no masking needed for this row in this block
+      const unsigned span = (unsigned)(hi_i - lo_i);
+      const bool any_vis = hi_i >= lo_i;
+      // the whole 128-column row of S in registers: four loads in flight, one wait
+      uint32_t v0[32], v1[32], v2[32], v3[32];
+      tmem_ld32(tmem_S + lane_off, v0);
+      tmem_ld32(tmem_S + lane_off + 32, v1);
+      tmem_ld32(tmem_S + lane_off + 64, v2);
+      tmem_ld32(tmem_S + lane_off + 96, v3);
+      tmem_ld_wait();
+      float mx = -INFINITY;
+      if (full) {
+#pragma unroll
+        for (int t = 0; t < 32; ++t)
+          mx = fmaxf(mx, fmaxf(fmaxf(__uint_as_float(v0[t]), __uint_as_float(v1[t])), fmaxf(__uint_as_float(v2[t]), __uint_as_float(v3[t]))));
+      } else {
+        const int col0 = kb - lo_i;
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          if (!((unsigned)(col0 + t) <= span && any_vis)) v0[t] = 0xff800000u;          // -inf: exp2 gives exactly 0
+          if (!((unsigned)(col0 + 32 + t) <= span && any_vis)) v1[t] = 0xff800000u;
+          if (!((unsigned)(col0 + 64 + t) <= span && any_vis)) v2[t] = 0xff800000u;
+          if (!((unsigned)(col0 + 96 + t) <= span && any_vis)) v3[t] = 0xff800000u;
+          mx = fmaxf(mx, fmaxf(fmaxf(__uint_as_float(v0[t]), __uint_as_float(v1[t])), fmaxf(__uint_as_float(v2[t]), __uint_as_float(v3[t]))));
+        }
+      }
+      mx *= c;
+      float alpha = 1.f;
+      if (mx > m_used + 8.f || (m_used == -INFINITY && mx > -INFINITY)) {
+        alpha = (m_used == -INFINITY) ? 0.f : exp2f(m_used - mx);
+        m_used = mx;
+        l *= alpha;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {  // rescale the accumulator rows of this warp
+        if (!mbar_wait(o_done, (j - 1) & 1, abort_flag)) { ATT_FAIL(ERR_WAIT_TMEM_FULL); alive = false; break; }
+        tc_fence_after();
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t v[32];
+          tmem_ld32(tmem_O + lane_off + cc * 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int t = 0; t < 32; ++t) v[t] = __float_as_uint(__uint_as_float(v[t]) * alpha);
+          tmem_st32(tmem_O + lane_off + cc * 32, v);
+        }
+      }
+      // rows that have seen no key yet keep m_used = -inf: use 0 so that exp2(-inf - 0) = 0 and not NaN
+      const float mneg = (m_used == -INFINITY) ? 0.f : -m_used;
+      auto emit = [&](const uint32_t (&vv)[32], int cc) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+          const float p0 = exp2f(fmaf(__uint_as_float(vv[2 * t]), c, mneg));
+          const float p1 = exp2f(fmaf(__uint_as_float(vv[2 * t + 1]), c, mneg));
+          l += p0 + p1;
+          pk[t] = pack_bf16x2(p0, p1);
+        }
+        tmem_st16(tmem_S + lane_off + cc * 16, pk);
+      };
+      emit(v0, 0);
+      emit(v1, 1);
+      emit(v2, 2);
+      emit(v3, 3);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_ready);
+    }
+    if (alive) {
+      if (!mbar_wait(o_done, (nb - 1) & 1, abort_flag)) {
+        ATT_FAIL(ERR_WAIT_TMEM_FULL);
+      } else {
+        tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        __nv_bfloat16* orow = p.out + ((size_t)i * p.H + h) * 128;
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t v[32];
+          tmem_ld32(tmem_O + lane_off + cc * 32, v);
+          tmem_ld_wait();
+          if (row_ok) {
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              uint4 w;
+              w.x = pack_bf16x2(__uint_as_float(v[8 * t]) * inv, __uint_as_float(v[8 * t + 1]) * inv);
+              w.y = pack_bf16x2(__uint_as_float(v[8 * t + 2]) * inv, __uint_as_float(v[8 * t + 3]) * inv);
+              w.z = pack_bf16x2(__uint_as_float(v[8 * t + 4]) * inv, __uint_as_float(v[8 * t + 5]) * inv);
+              w.w = pack_bf16x2(__uint_as_float(v[8 * t + 6]) * inv, __uint_as_float(v[8 * t + 7]) * inv);
+              *reinterpret_cast<uint4*>(orow + cc * 32 + t * 8) = w;
+            }
+          }
+        }
+        if (row_ok) p.lse[(size_t)h * p.T + i] = (m_used + log2f(l)) * 0.6931471805599453f;
+      }
+    }
+  }
+#undef ATT_FAIL
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    if (*abort_flag != 0) {
+      const long long t0 = clock64();
+      while (clock64() - t0 < 2000000LL) { __nanosleep(1000); }
+    }
+    tc_fence_after();
+    tmem_dealloc(tmem_S, 256);
+  }
+}
+
+// ---- host ---------------------------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn attn_encode() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// [T, H, 128] bf16 (token stride `row_stride` elements) as {d, head, token} with boxes of 64 dims x 1 head x 128 tokens
+static int attn_map(CUtensorMap* m, const void* ptr, int T, int H, long long row_stride) {
+  EncodeTiledFn enc = attn_encode();
+  if (!enc) return -1;
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (row_stride * 2) % 16) return -2;
+  cuuint64_t dims[3] = {128, (cuuint64_t)H, (cuuint64_t)T};
+  cuuint64_t strides[2] = {256, (cuuint64_t)row_stride * 2};
+  cuuint32_t box[3] = {64, 1, 128};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -100 - (int)r;
+}
+
+}  // namespace mng
+
+using namespace mng;
+
+extern "C" int mng_attn_fwd(const void* q, const void* k, const void* v, const int* doc_start, void* out, float* lse, int T,
+                            int H, long long row_stride, int window, float scale, void* stream, uint32_t* status) {
+  if (T <= 0 || H <= 0) return 0;
+  static thread_local bool ctx_bound = false;
+  if (!ctx_bound) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaSetDevice(dev);
+    cudaFree(nullptr);
+    ctx_bound = true;
+  }
+  CUtensorMap tq, tk, tv;
+  int rc;
+  if ((rc = attn_map(&tq, q, T, H, row_stride))) return rc;
+  if ((rc = attn_map(&tk, k, T, H, row_stride))) return rc - 1000;
+  if ((rc = attn_map(&tv, v, T, H, row_stride))) return rc - 2000;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM) != cudaSuccess) return -3;
+    attr = true;
+  }
+  AttnParams p{doc_start, reinterpret_cast<__nv_bfloat16*>(out), lse, T, H, window, scale * 1.4426950408889634f};
+  dim3 grid((T + 127) / 128, H);
+  attn_fwd_kernel<<<grid, ATT_THREADS, ATT_SMEM, (cudaStream_t)stream>>>(tq, tk, tv, p, status);
+  return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}

@@ -462,6 +462,23 @@ void embed_bwd(const Tensor& g, const Tensor& sorted_ids, const Tensor& perm, Te
   g_launches += 1;
 }
 
+std::vector<Tensor> attn_fwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& doc_start, int64_t window,
+                             double scale) {
+  TORCH_CHECK(q.is_cuda() && q.dim() == 3 && q.size(2) == 128 && q.scalar_type() == torch::kBFloat16);
+  TORCH_CHECK(k.sizes() == q.sizes() && v.sizes() == q.sizes() && k.scalar_type() == q.scalar_type() && v.scalar_type() == q.scalar_type());
+  for (const Tensor* t : {&q, &k, &v}) TORCH_CHECK(t->stride(2) == 1 && t->stride(1) == 128 && t->stride(0) == q.stride(0));
+  TORCH_CHECK(doc_start.scalar_type() == torch::kInt32 && doc_start.is_contiguous() && doc_start.numel() == q.size(0));
+  c10::cuda::CUDAGuard guard(q.device());
+  const int64_t T = q.size(0), H = q.size(1);
+  Tensor out = torch::empty({T, H, 128}, q.options());
+  Tensor lse = torch::empty({H, T}, q.options().dtype(torch::kFloat32));
+  check(mng_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), doc_start.data_ptr<int>(), out.data_ptr(), lse.data_ptr<float>(),
+                     (int)T, (int)H, q.stride(0), (int)window, (float)scale, cur_stream(), status_ptr(q)),
+        "mng_attn_fwd");
+  g_launches += 1;
+  return {out, lse};
+}
+
 Tensor status_tensor(const Tensor& like) {
   status_ptr(like);
   return g_status;
@@ -491,6 +508,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_bwd", &embed_bwd);
   m.def("dc_mix_fwd", &dc_mix_fwd);
   m.def("dc_mix_bwd", &dc_mix_bwd);
+  m.def("attn_fwd", &attn_fwd);
   m.def("status_tensor", &status_tensor);
   m.def("launch_count", &launch_count);
 }

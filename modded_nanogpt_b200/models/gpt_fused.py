@@ -81,6 +81,13 @@ def forward_fused(m, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, big
     x = lincomb([Term(x), Term(x_prev, gate=g, col=0)])
     x = x0 = fused.rms_norm(x)
 
+    # document starts for the attention kernel: once per forward for the plain and the doubled (paired-head) packing
+    ds1 = ds2 = seq2 = None
+    if fused.ATTN_KERNEL:
+        ds1 = fused.doc_starts(seqlens, T)
+        if any(pl.paired for pl in m.plan):
+            seq2 = 2 * seqlens
+            ds2 = fused.doc_starts(seq2, 2 * T)
     cos_t, sin_t = _rope_tables(m.yarn, 2 * T, x.device)
     cos_p, sin_p = _rope_tables(m.yarn_paired_head, 2 * T, x.device)
 
@@ -133,9 +140,10 @@ def forward_fused(m, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, big
             q, k, v = qkv_post(qkv, ct, st, ve_t, vgate, vadd, H, pl.paired, pl.long_window and not pl.paired)
             if pl.paired:
                 y = ops.attention(q.view(2 * T, H // 2, Dh), k.view(2 * T, H // 2, Dh), v.view(2 * T, H // 2, Dh),
-                                  2 * seqlens, ws[pl.long_window], yarn.attn_scale, 2 * max_len).view(T, H, Dh)
+                                  seq2 if seq2 is not None else 2 * seqlens, ws[pl.long_window], yarn.attn_scale, 2 * max_len,
+                                  ds2).view(T, H, Dh)
             else:
-                y = ops.attention(q, k, v, seqlens, ws[pl.long_window], yarn.attn_scale, max_len)
+                y = ops.attention(q, k, v, seqlens, ws[pl.long_window], yarn.attn_scale, max_len, ds1)
             gt, lay = gate_of(i) if track1 else (None, None)
             if track1 and pl.dc and not pl.paired:
                 o = lay1["dc"]

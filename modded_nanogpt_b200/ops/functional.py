@@ -16,13 +16,16 @@ def rms_norm(x: Tensor) -> Tensor:
     return ref.rms_norm(x)
 
 
-def attention(q: Tensor, k: Tensor, v: Tensor, cu_seqlens: Tensor, window: int, scale: float, max_len: int) -> Tensor:
-    """Causal, document-masked sliding-window attention on packed sequences; q,k,v [T,H,D]."""
+def attention(q: Tensor, k: Tensor, v: Tensor, cu_seqlens: Tensor, window: int, scale: float, max_len: int,
+              doc_start: Tensor | None = None) -> Tensor:
+    """Causal, document-masked sliding-window attention on packed sequences; q,k,v [T,H,D].
+    `doc_start` (int32 [T], first token of each token's document) may be passed by callers that run
+    several layers on the same packing; it is derived from `cu_seqlens` otherwise."""
     if q.is_cuda and q.dtype == torch.bfloat16:
         if use_kernel("attention", q):
             from . import fused
             if fused.attention_supported(q, window):
-                return fused.attention(q, k, v, cu_seqlens, window, scale, max_len)
+                return fused.attention(q, k, v, cu_seqlens, window, scale, max_len, doc_start)
         from .library import flash_attention_varlen
         return flash_attention_varlen(q, k, v, cu_seqlens, window, scale, max_len)
     return ref.attention_varlen(q, k, v, cu_seqlens, window, scale)
