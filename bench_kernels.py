@@ -73,8 +73,8 @@ def build_case(name, T, bn, fused):
         tg, pt = torch.randint(0, V, (T,), device=dev), torch.randint(-1, V, (T,), device=dev)
         w, pw = torch.tensor([1.0, 0.5, 0.25], device=dev), torch.tensor([0.3], device=dev)
         return (lambda: lib.softcap_ce(logits, tg, w, pt, pw, e5, 23.0, 5.0, 7.5, 1.0)), 0, T * V * (3 if e5 else 4)
-    if name.startswith("attn_"):            # attn_{ours|fa2}_{short|long|paired}: packed documents, sliding window
-        _, impl, kind = name.split("_")
+    if name.startswith("attn"):             # attn[bwd]_{ours|fa2}_{short|long|paired}: packed documents, sliding window
+        op, impl, kind = name.split("_")
         Tq, Hh, window = (2 * T, 3, 2 * 640) if kind == "paired" else (T, 6, 640 if kind == "short" else 1408)
         g = torch.Generator(device=dev).manual_seed(0)
         q, k, v = (torch.randn(Tq, Hh, 128, device=dev, generator=g).to(BF) for _ in range(3))
@@ -87,9 +87,21 @@ def build_case(name, T, bn, fused):
         cu[:len(starts)] = starts.int()
         cu = cu.to(dev)
         pos = torch.arange(Tq, device=dev)
-        ds = fused.doc_starts(cu, Tq)
+        bounds = fused.doc_bounds(cu, Tq)
+        ds = bounds[0].contiguous()
         flops = 4 * 128 * Hh * int((pos - torch.maximum(ds.long(), pos - window) + 1).sum())
         max_len = 4096
+        if op == "attnbwd":                 # 5 GEMMs of the same size as the forward's 2
+            lib = fused._C()
+            out, lse = lib.attn_fwd(q, k, v, ds, window, 0.12)
+            dout = torch.randn_like(out)
+            if impl == "ours":
+                de = bounds[1].contiguous()
+                return (lambda: lib.attn_bwd(dout, q, k, v, out, lse, ds, de, window, 0.12)), flops * 5 // 2, 3 * Tq * Hh * 256
+            from flash_attn.flash_attn_interface import _wrapped_flash_attn_varlen_backward as fa_bwd
+            dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+            return (lambda: fa_bwd(dout, q, k, v, out, lse, dq, dk, dv, cu, cu, max_len, max_len, 0.0, 0.12, True, window, 0, 0.0,
+                                   None, False, rng_state=None)), flops * 5 // 2, 3 * Tq * Hh * 256
         if impl == "ours":
             lib = fused._C()
             return (lambda: lib.attn_fwd(q, k, v, ds, window, 0.12)), flops, Tq * Hh * 256
@@ -101,7 +113,8 @@ def build_case(name, T, bn, fused):
 
 CASES = ["gemm_bf16_up", "gemm_bf16_dpre", "gemm_bf16_down", "gemm_bf16_dw", "gemm_fp8_relu2", "gemm_fp8_down", "gemm_bf16_qkv",
          "gemm_bf16_o", "gemm_bf16_o_null", "gemm_bf16_up_null", "gemm_fp8_logits", "gemm_fp8_lmhead_dx", "gemm_fp8_lmhead_dw", "softcap_ce_e5m2", "softcap_ce_bf16",
-         "attn_ours_short", "attn_fa2_short", "attn_ours_long", "attn_fa2_long", "attn_ours_paired", "attn_fa2_paired"]
+         "attn_ours_short", "attn_fa2_short", "attn_ours_long", "attn_fa2_long", "attn_ours_paired", "attn_fa2_paired",
+         "attnbwd_ours_short", "attnbwd_fa2_short", "attnbwd_ours_long", "attnbwd_fa2_long", "attnbwd_ours_paired", "attnbwd_fa2_paired"]
 
 
 def main():

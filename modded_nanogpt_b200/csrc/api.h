@@ -142,6 +142,13 @@ int mng_embed_bwd(const void* g, const long long* sorted_ids, const long long* p
 int mng_attn_fwd(const void* q, const void* k, const void* v, const int* doc_start, void* out, float* lse, int T, int H,
                  long long row_stride, int window, float scale, void* stream, uint32_t* status);
 
+// Backward of the same attention: dq, dk, dv [T, H, 128] bf16 contiguous from q, k, v, the forward's out and lse and
+// the incoming gradient dout (contiguous).  doc_end[i] = first token of the next document.  delta, lse2: [H, T] fp32
+// scratch owned by the caller.  T must be a multiple of 4.
+int mng_attn_bwd(const void* q, const void* k, const void* v, const void* out, const void* dout, const float* lse,
+                 const int* doc_start, const int* doc_end, void* dq, void* dk, void* dv, float* delta, float* lse2, int T,
+                 int H, long long row_stride, int window, float scale, void* stream, uint32_t* status);
+
 // Barrier across ranks on signal pads (bounded wait; sets *status on expiry).
 int mng_peer_barrier(const PeerPtrs* pads, int rank, uint32_t epoch, uint32_t* status, void* stream);
 

@@ -326,3 +326,338 @@ extern "C" int mng_attn_fwd(const void* q, const void* k, const void* v, const i
   attn_fwd_kernel<<<grid, ATT_THREADS, ATT_SMEM, (cudaStream_t)stream>>>(tq, tk, tv, p, status);
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
+
+// =====================================================================================================
+// Backward.  Two launches of one templated kernel, both with the forward's structure (owner tile resident,
+// the other side streamed, everything recomputed from q, k, v, dO and the forward's log-sum-exp):
+//
+//   DKV = true   owner = 128 keys (K, V tiles), stream = query blocks (Q, dO, lse, delta):
+//                S^T = K Q^T, dP^T = V dO^T (lanes = keys), P^T = exp2(S^T c - lse), dS^T = P^T (dP^T - delta) scale,
+//                dV += P^T dO, dK += dS^T Q          (P^T, dS^T as bf16 A operands read from TMEM)
+//   DKV = false  owner = 128 queries (Q, dO tiles), stream = key blocks (K, V):
+//                S = Q K^T, dP = dO V^T (lanes = queries), dS = P (dP - delta) scale, dQ += dS K
+//
+// The score tiles are computed twice (once per launch) so that no gradient needs atomics or a second pass:
+// each output row is written exactly once.  TMEM: S [0,128), dP [128,256), accumulators [256,384), [384,512).
+// The bf16 operands alias the fp32 tiles they were computed from: columns [0,32) and [64,96) of each
+// region (each half of the eight element-wise warps stays inside its own 64 columns).  320 threads: warp 0 TMA,
+// warp 1 MMA, warps 2-9 element-wise (warp w: TMEM lanes (w%4)*32.., columns ((w-2)/4)*64..).
+// delta[h,i] = sum_d dO[i,h,d] O[i,h,d] and lse2 = lse * log2(e) come from a small pre-kernel.
+namespace mng {
+
+constexpr int ATB_THREADS = 320;
+constexpr int ATB_VEC_BYTES = 2 * 2 * 512;           // 2 stages x (lse2, delta) x 128 floats
+constexpr int ATB_SMEM = 6 * ATT_TILE_BYTES + ATB_VEC_BYTES + 1024 + 1024;
+
+struct AttnBwdParams {
+  const int* doc_start;     // [T]
+  const int* doc_end;       // [T] first token of the next document
+  const float* lse2;        // [H, T] log-sum-exp in log2 units
+  const float* delta;       // [H, T]
+  __nv_bfloat16* out1;      // DKV: dK, else dQ     [T, H, 128]
+  __nv_bfloat16* out2;      // DKV: dV
+  int T, H, window;
+  float scale_log2, scale;
+};
+
+__global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
+                                     const float* __restrict__ lse, float* __restrict__ delta, float* __restrict__ lse2, int T,
+                                     int H) {
+  const long long row = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 4;      // (token, head) pair: 16 lanes each
+  const int part = threadIdx.x & 15;
+  float acc = 0.f;
+  if (row < (long long)T * H) {
+    const uint4 a = *reinterpret_cast<const uint4*>(o + row * 128 + part * 8);
+    const uint4 b = *reinterpret_cast<const uint4*>(dout + row * 128 + part * 8);
+    const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+    const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&b);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float2 x = __bfloat1622float2(a2[t]), y = __bfloat1622float2(b2[t]);
+      acc += x.x * y.x + x.y * y.y;
+    }
+  }
+#pragma unroll
+  for (int s = 8; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
+  if (part == 0 && row < (long long)T * H) {
+    const int i = (int)(row / H), h = (int)(row % H);
+    delta[(size_t)h * T + i] = acc;
+    lse2[(size_t)h * T + i] = lse[(size_t)h * T + i] * 1.4426950408889634f;
+  }
+}
+
+__device__ __forceinline__ void attn_bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               :
+               : "r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+template <bool DKV>
+__global__ void __launch_bounds__(ATB_THREADS, 1)
+attn_bwd_kernel(const __grid_constant__ CUtensorMap tx1, const __grid_constant__ CUtensorMap tx2,
+                const __grid_constant__ CUtensorMap ty1, const __grid_constant__ CUtensorMap ty2, AttnBwdParams p,
+                uint32_t* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sX1 = smem;
+  uint8_t* sX2 = smem + ATT_TILE_BYTES;
+  uint8_t* sY = smem + 2 * ATT_TILE_BYTES;                  // stage s: Y1 at sY + s*2*TILE, Y2 right after
+  float* vec = reinterpret_cast<float*>(smem + 6 * ATT_TILE_BYTES);   // stage s: lse2 at vec + s*256, delta at +128
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * ATT_TILE_BYTES + ATB_VEC_BYTES);
+  uint64_t* x_full = bars + 0;
+  uint64_t* y_full = bars + 1;       // [2]
+  uint64_t* y_empty = bars + 3;      // [2]
+  uint64_t* sdp_full = bars + 5;
+  uint64_t* pds_ready = bars + 6;
+  uint64_t* acc_done = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  volatile uint32_t* abort_flag = tmem_slot + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y;
+  const int r0 = (DKV ? (int)blockIdx.x : (int)(gridDim.x - 1 - blockIdx.x)) * 128;    // owner tile start
+  const int r_last = min(r0 + 127, p.T - 1);
+  int s0, nb;                                                // stream start row and number of 128-row blocks
+  if (DKV) {
+    s0 = r0;
+    const int i_max = min(min(r_last + p.window, p.doc_end[r_last] - 1), p.T - 1);
+    nb = (i_max - s0) / 128 + 1;
+  } else {
+    s0 = max(p.doc_start[r0], r0 - p.window);
+    nb = (r_last - s0) / 128 + 1;
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(x_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&y_full[s], 1);
+      mbar_init(&y_empty[s], 1);
+    }
+    mbar_init(sdp_full, 1);
+    mbar_init(pds_ready, 8);
+    mbar_init(acc_done, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+    tma_prefetch_desc(&tx1);
+    tma_prefetch_desc(&tx2);
+    tma_prefetch_desc(&ty1);
+    tma_prefetch_desc(&ty2);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tm = *tmem_slot;
+  const uint32_t tm_S = tm, tm_dP = tm + 128, tm_A1 = tm + 256, tm_A2 = tm + 384;
+#define ATB_FAIL(code)                                                          \
+  do {                                                                          \
+    if (*abort_flag == 0) { *abort_flag = (code); atomicCAS(status, 0u, (code)); } \
+  } while (0)
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_expect_tx(x_full, 2 * ATT_TILE_BYTES);
+      tma_load_3d(sX1, &tx1, x_full, 0, h, r0);
+      tma_load_3d(sX1 + 16384, &tx1, x_full, 64, h, r0);
+      tma_load_3d(sX2, &tx2, x_full, 0, h, r0);
+      tma_load_3d(sX2 + 16384, &tx2, x_full, 64, h, r0);
+      for (int n = 0; n < nb; ++n) {
+        const int st = n & 1, srow = s0 + n * 128;
+        if (!mbar_wait(&y_empty[st], ((n >> 1) & 1) ^ 1, abort_flag)) { ATB_FAIL(ERR_WAIT_SMEM_EMPTY); break; }
+        uint8_t* y1 = sY + st * 2 * ATT_TILE_BYTES;
+        uint8_t* y2 = y1 + ATT_TILE_BYTES;
+        uint32_t bytes = 2 * ATT_TILE_BYTES;
+        const int cnt = min(128, p.T - srow);
+        if (DKV) bytes += 2u * cnt * 4u;
+        mbar_expect_tx(&y_full[st], bytes);
+        tma_load_3d(y1, &ty1, &y_full[st], 0, h, srow);
+        tma_load_3d(y1 + 16384, &ty1, &y_full[st], 64, h, srow);
+        tma_load_3d(y2, &ty2, &y_full[st], 0, h, srow);
+        tma_load_3d(y2 + 16384, &ty2, &y_full[st], 64, h, srow);
+        if (DKV) {
+          attn_bulk_load(vec + st * 256, p.lse2 + (size_t)h * p.T + srow, cnt * 4, &y_full[st]);
+          attn_bulk_load(vec + st * 256 + 128, p.delta + (size_t)h * p.T + srow, cnt * 4, &y_full[st]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t IDESC_SS = make_idesc(1, 1, 0, 0, 128, 128);
+      constexpr uint32_t IDESC_TS = make_idesc(1, 1, 0, 1, 128, 128);
+      const uint32_t aX1 = smem_u32(sX1), aX2 = smem_u32(sX2);
+      bool ok = mbar_wait(x_full, 0, abort_flag);
+      if (!ok) ATB_FAIL(ERR_WAIT_TMA_FULL);
+      int n = 0;
+      for (; ok && n < nb; ++n) {
+        const int st = n & 1;
+        const uint32_t aY1 = smem_u32(sY + st * 2 * ATT_TILE_BYTES), aY2 = aY1 + ATT_TILE_BYTES;
+        if (!mbar_wait(&y_full[st], (n >> 1) & 1, abort_flag)) { ATB_FAIL(ERR_WAIT_TMA_FULL); ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
+          umma_f16(tm_S, make_smem_desc(aX1 + off, 16, 1024), make_smem_desc(aY1 + off, 16, 1024), IDESC_SS, k != 0);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
+          umma_f16(tm_dP, make_smem_desc(aX2 + off, 16, 1024), make_smem_desc(aY2 + off, 16, 1024), IDESC_SS, k != 0);
+        }
+        umma_commit(sdp_full);
+        if (!mbar_wait(pds_ready, n & 1, abort_flag)) { ATB_FAIL(ERR_WAIT_TMEM_EMPTY); ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {                        // 16 stream rows per MMA: 8 TMEM columns of packed bf16
+          const uint32_t acol = (k < 4) ? k * 8 : 64 + (k - 4) * 8;
+          if (DKV) {
+            umma_f16_ts(tm_A2, tm_S + acol, make_smem_desc(aY2 + k * 2048, 16384, 1024), IDESC_TS, (n | k) != 0);   // dV += P^T dO
+            umma_f16_ts(tm_A1, tm_dP + acol, make_smem_desc(aY1 + k * 2048, 16384, 1024), IDESC_TS, (n | k) != 0);  // dK += dS^T Q
+          } else {
+            umma_f16_ts(tm_A1, tm_dP + acol, make_smem_desc(aY1 + k * 2048, 16384, 1024), IDESC_TS, (n | k) != 0);  // dQ += dS K
+          }
+        }
+        umma_commit(&y_empty[st]);
+      }
+      if (ok) umma_commit(acc_done);
+    }
+  } else {
+    const int sub = warp & 3, half = (warp - 2) >> 2;
+    const int r = sub * 32 + lane;
+    const int g = r0 + r;                                    // owner row: a key (DKV) or a query
+    const bool row_ok = g < p.T;
+    int lo, hi;                                              // visible stream rows for this owner row
+    float my_lse2 = 0.f, my_delta = 0.f;
+    if (DKV) {
+      lo = g;
+      hi = row_ok ? min(min(g + p.window, p.doc_end[g] - 1), p.T - 1) : -1;
+    } else {
+      lo = row_ok ? max(p.doc_start[g], g - p.window) : 0;
+      hi = row_ok ? g : -1;
+      if (row_ok) {
+        my_lse2 = p.lse2[(size_t)h * p.T + g];
+        my_delta = p.delta[(size_t)h * p.T + g];
+      }
+    }
+    const bool any_vis = hi >= lo;
+    const unsigned span = (unsigned)(hi - lo);
+    const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
+    const float c = p.scale_log2, sc = p.scale;
+    bool alive = true;
+    for (int n = 0; n < nb; ++n) {
+      const int st = n & 1, srow = s0 + n * 128;
+      if (!mbar_wait(sdp_full, n & 1, abort_flag)) { ATB_FAIL(ERR_WAIT_TMEM_FULL); alive = false; break; }
+      tc_fence_after();
+      const float* vl = vec + st * 256;
+      const float* vd = vl + 128;
+#pragma unroll 1
+      for (int cc = half * 2; cc < half * 2 + 2; ++cc) {
+        uint32_t s[32], d[32];
+        tmem_ld32(tm_S + lane_off + cc * 32, s);
+        tmem_ld32(tm_dP + lane_off + cc * 32, d);
+        tmem_ld_wait();
+        uint32_t pk_p[16], pk_ds[16];
+        const int col0 = srow + cc * 32 - lo;
+#pragma unroll
+        for (int t = 0; t < 32; t += 2) {
+          float pv[2], dv[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const float l2 = DKV ? vl[cc * 32 + t + u] : my_lse2;
+            const float dl = DKV ? vd[cc * 32 + t + u] : my_delta;
+            const bool vis = any_vis && (unsigned)(col0 + t + u) <= span;
+            const float pe = exp2f(fmaf(__uint_as_float(s[t + u]), c, -l2));
+            pv[u] = vis ? pe : 0.f;
+            dv[u] = vis ? pe * (__uint_as_float(d[t + u]) - dl) * sc : 0.f;
+          }
+          pk_p[t >> 1] = pack_bf16x2(pv[0], pv[1]);
+          pk_ds[t >> 1] = pack_bf16x2(dv[0], dv[1]);
+        }
+        const uint32_t dst = lane_off + half * 64 + (cc & 1) * 16;
+        if (DKV) tmem_st16(tm_S + dst, pk_p);
+        tmem_st16(tm_dP + dst, pk_ds);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pds_ready);
+    }
+    if (alive) {
+      if (!mbar_wait(acc_done, 0, abort_flag)) {
+        ATB_FAIL(ERR_WAIT_TMEM_FULL);
+      } else {
+        tc_fence_after();
+#pragma unroll 1
+        for (int which = 0; which < (DKV ? 2 : 1); ++which) {
+          __nv_bfloat16* orow = (which == 0 ? p.out1 : p.out2) + ((size_t)g * p.H + h) * 128 + half * 64;
+#pragma unroll 1
+          for (int cc = 0; cc < 2; ++cc) {
+            uint32_t v[32];
+            tmem_ld32((which == 0 ? tm_A1 : tm_A2) + lane_off + half * 64 + cc * 32, v);
+            tmem_ld_wait();
+            if (row_ok) {
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                uint4 w;
+                w.x = pack_bf16x2(__uint_as_float(v[8 * t]), __uint_as_float(v[8 * t + 1]));
+                w.y = pack_bf16x2(__uint_as_float(v[8 * t + 2]), __uint_as_float(v[8 * t + 3]));
+                w.z = pack_bf16x2(__uint_as_float(v[8 * t + 4]), __uint_as_float(v[8 * t + 5]));
+                w.w = pack_bf16x2(__uint_as_float(v[8 * t + 6]), __uint_as_float(v[8 * t + 7]));
+                *reinterpret_cast<uint4*>(orow + cc * 32 + t * 8) = w;
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+#undef ATB_FAIL
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    if (*abort_flag != 0) {
+      const long long t0 = clock64();
+      while (clock64() - t0 < 2000000LL) { __nanosleep(1000); }
+    }
+    tc_fence_after();
+    tmem_dealloc(tm, 512);
+  }
+}
+
+}  // namespace mng
+
+extern "C" int mng_attn_bwd(const void* q, const void* k, const void* v, const void* out, const void* dout, const float* lse,
+                            const int* doc_start, const int* doc_end, void* dq, void* dk, void* dv, float* delta, float* lse2,
+                            int T, int H, long long row_stride, int window, float scale, void* stream, uint32_t* status) {
+  if (T <= 0 || H <= 0) return 0;
+  if (T % 4) return -5;                                    // rows of the [H, T] vectors must stay 16-byte aligned
+  CUtensorMap tq, tk, tv, tdo;
+  int rc;
+  if ((rc = attn_map(&tq, q, T, H, row_stride))) return rc;
+  if ((rc = attn_map(&tk, k, T, H, row_stride))) return rc - 1000;
+  if ((rc = attn_map(&tv, v, T, H, row_stride))) return rc - 2000;
+  if ((rc = attn_map(&tdo, dout, T, H, (long long)H * 128))) return rc - 3000;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(attn_bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ATB_SMEM) != cudaSuccess ||
+        cudaFuncSetAttribute(attn_bwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ATB_SMEM) != cudaSuccess)
+      return -3;
+    attr = true;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  const long long rows = (long long)T * H;
+  attn_bwd_prep_kernel<<<(unsigned)((rows * 16 + 255) / 256), 256, 0, st>>>(
+      reinterpret_cast<const __nv_bfloat16*>(out), reinterpret_cast<const __nv_bfloat16*>(dout), lse, delta, lse2, T, H);
+  const float c = scale * 1.4426950408889634f;
+  dim3 grid((T + 127) / 128, H);
+  AttnBwdParams pa{doc_start, doc_end, lse2, delta, reinterpret_cast<__nv_bfloat16*>(dk), reinterpret_cast<__nv_bfloat16*>(dv),
+                   T, H, window, c, scale};
+  attn_bwd_kernel<true><<<grid, ATB_THREADS, ATB_SMEM, st>>>(tk, tv, tq, tdo, pa, status);
+  AttnBwdParams pb{doc_start, doc_end, lse2, delta, reinterpret_cast<__nv_bfloat16*>(dq), nullptr, T, H, window, c, scale};
+  attn_bwd_kernel<false><<<grid, ATB_THREADS, ATB_SMEM, st>>>(tq, tdo, tk, tv, pb, status);
+  return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}

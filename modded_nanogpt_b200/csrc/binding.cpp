@@ -479,6 +479,30 @@ std::vector<Tensor> attn_fwd(const Tensor& q, const Tensor& k, const Tensor& v, 
   return {out, lse};
 }
 
+std::vector<Tensor> attn_bwd(const Tensor& dout, const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& out,
+                             const Tensor& lse, const Tensor& doc_start, const Tensor& doc_end, int64_t window, double scale) {
+  TORCH_CHECK(q.is_cuda() && q.dim() == 3 && q.size(2) == 128 && q.scalar_type() == torch::kBFloat16);
+  for (const Tensor* t : {&q, &k, &v})
+    TORCH_CHECK(t->sizes() == q.sizes() && t->stride(2) == 1 && t->stride(1) == 128 && t->stride(0) == q.stride(0));
+  TORCH_CHECK(out.is_contiguous() && dout.is_contiguous() && out.sizes() == q.sizes() && dout.sizes() == q.sizes());
+  TORCH_CHECK(dout.scalar_type() == torch::kBFloat16 && out.scalar_type() == torch::kBFloat16);
+  const int64_t T = q.size(0), H = q.size(1);
+  TORCH_CHECK(lse.scalar_type() == torch::kFloat32 && lse.is_contiguous() && lse.size(0) == H && lse.size(1) == T);
+  TORCH_CHECK(doc_start.scalar_type() == torch::kInt32 && doc_start.is_contiguous() && doc_start.numel() == T);
+  TORCH_CHECK(doc_end.scalar_type() == torch::kInt32 && doc_end.is_contiguous() && doc_end.numel() == T);
+  c10::cuda::CUDAGuard guard(q.device());
+  Tensor dq = torch::empty({T, H, 128}, q.options()), dk = torch::empty({T, H, 128}, q.options()),
+         dv = torch::empty({T, H, 128}, q.options());
+  Tensor scratch = torch::empty({2, H, T}, q.options().dtype(torch::kFloat32));
+  check(mng_attn_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), dout.data_ptr(), lse.data_ptr<float>(),
+                     doc_start.data_ptr<int>(), doc_end.data_ptr<int>(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+                     scratch.data_ptr<float>(), scratch.data_ptr<float>() + H * T, (int)T, (int)H, q.stride(0), (int)window,
+                     (float)scale, cur_stream(), status_ptr(q)),
+        "mng_attn_bwd");
+  g_launches += 3;
+  return {dq, dk, dv};
+}
+
 Tensor status_tensor(const Tensor& like) {
   status_ptr(like);
   return g_status;
@@ -509,6 +533,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dc_mix_fwd", &dc_mix_fwd);
   m.def("dc_mix_bwd", &dc_mix_bwd);
   m.def("attn_fwd", &attn_fwd);
+  m.def("attn_bwd", &attn_bwd);
   m.def("status_tensor", &status_tensor);
   m.def("launch_count", &launch_count);
 }

@@ -84,10 +84,10 @@ def forward_fused(m, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, big
     # document starts for the attention kernel: once per forward for the plain and the doubled (paired-head) packing
     ds1 = ds2 = seq2 = None
     if fused.ATTN_KERNEL:
-        ds1 = fused.doc_starts(seqlens, T)
+        ds1 = fused.doc_bounds(seqlens, T)
         if any(pl.paired for pl in m.plan):
             seq2 = 2 * seqlens
-            ds2 = fused.doc_starts(seq2, 2 * T)
+            ds2 = fused.doc_bounds(seq2, 2 * T)
     cos_t, sin_t = _rope_tables(m.yarn, 2 * T, x.device)
     cos_p, sin_p = _rope_tables(m.yarn_paired_head, 2 * T, x.device)
 

@@ -19,8 +19,8 @@ def rms_norm(x: Tensor) -> Tensor:
 def attention(q: Tensor, k: Tensor, v: Tensor, cu_seqlens: Tensor, window: int, scale: float, max_len: int,
               doc_start: Tensor | None = None) -> Tensor:
     """Causal, document-masked sliding-window attention on packed sequences; q,k,v [T,H,D].
-    `doc_start` (int32 [T], first token of each token's document) may be passed by callers that run
-    several layers on the same packing; it is derived from `cu_seqlens` otherwise."""
+    `doc_start` (int32 [2, T] from `fused.doc_bounds`: first token of each token's document and of the next
+    one) may be passed by callers that run several layers on the same packing."""
     if q.is_cuda and q.dtype == torch.bfloat16:
         if use_kernel("attention", q):
             from . import fused

@@ -286,35 +286,45 @@ def softcap_ce(x, w, targets, mtp_weights, prefix_targets, prefix_weight, a, b, 
 # attention / DC: tcgen05 kernels are selected here once available for the shape
 
 
-def doc_starts(cu_seqlens: Tensor, T: int) -> Tensor:
-    """int32 [T]: index of the first token of the document each token belongs to (cu_seqlens is padded with T)."""
+def doc_bounds(cu_seqlens: Tensor, T: int) -> Tensor:
+    """int32 [2, T]: for every token the index of the first token of its document and of the next
+    document (cu_seqlens is padded with T)."""
     pos = torch.arange(T, device=cu_seqlens.device, dtype=cu_seqlens.dtype)
-    return cu_seqlens[torch.searchsorted(cu_seqlens, pos, right=True) - 1].to(torch.int32)
+    nxt = torch.searchsorted(cu_seqlens, pos, right=True)
+    return torch.stack([cu_seqlens[nxt - 1], cu_seqlens[nxt.clamp_(max=cu_seqlens.numel() - 1)]]).to(torch.int32)
+
+
+def doc_starts(cu_seqlens: Tensor, T: int) -> Tensor:
+    return doc_bounds(cu_seqlens, T)[0]
 
 
 class _Attention(torch.autograd.Function):
-    """Forward on the tcgen05 kernel (csrc/attn_sm100.cu); backward by FlashAttention-2's varlen kernel
-    (library call), which takes the forward's output and log-sum-exp."""
+    """Forward and backward on the tcgen05 kernels (csrc/attn_sm100.cu).  `MNG_ATTN_BWD=fa2` routes the
+    backward to FlashAttention-2's varlen kernel (library call) with the forward's output and log-sum-exp."""
 
     @staticmethod
-    def forward(ctx, q, k, v, cu_seqlens, doc_start, window, scale, max_len):
+    def forward(ctx, q, k, v, cu_seqlens, bounds, window, scale, max_len):
         q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
-        out, lse = _C().attn_fwd(q, k, v, doc_start, window, scale)
-        ctx.save_for_backward(q, k, v, out, lse, cu_seqlens)
+        out, lse = _C().attn_fwd(q, k, v, bounds[0], window, scale)
+        ctx.save_for_backward(q, k, v, out, lse, cu_seqlens, bounds)
         ctx.cfg = (window, scale, max_len)
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        from flash_attn.flash_attn_interface import _wrapped_flash_attn_varlen_backward as fa_bwd
-        q, k, v, out, lse, cu = ctx.saved_tensors
+        q, k, v, out, lse, cu, bounds = ctx.saved_tensors
         window, scale, max_len = ctx.cfg
-        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-        fa_bwd(dout.contiguous(), q, k, v, out, lse, dq, dk, dv, cu, cu, max_len, max_len, 0.0, scale, True, window, 0, 0.0,
-               None, False, rng_state=None)
+        if ATTN_BWD_KERNEL and q.shape[0] % 4 == 0:
+            dq, dk, dv = _C().attn_bwd(dout.contiguous(), q, k, v, out, lse, bounds[0], bounds[1], window, scale)
+        else:
+            from flash_attn.flash_attn_interface import _wrapped_flash_attn_varlen_backward as fa_bwd
+            dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+            fa_bwd(dout.contiguous(), q, k, v, out, lse, dq, dk, dv, cu, cu, max_len, max_len, 0.0, scale, True, window, 0,
+                   0.0, None, False, rng_state=None)
         return dq, dk, dv, None, None, None, None, None
 
 
+ATTN_BWD_KERNEL = os.environ.get("MNG_ATTN_BWD", "own") != "fa2"
 ATTN_KERNEL = os.environ.get("MNG_ATTN", "1") != "0"
 
 
@@ -323,10 +333,11 @@ def attention_supported(q: Tensor, window: int) -> bool:
 
 
 def attention(q: Tensor, k: Tensor, v: Tensor, cu_seqlens: Tensor, window: int, scale: float, max_len: int,
-              doc_start: Tensor | None = None) -> Tensor:
-    if doc_start is None:
-        doc_start = doc_starts(cu_seqlens, q.shape[0])
-    return _Attention.apply(q, k, v, cu_seqlens, doc_start, int(window), float(scale), int(max_len))
+              bounds: Tensor | None = None) -> Tensor:
+    """`bounds` = doc_bounds(cu_seqlens, T), computed here when the caller does not share one across layers."""
+    if bounds is None:
+        bounds = doc_bounds(cu_seqlens, q.shape[0])
+    return _Attention.apply(q, k, v, cu_seqlens, bounds, int(window), float(scale), int(max_len))
 
 
 def dc_supported(q: Tensor, window: int) -> bool:

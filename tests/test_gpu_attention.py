@@ -33,12 +33,32 @@ def test_attention_forward_matches_reference(T, H, docs, window):
     assert torch.equal(out, fused.attention(q, k, v, cu, window, scale, 2048))
 
 
+@pytest.mark.parametrize("T,H,docs,window", [(256, 1, [0], 1024), (1024, 6, [0, 300, 650, 800], 384), (1152, 3, [0, 1, 130, 1000], 128),
+                                             (2048, 2, [0, 5, 700, 1500, 2047], 640)])
+def test_attention_backward_matches_reference(T, H, docs, window):
+    from modded_nanogpt_b200.ops import fused
+    from modded_nanogpt_b200.ops import reference as ref
+    q, k, v, cu = _case(T, H, docs, seed=5)
+    w = torch.randn(T, H, 128, device="cuda")
+    got, want = [], []
+    for impl, dst in ((fused.attention, got), (ref.attention_varlen, want)):
+        qq, kk, vv = (t.clone().requires_grad_(True) for t in (q, k, v))
+        o = impl(qq, kk, vv, cu, window, 0.12, 2048) if impl is fused.attention else impl(qq, kk, vv, cu, window, 0.12)
+        (o.float() * w).sum().backward()
+        dst.extend([qq.grad, kk.grad, vv.grad])
+    fused.check_status()
+    for a, b, n in zip(got, want, ("dq", "dk", "dv")):
+        assert _rel(a, b) < 2e-2, (n, _rel(a, b))
+
+
 def test_attention_lse_and_backward_match_flash_attn():
     from flash_attn import flash_attn_varlen_func
     from modded_nanogpt_b200.ops import fused
     T, H, window, scale = 2048, 6, 384, 0.1
     q, k, v, cu = _case(T, H, [0, 300, 650, 1800], seed=3)
     ds = fused.doc_starts(cu, T)
+    assert torch.equal(fused.doc_bounds(cu, T)[1], torch.tensor([300, 650, 1800, T], device="cuda", dtype=torch.int32)[
+        torch.bucketize(torch.arange(T, device="cuda"), torch.tensor([300, 650, 1800], device="cuda"), right=True)])
     out, lse = fused._C().attn_fwd(q, k, v, ds, window, scale)
     qf, kf, vf = q.float(), k.float(), v.float()
     i = torch.arange(T, device="cuda")

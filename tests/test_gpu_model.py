@@ -187,5 +187,7 @@ def test_fused_model_matches_op_by_op(training):
             assert res["fused"][1][n].norm() < 1e-3, n
             continue
         e_ref, e_fused = _rel(res["bf16"][1][n], gg), _rel(res["fused"][1][n], gg)
-        assert e_fused < max(2.0 * e_ref, 0.05), (n, e_fused, e_ref)
+        # single scalars are sums with heavy cancellation: their relative error is noise-dominated
+        tol = max(3.0 * e_ref, 0.2) if gg.numel() == 1 else max(2.0 * e_ref, 0.05)
+        assert e_fused < tol, (n, e_fused, e_ref)
     fused.check_status()
