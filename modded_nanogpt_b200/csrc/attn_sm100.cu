@@ -115,7 +115,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
     if (lane == 0) {
       constexpr uint32_t IDESC_S = make_idesc(1, 1, 0, 0, 128, 128);
       constexpr uint32_t IDESC_PV = make_idesc(1, 1, 0, 1, 128, 128);
-      const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV);
+      // descriptors differ only in the 14-bit start-address field (address >> 4): build once, then add offsets
+      const uint64_t dQ = make_smem_desc(smem_u32(sQ), 16, 1024), dK = make_smem_desc(smem_u32(sK), 16, 1024);
+      const uint64_t dV = make_smem_desc(smem_u32(sV), 16384, 1024);
       bool ok = mbar_wait(q_full, 0, abort_flag);
       if (!ok) ATT_FAIL(ERR_WAIT_TMA_FULL);
       for (int j = 0; ok && j < nb; ++j) {
@@ -123,8 +125,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
-          umma_f16(tmem_S, make_smem_desc(aQ + off, 16, 1024), make_smem_desc(aK + off, 16, 1024), IDESC_S, k != 0);
+          const uint32_t off = ((k >> 2) * 16384 + (k & 3) * 32) >> 4;
+          umma_f16(tmem_S, dQ + off, dK + off, IDESC_S, k != 0);
         }
         umma_commit(k_empty);
         umma_commit(s_full);
@@ -133,7 +135,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < 8; ++k)                          // 16 keys per MMA: 8 TMEM columns of packed bf16
-          umma_f16_ts(tmem_O, tmem_S + k * 8, make_smem_desc(aV + k * 2048, 16384, 1024), IDESC_PV, (j | k) != 0);
+          umma_f16_ts(tmem_O, tmem_S + k * 8, dV + ((k * 2048) >> 4), IDESC_PV, (j | k) != 0);
         umma_commit(v_empty);
         umma_commit(o_done);
       }
@@ -281,14 +283,14 @@ static EncodeTiledFn attn_encode() {
   return fn;
 }
 
-// [T, H, 128] bf16 (token stride `row_stride` elements) as {d, head, token} with boxes of 64 dims x 1 head x 128 tokens
-static int attn_map(CUtensorMap* m, const void* ptr, int T, int H, long long row_stride) {
+// [T, H, 128] bf16 (token stride `row_stride` elements) as {d, head, token} with boxes of 64 dims x 1 head x box_rows tokens
+static int attn_map(CUtensorMap* m, const void* ptr, int T, int H, long long row_stride, int box_rows = 128) {
   EncodeTiledFn enc = attn_encode();
   if (!enc) return -1;
   if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (row_stride * 2) % 16) return -2;
   cuuint64_t dims[3] = {128, (cuuint64_t)H, (cuuint64_t)T};
   cuuint64_t strides[2] = {256, (cuuint64_t)row_stride * 2};
-  cuuint32_t box[3] = {64, 1, 128};
+  cuuint32_t box[3] = {64, 1, (cuuint32_t)box_rows};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -331,29 +333,36 @@ extern "C" int mng_attn_fwd(const void* q, const void* k, const void* v, const i
 // Backward.  Two launches of one templated kernel, both with the forward's structure (owner tile resident,
 // the other side streamed, everything recomputed from q, k, v, dO and the forward's log-sum-exp):
 //
-//   DKV = true   owner = 128 keys (K, V tiles), stream = query blocks (Q, dO, lse, delta):
+//   DKV = true   owner = 128 keys (K, V tiles), stream = blocks of 64 queries (Q, dO, lse, delta):
 //                S^T = K Q^T, dP^T = V dO^T (lanes = keys), P^T = exp2(S^T c - lse), dS^T = P^T (dP^T - delta) scale,
 //                dV += P^T dO, dK += dS^T Q          (P^T, dS^T as bf16 A operands read from TMEM)
-//   DKV = false  owner = 128 queries (Q, dO tiles), stream = key blocks (K, V):
+//   DKV = false  owner = 128 queries (Q, dO tiles), stream = blocks of 64 keys (K, V):
 //                S = Q K^T, dP = dO V^T (lanes = queries), dS = P (dP - delta) scale, dQ += dS K
 //
 // The score tiles are computed twice (once per launch) so that no gradient needs atomics or a second pass:
-// each output row is written exactly once.  TMEM: S [0,128), dP [128,256), accumulators [256,384), [384,512).
-// The bf16 operands alias the fp32 tiles they were computed from: columns [0,32) and [64,96) of each
-// region (each half of the eight element-wise warps stays inside its own 64 columns).  320 threads: warp 0 TMA,
-// warp 1 MMA, warps 2-9 element-wise (warp w: TMEM lanes (w%4)*32.., columns ((w-2)/4)*64..).
-// delta[h,i] = sum_d dO[i,h,d] O[i,h,d] and lse2 = lse * log2(e) come from a small pre-kernel.
+// each output row is written exactly once.  TMEM: two S buffers [0,64) [64,128), two dP buffers [128,192)
+// [192,256), accumulators [256,384) and [384,512).  With two score buffers the issuing thread runs one block
+// ahead: S/dP of block n+1 are computed while the element-wise warps turn block n into P / dS, whose
+// accumulating MMAs then overlap the element-wise work on block n+1.  The bf16 operands alias the fp32
+// tiles they were computed from (each element-wise warp writes only inside the 32 columns it has read).
+// 576 threads: warp 0 TMA (4-stage ring of stream blocks), warp 1 MMA, warps 2-17 element-wise (warp w: TMEM
+// lanes (w%4)*32.., columns ((w-2)/4)*16.. of the block; sixteen warps because the work is bound by
+// TMEM round-trip latency, not by issue slots).  delta[h,i] = sum_d dO[i,h,d] O[i,h,d] and
+// lse2 = lse * log2(e) come from a small pre-kernel.
 namespace mng {
 
-constexpr int ATB_THREADS = 320;
-constexpr int ATB_VEC_BYTES = 2 * 2 * 512;           // 2 stages x (lse2, delta) x 128 floats
-constexpr int ATB_SMEM = 6 * ATT_TILE_BYTES + ATB_VEC_BYTES + 1024 + 1024;
+constexpr int ATB_THREADS = 576;                          // 2 + 16 warps
+constexpr int ATB_STAGES = 4;
+constexpr int ATB_BLK = 64;                               // stream rows per block
+constexpr int ATB_YTILE = ATB_BLK * 128 * 2;              // 16 KB: two boxes of 64 rows x 64 dims
+constexpr int ATB_VEC_BYTES = ATB_STAGES * 2 * ATB_BLK * 4;
+constexpr int ATB_SMEM = 2 * ATT_TILE_BYTES + ATB_STAGES * 2 * ATB_YTILE + ATB_VEC_BYTES + 1024 + 1024;
 
 struct AttnBwdParams {
   const int* doc_start;     // [T]
   const int* doc_end;       // [T] first token of the next document
   const float* lse2;        // [H, T] log-sum-exp in log2 units
-  const float* delta;       // [H, T]
+  const float* delta;       // [H, T] rowsum(dO o O) * scale
   __nv_bfloat16* out1;      // DKV: dK, else dQ     [T, H, 128]
   __nv_bfloat16* out2;      // DKV: dV
   int T, H, window;
@@ -362,7 +371,7 @@ struct AttnBwdParams {
 
 __global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
                                      const float* __restrict__ lse, float* __restrict__ delta, float* __restrict__ lse2, int T,
-                                     int H) {
+                                     int H, float scale) {
   const long long row = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 4;      // (token, head) pair: 16 lanes each
   const int part = threadIdx.x & 15;
   float acc = 0.f;
@@ -381,7 +390,7 @@ __global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, const 
   for (int s = 8; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
   if (part == 0 && row < (long long)T * H) {
     const int i = (int)(row / H), h = (int)(row % H);
-    delta[(size_t)h * T + i] = acc;
+    delta[(size_t)h * T + i] = acc * scale;       // pre-multiplied: dS = P (dP scale - delta scale)
     lse2[(size_t)h * T + i] = lse[(size_t)h * T + i] * 1.4426950408889634f;
   }
 }
@@ -402,40 +411,42 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tx1, const __grid_constant__
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sX1 = smem;
   uint8_t* sX2 = smem + ATT_TILE_BYTES;
-  uint8_t* sY = smem + 2 * ATT_TILE_BYTES;                  // stage s: Y1 at sY + s*2*TILE, Y2 right after
-  float* vec = reinterpret_cast<float*>(smem + 6 * ATT_TILE_BYTES);   // stage s: lse2 at vec + s*256, delta at +128
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * ATT_TILE_BYTES + ATB_VEC_BYTES);
+  uint8_t* sY = smem + 2 * ATT_TILE_BYTES;                  // stage s: Y1 at sY + s*2*YTILE, Y2 right after
+  float* vec = reinterpret_cast<float*>(sY + ATB_STAGES * 2 * ATB_YTILE);   // stage s: lse2 at vec + s*128, delta at +64
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(vec) + ATB_VEC_BYTES);
   uint64_t* x_full = bars + 0;
-  uint64_t* y_full = bars + 1;       // [2]
-  uint64_t* y_empty = bars + 3;      // [2]
-  uint64_t* sdp_full = bars + 5;
-  uint64_t* pds_ready = bars + 6;
-  uint64_t* acc_done = bars + 7;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  uint64_t* y_full = bars + 1;                     // [4]
+  uint64_t* y_empty = y_full + ATB_STAGES;         // [4]
+  uint64_t* sdp_full = y_empty + ATB_STAGES;       // [2]
+  uint64_t* pds_ready = sdp_full + 2;              // [2]
+  uint64_t* acc_done = pds_ready + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_done + 1);
   volatile uint32_t* abort_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y;
   const int r0 = (DKV ? (int)blockIdx.x : (int)(gridDim.x - 1 - blockIdx.x)) * 128;    // owner tile start
   const int r_last = min(r0 + 127, p.T - 1);
-  int s0, nb;                                                // stream start row and number of 128-row blocks
+  int s0, nb;                                                // stream start row and number of 64-row blocks
   if (DKV) {
     s0 = r0;
     const int i_max = min(min(r_last + p.window, p.doc_end[r_last] - 1), p.T - 1);
-    nb = (i_max - s0) / 128 + 1;
+    nb = (i_max - s0) / ATB_BLK + 1;
   } else {
     s0 = max(p.doc_start[r0], r0 - p.window);
-    nb = (r_last - s0) / 128 + 1;
+    nb = (r_last - s0) / ATB_BLK + 1;
   }
 
   if (threadIdx.x == 0) {
     mbar_init(x_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < ATB_STAGES; ++s) {
       mbar_init(&y_full[s], 1);
       mbar_init(&y_empty[s], 1);
     }
-    mbar_init(sdp_full, 1);
-    mbar_init(pds_ready, 8);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sdp_full[s], 1);
+      mbar_init(&pds_ready[s], 16);
+    }
     mbar_init(acc_done, 1);
     *abort_flag = 0;
     mbar_fence_init();
@@ -466,66 +477,73 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tx1, const __grid_constant__
       tma_load_3d(sX2, &tx2, x_full, 0, h, r0);
       tma_load_3d(sX2 + 16384, &tx2, x_full, 64, h, r0);
       for (int n = 0; n < nb; ++n) {
-        const int st = n & 1, srow = s0 + n * 128;
-        if (!mbar_wait(&y_empty[st], ((n >> 1) & 1) ^ 1, abort_flag)) { ATB_FAIL(ERR_WAIT_SMEM_EMPTY); break; }
-        uint8_t* y1 = sY + st * 2 * ATT_TILE_BYTES;
-        uint8_t* y2 = y1 + ATT_TILE_BYTES;
-        uint32_t bytes = 2 * ATT_TILE_BYTES;
-        const int cnt = min(128, p.T - srow);
+        const int st = n % ATB_STAGES, srow = s0 + n * ATB_BLK;
+        if (!mbar_wait(&y_empty[st], ((n / ATB_STAGES) & 1) ^ 1, abort_flag)) { ATB_FAIL(ERR_WAIT_SMEM_EMPTY); break; }
+        uint8_t* y1 = sY + st * 2 * ATB_YTILE;
+        uint8_t* y2 = y1 + ATB_YTILE;
+        uint32_t bytes = 2 * ATB_YTILE;
+        const int cnt = min(ATB_BLK, p.T - srow);
         if (DKV) bytes += 2u * cnt * 4u;
         mbar_expect_tx(&y_full[st], bytes);
         tma_load_3d(y1, &ty1, &y_full[st], 0, h, srow);
-        tma_load_3d(y1 + 16384, &ty1, &y_full[st], 64, h, srow);
+        tma_load_3d(y1 + ATB_YTILE / 2, &ty1, &y_full[st], 64, h, srow);
         tma_load_3d(y2, &ty2, &y_full[st], 0, h, srow);
-        tma_load_3d(y2 + 16384, &ty2, &y_full[st], 64, h, srow);
+        tma_load_3d(y2 + ATB_YTILE / 2, &ty2, &y_full[st], 64, h, srow);
         if (DKV) {
-          attn_bulk_load(vec + st * 256, p.lse2 + (size_t)h * p.T + srow, cnt * 4, &y_full[st]);
-          attn_bulk_load(vec + st * 256 + 128, p.delta + (size_t)h * p.T + srow, cnt * 4, &y_full[st]);
+          attn_bulk_load(vec + st * 2 * ATB_BLK, p.lse2 + (size_t)h * p.T + srow, cnt * 4, &y_full[st]);
+          attn_bulk_load(vec + st * 2 * ATB_BLK + ATB_BLK, p.delta + (size_t)h * p.T + srow, cnt * 4, &y_full[st]);
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t IDESC_SS = make_idesc(1, 1, 0, 0, 128, 128);
+      constexpr uint32_t IDESC_SS = make_idesc(1, 1, 0, 0, 128, ATB_BLK);
       constexpr uint32_t IDESC_TS = make_idesc(1, 1, 0, 1, 128, 128);
-      const uint32_t aX1 = smem_u32(sX1), aX2 = smem_u32(sX2);
+      const uint64_t dX1 = make_smem_desc(smem_u32(sX1), 16, 1024), dX2 = make_smem_desc(smem_u32(sX2), 16, 1024);
+      const uint64_t dYk = make_smem_desc(smem_u32(sY), 16, 1024);                 // stream tile as K-major B (scores)
+      const uint64_t dYm = make_smem_desc(smem_u32(sY), ATB_YTILE / 2, 1024);      // the same bytes as MN-major B (accumulation)
       bool ok = mbar_wait(x_full, 0, abort_flag);
       if (!ok) ATB_FAIL(ERR_WAIT_TMA_FULL);
-      int n = 0;
-      for (; ok && n < nb; ++n) {
-        const int st = n & 1;
-        const uint32_t aY1 = smem_u32(sY + st * 2 * ATT_TILE_BYTES), aY2 = aY1 + ATT_TILE_BYTES;
-        if (!mbar_wait(&y_full[st], (n >> 1) & 1, abort_flag)) { ATB_FAIL(ERR_WAIT_TMA_FULL); ok = false; break; }
-        tc_fence_after();
+      for (int n = 0; ok && n <= nb; ++n) {
+        if (n < nb) {                                        // scores of block n into buffer n & 1
+          const int st = n % ATB_STAGES, b = n & 1;
+          const uint64_t dY1 = dYk + ((st * 2 * ATB_YTILE) >> 4), dY2 = dY1 + (ATB_YTILE >> 4);
+          if (!mbar_wait(&y_full[st], (n / ATB_STAGES) & 1, abort_flag)) { ATB_FAIL(ERR_WAIT_TMA_FULL); ok = false; break; }
+          tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
-          umma_f16(tm_S, make_smem_desc(aX1 + off, 16, 1024), make_smem_desc(aY1 + off, 16, 1024), IDESC_SS, k != 0);
-        }
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
-          umma_f16(tm_dP, make_smem_desc(aX2 + off, 16, 1024), make_smem_desc(aY2 + off, 16, 1024), IDESC_SS, k != 0);
-        }
-        umma_commit(sdp_full);
-        if (!mbar_wait(pds_ready, n & 1, abort_flag)) { ATB_FAIL(ERR_WAIT_TMEM_EMPTY); ok = false; break; }
-        tc_fence_after();
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {                        // 16 stream rows per MMA: 8 TMEM columns of packed bf16
-          const uint32_t acol = (k < 4) ? k * 8 : 64 + (k - 4) * 8;
-          if (DKV) {
-            umma_f16_ts(tm_A2, tm_S + acol, make_smem_desc(aY2 + k * 2048, 16384, 1024), IDESC_TS, (n | k) != 0);   // dV += P^T dO
-            umma_f16_ts(tm_A1, tm_dP + acol, make_smem_desc(aY1 + k * 2048, 16384, 1024), IDESC_TS, (n | k) != 0);  // dK += dS^T Q
-          } else {
-            umma_f16_ts(tm_A1, tm_dP + acol, make_smem_desc(aY1 + k * 2048, 16384, 1024), IDESC_TS, (n | k) != 0);  // dQ += dS K
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t xo = ((k >> 2) * 16384 + (k & 3) * 32) >> 4, yo = ((k >> 2) * (ATB_YTILE / 2) + (k & 3) * 32) >> 4;
+            umma_f16(tm_S + b * ATB_BLK, dX1 + xo, dY1 + yo, IDESC_SS, k != 0);
           }
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t xo = ((k >> 2) * 16384 + (k & 3) * 32) >> 4, yo = ((k >> 2) * (ATB_YTILE / 2) + (k & 3) * 32) >> 4;
+            umma_f16(tm_dP + b * ATB_BLK, dX2 + xo, dY2 + yo, IDESC_SS, k != 0);
+          }
+          umma_commit(&sdp_full[b]);
         }
-        umma_commit(&y_empty[st]);
+        if (n >= 1) {                                        // accumulate block n-1 from its bf16 operands in TMEM
+          const int m = n - 1, st = m % ATB_STAGES, b = m & 1;
+          const uint64_t dY1 = dYm + ((st * 2 * ATB_YTILE) >> 4), dY2 = dY1 + (ATB_YTILE >> 4);
+          if (!mbar_wait(&pds_ready[b], (m >> 1) & 1, abort_flag)) { ATB_FAIL(ERR_WAIT_TMEM_EMPTY); ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < ATB_BLK / 16; ++k) {           // 16 stream rows per MMA: 8 TMEM columns of packed bf16
+            const uint32_t acol = b * ATB_BLK + k * 16;          // warp quarter k packed its 16 columns into 8
+            if (DKV) {
+              umma_f16_ts(tm_A2, tm_S + acol, dY2 + ((k * 2048) >> 4), IDESC_TS, (m | k) != 0);    // dV += P^T dO
+              umma_f16_ts(tm_A1, tm_dP + acol, dY1 + ((k * 2048) >> 4), IDESC_TS, (m | k) != 0);   // dK += dS^T Q
+            } else {
+              umma_f16_ts(tm_A1, tm_dP + acol, dY1 + ((k * 2048) >> 4), IDESC_TS, (m | k) != 0);   // dQ += dS K
+            }
+          }
+          umma_commit(&y_empty[st]);
+        }
       }
       if (ok) umma_commit(acc_done);
     }
   } else {
-    const int sub = warp & 3, half = (warp - 2) >> 2;
+    const int sub = warp & 3, quarter = (warp - 2) >> 2;     // TMEM lanes sub*32.., block columns quarter*16..
     const int r = sub * 32 + lane;
     const int g = r0 + r;                                    // owner row: a key (DKV) or a query
     const bool row_ok = g < p.T;
@@ -548,42 +566,64 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tx1, const __grid_constant__
     const float c = p.scale_log2, sc = p.scale;
     bool alive = true;
     for (int n = 0; n < nb; ++n) {
-      const int st = n & 1, srow = s0 + n * 128;
-      if (!mbar_wait(sdp_full, n & 1, abort_flag)) { ATB_FAIL(ERR_WAIT_TMEM_FULL); alive = false; break; }
+      const int st = n % ATB_STAGES, b = n & 1, srow = s0 + n * ATB_BLK;
+      if (!mbar_wait(&sdp_full[b], (n >> 1) & 1, abort_flag)) { ATB_FAIL(ERR_WAIT_TMEM_FULL); alive = false; break; }
       tc_fence_after();
-      const float* vl = vec + st * 256;
-      const float* vd = vl + 128;
-#pragma unroll 1
-      for (int cc = half * 2; cc < half * 2 + 2; ++cc) {
-        uint32_t s[32], d[32];
-        tmem_ld32(tm_S + lane_off + cc * 32, s);
-        tmem_ld32(tm_dP + lane_off + cc * 32, d);
-        tmem_ld_wait();
-        uint32_t pk_p[16], pk_ds[16];
-        const int col0 = srow + cc * 32 - lo;
+      const float* vl = vec + st * 2 * ATB_BLK + quarter * 16;
+      const float* vd = vl + ATB_BLK;
+      const uint32_t col = lane_off + b * ATB_BLK + quarter * 16;
+      uint32_t s[16], d[16];
+      tmem_ld16(tm_S + col, s);
+      tmem_ld16(tm_dP + col, d);
+      tmem_ld_wait();
+      uint32_t pk_p[8], pk_ds[8];
+      const int col0 = srow + quarter * 16 - lo;
+      const bool full = any_vis && col0 >= 0 && (unsigned)(col0 + 15) <= span;     // all 16 columns visible for this row
+      if (__all_sync(0xffffffffu, full)) {
 #pragma unroll
-        for (int t = 0; t < 32; t += 2) {
+        for (int t = 0; t < 16; t += 4) {
+          float l2[4], dl[4];
+          if (DKV) {
+            *reinterpret_cast<float4*>(l2) = *reinterpret_cast<const float4*>(vl + t);
+            *reinterpret_cast<float4*>(dl) = *reinterpret_cast<const float4*>(vd + t);
+          } else {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) { l2[u] = my_lse2; dl[u] = my_delta; }
+          }
+          float pv[4], dv[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            pv[u] = exp2f(fmaf(__uint_as_float(s[t + u]), c, -l2[u]));
+            dv[u] = pv[u] * fmaf(__uint_as_float(d[t + u]), sc, -dl[u]);
+          }
+          pk_p[t >> 1] = pack_bf16x2(pv[0], pv[1]);
+          pk_p[(t >> 1) + 1] = pack_bf16x2(pv[2], pv[3]);
+          pk_ds[t >> 1] = pack_bf16x2(dv[0], dv[1]);
+          pk_ds[(t >> 1) + 1] = pack_bf16x2(dv[2], dv[3]);
+        }
+      } else {
+#pragma unroll
+        for (int t = 0; t < 16; t += 2) {
           float pv[2], dv[2];
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
-            const float l2 = DKV ? vl[cc * 32 + t + u] : my_lse2;
-            const float dl = DKV ? vd[cc * 32 + t + u] : my_delta;
+            const float l2 = DKV ? vl[t + u] : my_lse2;
+            const float dl = DKV ? vd[t + u] : my_delta;
             const bool vis = any_vis && (unsigned)(col0 + t + u) <= span;
             const float pe = exp2f(fmaf(__uint_as_float(s[t + u]), c, -l2));
             pv[u] = vis ? pe : 0.f;
-            dv[u] = vis ? pe * (__uint_as_float(d[t + u]) - dl) * sc : 0.f;
+            dv[u] = vis ? pe * fmaf(__uint_as_float(d[t + u]), sc, -dl) : 0.f;
           }
           pk_p[t >> 1] = pack_bf16x2(pv[0], pv[1]);
           pk_ds[t >> 1] = pack_bf16x2(dv[0], dv[1]);
         }
-        const uint32_t dst = lane_off + half * 64 + (cc & 1) * 16;
-        if (DKV) tmem_st16(tm_S + dst, pk_p);
-        tmem_st16(tm_dP + dst, pk_ds);
       }
+      if (DKV) tmem_st8(tm_S + col, pk_p);
+      tmem_st8(tm_dP + col, pk_ds);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(pds_ready);
+      if (lane == 0) mbar_arrive(&pds_ready[b]);
     }
     if (alive) {
       if (!mbar_wait(acc_done, 0, abort_flag)) {
@@ -592,11 +632,11 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tx1, const __grid_constant__
         tc_fence_after();
 #pragma unroll 1
         for (int which = 0; which < (DKV ? 2 : 1); ++which) {
-          __nv_bfloat16* orow = (which == 0 ? p.out1 : p.out2) + ((size_t)g * p.H + h) * 128 + half * 64;
+          __nv_bfloat16* orow = (which == 0 ? p.out1 : p.out2) + ((size_t)g * p.H + h) * 128 + quarter * 32;
 #pragma unroll 1
-          for (int cc = 0; cc < 2; ++cc) {
+          for (int cc = 0; cc < 1; ++cc) {
             uint32_t v[32];
-            tmem_ld32((which == 0 ? tm_A1 : tm_A2) + lane_off + half * 64 + cc * 32, v);
+            tmem_ld32((which == 0 ? tm_A1 : tm_A2) + lane_off + quarter * 32, v);
             tmem_ld_wait();
             if (row_ok) {
 #pragma unroll
@@ -635,12 +675,13 @@ extern "C" int mng_attn_bwd(const void* q, const void* k, const void* v, const v
                             int T, int H, long long row_stride, int window, float scale, void* stream, uint32_t* status) {
   if (T <= 0 || H <= 0) return 0;
   if (T % 4) return -5;                                    // rows of the [H, T] vectors must stay 16-byte aligned
-  CUtensorMap tq, tk, tv, tdo;
+  CUtensorMap tq, tk, tv, tdo, sq, sk, sv, sdo;            // owner maps (128-row boxes) and stream maps (64-row boxes)
   int rc;
-  if ((rc = attn_map(&tq, q, T, H, row_stride))) return rc;
-  if ((rc = attn_map(&tk, k, T, H, row_stride))) return rc - 1000;
-  if ((rc = attn_map(&tv, v, T, H, row_stride))) return rc - 2000;
-  if ((rc = attn_map(&tdo, dout, T, H, (long long)H * 128))) return rc - 3000;
+  const long long ds = (long long)H * 128;
+  if ((rc = attn_map(&tq, q, T, H, row_stride, 128)) || (rc = attn_map(&sq, q, T, H, row_stride, ATB_BLK))) return rc;
+  if ((rc = attn_map(&tk, k, T, H, row_stride, 128)) || (rc = attn_map(&sk, k, T, H, row_stride, ATB_BLK))) return rc - 1000;
+  if ((rc = attn_map(&tv, v, T, H, row_stride, 128)) || (rc = attn_map(&sv, v, T, H, row_stride, ATB_BLK))) return rc - 2000;
+  if ((rc = attn_map(&tdo, dout, T, H, ds, 128)) || (rc = attn_map(&sdo, dout, T, H, ds, ATB_BLK))) return rc - 3000;
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(attn_bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ATB_SMEM) != cudaSuccess ||
@@ -651,13 +692,13 @@ extern "C" int mng_attn_bwd(const void* q, const void* k, const void* v, const v
   cudaStream_t st = (cudaStream_t)stream;
   const long long rows = (long long)T * H;
   attn_bwd_prep_kernel<<<(unsigned)((rows * 16 + 255) / 256), 256, 0, st>>>(
-      reinterpret_cast<const __nv_bfloat16*>(out), reinterpret_cast<const __nv_bfloat16*>(dout), lse, delta, lse2, T, H);
+      reinterpret_cast<const __nv_bfloat16*>(out), reinterpret_cast<const __nv_bfloat16*>(dout), lse, delta, lse2, T, H, scale);
   const float c = scale * 1.4426950408889634f;
   dim3 grid((T + 127) / 128, H);
   AttnBwdParams pa{doc_start, doc_end, lse2, delta, reinterpret_cast<__nv_bfloat16*>(dk), reinterpret_cast<__nv_bfloat16*>(dv),
                    T, H, window, c, scale};
-  attn_bwd_kernel<true><<<grid, ATB_THREADS, ATB_SMEM, st>>>(tk, tv, tq, tdo, pa, status);
+  attn_bwd_kernel<true><<<grid, ATB_THREADS, ATB_SMEM, st>>>(tk, tv, sq, sdo, pa, status);
   AttnBwdParams pb{doc_start, doc_end, lse2, delta, reinterpret_cast<__nv_bfloat16*>(dq), nullptr, T, H, window, c, scale};
-  attn_bwd_kernel<false><<<grid, ATB_THREADS, ATB_SMEM, st>>>(tq, tdo, tk, tv, pb, status);
+  attn_bwd_kernel<false><<<grid, ATB_THREADS, ATB_SMEM, st>>>(tq, tdo, sk, sv, pb, status);
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
