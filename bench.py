@@ -37,6 +37,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--stage", type=int, default=2, help="schedule stage whose batch/window settings are timed")
     ap.add_argument("--tokens-per-gpu", type=int, default=0, help="override the micro-batch size (smoke runs only)")
+    ap.add_argument("--track", type=int, default=1, choices=[1, 2],
+                    help="2 = track-2 model at its 524,288-token plateau batch (own arm only; not the headline)")
     return ap.parse_args()
 
 
@@ -57,6 +59,9 @@ def reference_arm(args):
 def main():
     args = parse()
     if args.impl == "reference":
+        if args.track != 1:
+            print(json.dumps({"impl": "reference", "unavailable": "the reference arm is wired for the track-1 headline only"}))
+            return
         return reference_arm(args)
     import torch
     import torch.distributed as dist
@@ -73,11 +78,21 @@ def main():
     assert env.world_size == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={env.world_size}"
     native.available(required=True)
 
-    stages = track1_stages()
+    model = None
+    if args.track == 2:
+        from modded_nanogpt_b200.config import track2_hyperparameters, track2_schedule
+        from modded_nanogpt_b200.models.gpt_medium import GPTMedium
+        hp2 = track2_hyperparameters()
+        sched = track2_schedule(hp2)
+        stages = sched.stages
+        args.stage = next(i for i, s in enumerate(stages) if s.batch_size == 524288)
+    else:
+        stages = track1_stages()
     if args.tokens_per_gpu:
         for s in stages:
             s.batch_size = args.tokens_per_gpu * 8
-    sched = TrainingSchedule(stages, 1270, 15, cooldown_frac=0.60)
+    if args.track == 1:
+        sched = TrainingSchedule(stages, 1270, 15, cooldown_frac=0.60)
     first = sched.boundaries[args.stage][0] + 1               # 848: inside stage 2, after the embed split
     stage = stages[args.stage]
     K, W = args.steps, args.warmup
@@ -87,8 +102,15 @@ def main():
         write_synthetic_corpus(root, train_tokens=int(stage.batch_size * (n_steps + 2) * 1.02) + 1_000_000,
                                val_tokens=1_000_000, seed=0, max_doc_len=stage.train_max_seq_len)
     env.barrier()
-    hp = Hyperparameters(data_path=root, val_loss_every=0, seed=0)
-    tr = Trainer(track1_model(hp.val_batch_size // 8), sched, hp, env,
+    if args.track == 2:
+        hp = track2_hyperparameters(data_path=root, val_loss_every=0, seed=0)
+        eval_seq = hp.val_batch_size // 8
+        torch.manual_seed(0)
+        model = GPTMedium(max_seq_len=eval_seq, world_size=env.world_size, grad_scale=env.grad_scale, use_fp8=True,
+                          eval_seq_len=eval_seq)
+    else:
+        hp = Hyperparameters(data_path=root, val_loss_every=0, seed=0)
+    tr = Trainer(None if model is not None else track1_model(hp.val_batch_size // 8), sched, hp, env, model=model,
                  logger=RunLogger(f"bench_{os.getpid()}", env.master, log_dir="/tmp/mng_logs", quiet=True))
     # enter the timed stage the way a run would: windows / YaRN state of the earlier stages applied
     for b0, _ in sched.boundaries[:args.stage + 1]:
@@ -165,12 +187,14 @@ def main():
     e2e_value = tokens / (max(e2e_ms, e2e_wall_ms) / 1e3)
     if env.master:
         out = {
-            "metric": "train tokens/s, track-1 GPT, stage-2 batch (393216 tok/step)", "value": value, "unit": "tokens/s",
+            "metric": ("train tokens/s, track-1 GPT, stage-2 batch (393216 tok/step)" if args.track == 1 else
+                       "train tokens/s, track-2 GPT, plateau batch (524288 tok/step)"), "value": value, "unit": "tokens/s",
             "n_gpus": env.world_size, "steps": K, "warmup": W, "ms_per_step": dev_ms / K, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": (value / BASELINE_TOKENS_PER_S) if BASELINE_TOKENS_PER_S else None,
             "dtype": "bf16 (fp8 e4m3 MLP forward and lm_head)", "data": "synthetic Zipf(1.1) ids, EoS-delimited lognormal docs; random-init weights",
             "impl": "ours",
-            "config": {"model": "track-1 GPT (11L, d768, 6x128 heads, vocab 50304)", "global_batch": stage.batch_size,
+            "config": {"model": ("track-1 GPT (11L, d768, 6x128 heads, vocab 50304)" if args.track == 1 else
+                                 "track-2 GPT (16L, d1024, 8x128 heads, vocab 50304)"), "global_batch": stage.batch_size,
                        "seq_len": stage.train_max_seq_len, "tokens_per_gpu_per_microbatch": stage.batch_size // 8,
                        "grad_accum": env.grad_accum_steps, "parallelism": f"dp{env.world_size}",
                        "windows": [w * hp.block_size for w in stage.window_sizes], "first_step": first,

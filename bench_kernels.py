@@ -73,6 +73,17 @@ def build_case(name, T, bn, fused):
         tg, pt = torch.randint(0, V, (T,), device=dev), torch.randint(-1, V, (T,), device=dev)
         w, pw = torch.tensor([1.0, 0.5, 0.25], device=dev), torch.tensor([0.3], device=dev)
         return (lambda: lib.softcap_ce(logits, tg, w, pt, pw, e5, 23.0, 5.0, 7.5, 1.0)), 0, T * V * (3 if e5 else 4)
+    if name == "lmhead_ce_fwdbwd":      # normed x [T,768] -> fp8 lm_head -> soft-capped CE with MTP weights -> dx, dW
+        x = (r(T, D) * 0.5).to(BF).requires_grad_(True)
+        w = (r(D, V) * 0.02).to(BF).requires_grad_(True)
+        tg = torch.randint(0, V, (T,), device=dev)
+        mtp, pw = torch.tensor([1.0, 0.5, 0.25], device=dev), torch.tensor([0.1], device=dev)
+        pt = torch.randint(-1, V, (T,), device=dev)
+
+        def run():
+            x.grad = w.grad = None
+            fused.softcap_ce(x, w, tg, mtp, pt, pw, 23.0, 5.0, 7.5, grad_scale=1.0, fp8=True).sum().backward()
+        return run, 3 * 2 * T * D * V, T * V * 3
     if name.startswith("attn"):             # attn[bwd]_{ours|fa2}_{short|long|paired}: packed documents, sliding window
         op, impl, kind = name.split("_")
         Tq, Hh, window = (2 * T, 3, 2 * 640) if kind == "paired" else (T, 6, 640 if kind == "short" else 1408)
@@ -112,7 +123,7 @@ def build_case(name, T, bn, fused):
 
 
 CASES = ["gemm_bf16_up", "gemm_bf16_dpre", "gemm_bf16_down", "gemm_bf16_dw", "gemm_fp8_relu2", "gemm_fp8_down", "gemm_bf16_qkv",
-         "gemm_bf16_o", "gemm_bf16_o_null", "gemm_bf16_up_null", "gemm_fp8_logits", "gemm_fp8_lmhead_dx", "gemm_fp8_lmhead_dw", "softcap_ce_e5m2", "softcap_ce_bf16",
+         "gemm_bf16_o", "gemm_bf16_o_null", "gemm_bf16_up_null", "gemm_fp8_logits", "gemm_fp8_lmhead_dx", "gemm_fp8_lmhead_dw", "softcap_ce_e5m2", "softcap_ce_bf16", "lmhead_ce_fwdbwd",
          "attn_ours_short", "attn_fa2_short", "attn_ours_long", "attn_fa2_long", "attn_ours_paired", "attn_fa2_paired",
          "attnbwd_ours_short", "attnbwd_fa2_short", "attnbwd_ours_long", "attnbwd_fa2_long", "attnbwd_ours_paired", "attnbwd_fa2_paired"]
 

@@ -1,0 +1,76 @@
+"""Optimizer-step micro-benchmark: NorMuon (Polar Express) + Adam over all track-1 parameters with their
+collectives, on random gradients.  Compares the fused NVLink path (update kernels that read the peers'
+gradient shards and store the new weights to every peer) with the NCCL path (reduce-scatter / all-reduce /
+all-gather around the same update kernels).
+
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port 29533 \
+        bench_optimizer.py --steps 20
+
+Prints one JSON line per communication mode: device time (CUDA events, max over ranks) of odd steps
+(NorMuon + Adam) and even steps (NorMuon only)."""
+import argparse
+import json
+import os
+import sys
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--modes", default="nccl,fused")
+    a = ap.parse_args()
+    import torch
+    from modded_nanogpt_b200.config import Hyperparameters, TrainingSchedule, track1_model, track1_stages
+    from modded_nanogpt_b200.ops import fused
+    from modded_nanogpt_b200.runtime.dist import init_distributed, shutdown
+    from modded_nanogpt_b200.trainer import Trainer
+    from modded_nanogpt_b200.utils.logging import RunLogger
+    from modded_nanogpt_b200.utils.timing import max_over_ranks
+    env = init_distributed(accum_base=8)
+    for mode in a.modes.split(","):
+        if mode != "nccl" and env.world_size == 1:
+            continue
+        os.environ["MNG_COMM"] = mode
+        sched = TrainingSchedule(track1_stages(), 1270, 15, cooldown_frac=0.6)
+        hp = Hyperparameters(val_loss_every=0, seed=0)
+        tr = Trainer(track1_model(hp.val_batch_size // 8), sched, hp, env, use_cuda_graphs=False,
+                     logger=RunLogger(f"optbench_{mode}", env.master, log_dir="/tmp/mng_logs", quiet=True))
+        tr.manager.advance_schedule(848)
+        tr.manager.optimizer.split_embed = True
+        g = torch.Generator(device="cuda").manual_seed(env.rank)
+        params = list(tr.model.parameters())
+
+        def fill():
+            for p in params:
+                if p.grad is None:
+                    p.grad = torch.empty_like(p)
+                p.grad.copy_((torch.randn(p.shape, generator=g, device="cuda", dtype=torch.float32) * 1e-3).to(p.dtype))
+
+        times = {0: [], 1: []}
+        for step in range(849, 849 + a.steps + 4):
+            fill()
+            env.barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            tr.manager.step_optimizers(step)
+            e1.record()
+            torch.cuda.synchronize()
+            if step >= 853:
+                times[step % 2].append(max_over_ranks(e0.elapsed_time(e1)))
+        fused.check_status()
+        n_hidden = sum(p.numel() for l, p in tr.manager.optimizer.params.items() if tr.manager.optimizer.cfgs[l].optim == "normuon")
+        if env.master:
+            med = lambda v: sorted(v)[len(v) // 2]
+            print(json.dumps({"mode": mode, "n_gpus": env.world_size, "adam_step_ms": round(med(times[1]), 3),
+                              "muon_only_step_ms": round(med(times[0]), 3), "normuon_params": n_hidden,
+                              "all_params": sum(p.numel() for p in params)}), flush=True)
+        del tr
+        torch.cuda.empty_cache()
+    shutdown()
+
+
+if __name__ == "__main__":
+    main()
