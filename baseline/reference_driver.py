@@ -182,7 +182,8 @@ def drive(args, ref_dir: str) -> dict:
         "impl": "reference", "metric": "train tokens/s, track-1 GPT, stage-2 batch (393216 tok/step)",
         "value": tokens / (dev_ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": dev_ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "bf16 (fp8 MLP forward and lm_head)", "data": "synthetic Zipf(1.1) ids, EoS-delimited lognormal docs; random-init weights",
+        "dtype": ("bf16 (fp8 lm_head; bf16 MLP: reference run with its own DISABLE_FP8=1)" if os.environ.get("DISABLE_FP8")
+                  else "bf16 (fp8 MLP forward and lm_head)"), "data": "synthetic Zipf(1.1) ids, EoS-delimited lognormal docs; random-init weights",
         "config": {"model": "track-1 GPT (reference train_gpt.py HEAD)", "global_batch": stage.batch_size,
                    "seq_len": stage.train_max_seq_len, "grad_accum": ga, "parallelism": f"dp{world}",
                    "attention": "FlashAttention-2 (FA3 is a Hopper-only binary)", "first_step": first,

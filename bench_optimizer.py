@@ -6,6 +6,7 @@ all-gather around the same update kernels).
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port 29533 \
         bench_optimizer.py --steps 20
 
+The bigram table's gradient is reduced densely here (the sparse row exchange needs the loader's row bookkeeping).
 Prints one JSON line per communication mode: device time (CUDA events, max over ranks) of odd steps
 (NorMuon + Adam) and even steps (NorMuon only)."""
 import argparse
@@ -35,7 +36,7 @@ def main():
         os.environ["MNG_COMM"] = mode
         sched = TrainingSchedule(track1_stages(), 1270, 15, cooldown_frac=0.6)
         hp = Hyperparameters(val_loss_every=0, seed=0)
-        tr = Trainer(track1_model(hp.val_batch_size // 8), sched, hp, env, use_cuda_graphs=False,
+        tr = Trainer(track1_model(hp.val_batch_size // 8), sched, hp, env, use_cuda_graphs=False, sparse_min_world=1 << 30,
                      logger=RunLogger(f"optbench_{mode}", env.master, log_dir="/tmp/mng_logs", quiet=True))
         tr.manager.advance_schedule(848)
         tr.manager.optimizer.split_embed = True

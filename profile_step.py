@@ -1,0 +1,75 @@
+"""Per-kernel device-time table of the training step (torch.profiler, CUDA activities only).
+
+    python profile_step.py [--micro-steps 2] [--rows 60]
+
+Builds the track-1 trainer at its stage-2 configuration on synthetic data, warms up (including the CUDA-graph
+capture of the micro-step), then profiles `--micro-steps` micro-batches plus one optimizer step and prints the
+kernels sorted by total device time.  Times under the profiler are for shares, not for absolute claims."""
+import argparse
+import os
+import sys
+import time
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--micro-steps", type=int, default=2)
+    ap.add_argument("--rows", type=int, default=60)
+    ap.add_argument("--eager", action="store_true", help="profile the eager micro-step instead of the graph replay")
+    a = ap.parse_args()
+    import torch
+    from torch.autograd import DeviceType
+    from torch.profiler import ProfilerActivity, profile
+    from modded_nanogpt_b200.config import Hyperparameters, TrainingSchedule, track1_model, track1_stages
+    from modded_nanogpt_b200.data.shards import write_synthetic_corpus
+    from modded_nanogpt_b200.ops import fused
+    from modded_nanogpt_b200.runtime.dist import init_distributed
+    from modded_nanogpt_b200.trainer import Trainer
+    from modded_nanogpt_b200.utils.logging import RunLogger
+    env = init_distributed(accum_base=8)
+    sched = TrainingSchedule(track1_stages(), 1270, 15, cooldown_frac=0.6)
+    root = "/tmp/mng_profile_data"
+    write_synthetic_corpus(root, train_tokens=12_000_000, val_tokens=1_000_000, seed=0, max_doc_len=2048)
+    hp = Hyperparameters(data_path=root, val_loss_every=0)
+    tr = Trainer(track1_model(262144), sched, hp, env, use_cuda_graphs=not a.eager,
+                 logger=RunLogger("profile", True, log_dir="/tmp/mng_logs", quiet=True))
+    for b0, _ in sched.boundaries[:3]:
+        tr.manager.advance_schedule(b0)
+    tr.manager.optimizer.split_embed = True
+    tr.train_loader = tr.make_train_loader()
+    tr.train_loader.reparameterise(393216, 2048, 8)
+    m = tr.manager
+
+    def micro(step):
+        return tr.micro_step(tr.train_loader.next_batch(), step)
+
+    for _ in range(4):
+        micro(848)
+    m.step_optimizers(849)
+    tr.model.quantize_mlp_fp8(False)
+    torch.cuda.synchronize()
+    t = time.time()
+    for _ in range(4):
+        micro(850)
+    torch.cuda.synchronize()
+    print(f"micro-step wall ms (unprofiled): {(time.time() - t) / 4 * 1e3:.2f}")
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(a.micro_steps):
+            micro(851)
+        m.step_optimizers(851)
+        tr.model.quantize_mlp_fp8(False)
+        torch.cuda.synchronize()
+    ks = [e for e in prof.key_averages() if e.device_type == DeviceType.CUDA]
+    ks.sort(key=lambda e: -e.self_device_time_total)
+    tot = sum(e.self_device_time_total for e in ks)
+    print(f"device time of {a.micro_steps} micro-steps + 1 optimizer step (Adam step): {tot / 1e3:.2f} ms")
+    for e in ks[:a.rows]:
+        print(f"{e.self_device_time_total / 1e3:9.3f} ms {100 * e.self_device_time_total / tot:5.1f}% {e.count:5d} x "
+              f"{e.self_device_time_total / max(e.count, 1):9.1f} us  {e.key[:120]}")
+    fused.check_status()
+
+
+if __name__ == "__main__":
+    main()
