@@ -21,6 +21,13 @@ __device__ __forceinline__ uint4 pack_bf16x8(const float* v) {
   w.x = pack_bf16x2(v[0], v[1]); w.y = pack_bf16x2(v[2], v[3]); w.z = pack_bf16x2(v[4], v[5]); w.w = pack_bf16x2(v[6], v[7]);
   return w;
 }
+// Round two floats to bf16 and back with one packed conversion and two integer ops (a scalar
+// float -> bf16 -> float round trip goes through the low-rate conversion pipe instead).
+__device__ __forceinline__ void round_bf16x2(float& a, float& b) {
+  const uint32_t u = pack_bf16x2(a, b);
+  a = __uint_as_float(u << 16);
+  b = __uint_as_float(u & 0xffff0000u);
+}
 __device__ __forceinline__ void unpack_bf16x8(uint4 c, float* f) {
   const __nv_bfloat162* c2 = reinterpret_cast<const __nv_bfloat162*>(&c);
 #pragma unroll
@@ -136,13 +143,17 @@ struct EpiRelu2 {
     float post[32];
     float mx = 0.f;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const float cs = p.col_scale ? p.col_scale[col0 + j] : 1.f;
-      float pre = __bfloat162float(__float2bfloat16(acc[j] * rs * cs));
-      float r = fmaxf(pre, 0.f);
-      float q = __bfloat162float(__float2bfloat16(r * r));
-      post[j] = q;
-      mx = fmaxf(mx, q);
+    for (int j = 0; j < 32; j += 2) {
+      const float cs0 = p.col_scale ? p.col_scale[col0 + j] : 1.f, cs1 = p.col_scale ? p.col_scale[col0 + j + 1] : 1.f;
+      float a0 = acc[j] * rs * cs0, a1 = acc[j + 1] * rs * cs1;
+      round_bf16x2(a0, a1);                                   // pre-activation as the reference materialises it (bf16)
+      a0 = fmaxf(a0, 0.f);
+      a1 = fmaxf(a1, 0.f);
+      float q0 = a0 * a0, q1 = a1 * a1;
+      round_bf16x2(q0, q1);
+      post[j] = q0;
+      post[j + 1] = q1;
+      mx = fmaxf(mx, fmaxf(q0, q1));
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) io.put<64>(j, pack_bf16x8(post + 8 * j));
@@ -185,7 +196,12 @@ struct EpiDpre {
       float f[8];
       unpack_bf16x8(io.get<64>(j), f);
 #pragma unroll
-      for (int t = 0; t < 8; ++t) o[8 * j + t] = 2.f * __bfloat162float(__float2bfloat16(acc[8 * j + t])) * sqrtf(f[t]);
+      for (int t = 0; t < 8; t += 2) {
+        float a0 = acc[8 * j + t], a1 = acc[8 * j + t + 1];
+        round_bf16x2(a0, a1);
+        o[8 * j + t] = 2.f * a0 * sqrtf(f[t]);
+        o[8 * j + t + 1] = 2.f * a1 * sqrtf(f[t + 1]);
+      }
     }
     __syncwarp();
 #pragma unroll
@@ -273,13 +289,17 @@ struct TEpiRelu2 {
     float post[32];
     float mx = 0.f;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const float cs = p.col_scale ? p.col_scale[col0 + j] : 1.f;
-      const float pre = __bfloat162float(__float2bfloat16(acc[j] * rs * cs));
-      const float r = fmaxf(pre, 0.f);
-      const float q = __bfloat162float(__float2bfloat16(r * r));
-      post[j] = q;
-      mx = fmaxf(mx, q);
+    for (int j = 0; j < 32; j += 2) {
+      const float cs0 = p.col_scale ? p.col_scale[col0 + j] : 1.f, cs1 = p.col_scale ? p.col_scale[col0 + j + 1] : 1.f;
+      float a0 = acc[j] * rs * cs0, a1 = acc[j + 1] * rs * cs1;
+      round_bf16x2(a0, a1);                                   // pre-activation as the reference materialises it (bf16)
+      a0 = fmaxf(a0, 0.f);
+      a1 = fmaxf(a1, 0.f);
+      float q0 = a0 * a0, q1 = a1 * a1;
+      round_bf16x2(q0, q1);
+      post[j] = q0;
+      post[j + 1] = q1;
+      mx = fmaxf(mx, fmaxf(q0, q1));
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) out[j] = pack_bf16x8(post + 8 * j);
@@ -313,7 +333,12 @@ struct TEpiDpre {
       float f[8];
       unpack_bf16x8(cin[j], f);
 #pragma unroll
-      for (int t = 0; t < 8; ++t) o[8 * j + t] = 2.f * __bfloat162float(__float2bfloat16(acc[8 * j + t])) * sqrtf(f[t]);
+      for (int t = 0; t < 8; t += 2) {
+        float a0 = acc[8 * j + t], a1 = acc[8 * j + t + 1];
+        round_bf16x2(a0, a1);
+        o[8 * j + t] = 2.f * a0 * sqrtf(f[t]);
+        o[8 * j + t + 1] = 2.f * a1 * sqrtf(f[t + 1]);
+      }
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) out[j] = pack_bf16x8(o + 8 * j);
