@@ -58,6 +58,13 @@ def build_case(name, T, bn, fused):
         a, b = r(T, D).to(F8), r(D, V).to(F8)
         o = torch.empty(T, V, dtype=BF, device=dev)
         return (lambda: fused.gemm(a, b, b_mn=True, out=o, bn=bn)), 2 * T * D * V, T * V * 2
+    if name == "gemm_fp8_logits_kk":    # same product with the weight stored [V, 768] (K-major B)
+        a, b = r(T, D).to(F8), r(V, D).to(F8)
+        o = torch.empty(T, V, dtype=BF, device=dev)
+        return (lambda: fused.gemm(a, b, out=o, bn=bn)), 2 * T * D * V, T * V * 2
+    if name == "gemm_fp8_lmhead_dw_kmajor_a":   # dW with x stored transposed [768, T] (K-major A), dl as is (MN-major B)
+        a, b = r(D, T).to(F8), torch.randn(T, V, device=dev, dtype=BF).to(F8B)
+        return (lambda: fused.gemm(a, b, b_mn=True, bn=bn)), 2 * T * D * V, D * V * 2
     if name == "gemm_fp8_lmhead_dx":    # e5m2 [T,V] x e4m3 [768,V]^T
         a, b = torch.randn(T, V, device=dev, dtype=BF).to(F8B), r(D, V).to(F8)
         return (lambda: fused.gemm(a, b, bn=bn)), 2 * T * D * V, T * D * 2
@@ -123,7 +130,7 @@ def build_case(name, T, bn, fused):
 
 
 CASES = ["gemm_bf16_up", "gemm_bf16_dpre", "gemm_bf16_down", "gemm_bf16_dw", "gemm_fp8_relu2", "gemm_fp8_down", "gemm_bf16_qkv",
-         "gemm_bf16_o", "gemm_bf16_o_null", "gemm_bf16_up_null", "gemm_fp8_logits", "gemm_fp8_lmhead_dx", "gemm_fp8_lmhead_dw", "softcap_ce_e5m2", "softcap_ce_bf16", "lmhead_ce_fwdbwd",
+         "gemm_bf16_o", "gemm_bf16_o_null", "gemm_bf16_up_null", "gemm_fp8_logits", "gemm_fp8_logits_kk", "gemm_fp8_lmhead_dw_kmajor_a", "gemm_fp8_lmhead_dx", "gemm_fp8_lmhead_dw", "softcap_ce_e5m2", "softcap_ce_bf16", "lmhead_ce_fwdbwd",
          "attn_ours_short", "attn_fa2_short", "attn_ours_long", "attn_fa2_long", "attn_ours_paired", "attn_fa2_paired",
          "attnbwd_ours_short", "attnbwd_fa2_short", "attnbwd_ours_long", "attnbwd_fa2_long", "attnbwd_ours_paired", "attnbwd_fa2_paired"]
 

@@ -50,6 +50,8 @@ int mng_rmsnorm_bwd(const void* x, const void* dy, const float* rstd, void* dx, 
 int mng_quant_rows_e4m3(const void* x, void* q, float* scale, long long rows, int cols, void* stream);
 // dst[c, r] = src[r, c] (optionally += ), bf16; 32x32 tiles through shared memory.
 int mng_transpose_bf16(const void* src, void* dst, long long rows, long long cols, int accumulate, void* stream);
+// dst[c, r] = src[r, c] for 1-byte elements (fp8 activations); rows, cols multiples of 64.
+int mng_transpose_u8(const void* src, void* dst, long long rows, long long cols, void* stream);
 // Row-scaled e4m3 quantisation of the transpose: q[c, :] = src[:, c] / s[c], s[c] = amax(src[:, c]) / 448.
 // `amax_scratch`: `cols` 32-bit words of scratch memory owned by the caller.
 int mng_quant_transpose_e4m3(const void* src, void* q, float* scale, unsigned int* amax_scratch, long long rows,

@@ -154,6 +154,15 @@ void transpose(const Tensor& src, Tensor& dst, bool accumulate) {
   g_launches += 1;
 }
 
+Tensor transpose_u8(const Tensor& src) {
+  TORCH_CHECK(src.is_cuda() && src.dim() == 2 && src.is_contiguous() && src.element_size() == 1);
+  c10::cuda::CUDAGuard guard(src.device());
+  Tensor dst = torch::empty({src.size(1), src.size(0)}, src.options());
+  check(mng_transpose_u8(src.data_ptr(), dst.data_ptr(), src.size(0), src.size(1), cur_stream()), "mng_transpose_u8");
+  g_launches += 1;
+  return dst;
+}
+
 // q [cols, rows] e4m3 and scale [cols] of the transpose of src [rows, cols]; `scratch` is cols int32 words.
 void quant_transpose(const Tensor& src, Tensor& q, Tensor& scale, Tensor& scratch) {
   TORCH_CHECK(src.dim() == 2 && src.is_contiguous() && src.scalar_type() == torch::kBFloat16);
@@ -517,6 +526,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("quant_rows", &quant_rows);
   m.def("transpose", &transpose);
   m.def("quant_transpose", &quant_transpose);
+  m.def("transpose_u8", &transpose_u8);
   m.def("softcap_ce", &softcap_ce);
   m.def("adam", &adam);
   m.def("nesterov", &nesterov);

@@ -570,6 +570,7 @@ extern "C" int mng_gemm(const GemmDesc* gp) {
     if (!g.a_mn && !g.b_mn && af == 0 && bf == 0) return launch_store<1, false, false, 0, 0>(g);
     if (!g.a_mn && !g.b_mn && af == 1 && bf == 0) return launch_store<1, false, false, 1, 0>(g);
     if (!g.a_mn && g.b_mn && af == 0 && bf == 0) return launch_store<1, false, true, 0, 0>(g);
+    if (!g.a_mn && g.b_mn && af == 0 && bf == 1) return launch_store<1, false, true, 0, 1>(g);
     if (g.a_mn && g.b_mn && af == 0 && bf == 1) return launch_store<1, true, true, 0, 1>(g);
     if (g.a_mn && g.b_mn && af == 0 && bf == 0) return launch_store<1, true, true, 0, 0>(g);
     return -14;

@@ -249,6 +249,28 @@ extern "C" int mng_quant_rows_e4m3(const void* x, void* q, float* scale, long lo
   DISPATCH_COLS(quant_rows_kernel, (const __nv_bfloat16*)x, (uint8_t*)q, scale, rows, cols);
 }
 
+// dst[c, r] = src[r, c] for 1-byte elements; rows and cols multiples of 64.  64 x 64 tiles through shared memory,
+// 16-byte global accesses on both sides.
+__global__ void __launch_bounds__(256)
+transpose_u8_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, long long rows, long long cols) {
+  __shared__ uint8_t tile[64][64 + 16];
+  const long long r0 = (long long)blockIdx.y * 64, c0 = (long long)blockIdx.x * 64;
+  const int a = threadIdx.x >> 2, seg = threadIdx.x & 3;
+  *reinterpret_cast<uint4*>(&tile[a][seg * 16]) = *reinterpret_cast<const uint4*>(src + (r0 + a) * cols + c0 + seg * 16);
+  __syncthreads();
+  uint8_t v[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = tile[seg * 16 + j][a];
+  *reinterpret_cast<uint4*>(dst + (c0 + a) * rows + r0 + seg * 16) = *reinterpret_cast<const uint4*>(v);
+}
+
+extern "C" int mng_transpose_u8(const void* src, void* dst, long long rows, long long cols, void* stream) {
+  if (rows % 64 || cols % 64) return -1;
+  dim3 grid((unsigned)(cols / 64), (unsigned)(rows / 64));
+  transpose_u8_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>((const uint8_t*)src, (uint8_t*)dst, rows, cols);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
 extern "C" int mng_transpose_bf16(const void* src, void* dst, long long rows, long long cols, int accumulate, void* stream) {
   dim3 grid((unsigned)((cols + 63) / 64), (unsigned)((rows + 63) / 64));
   transpose_bf16_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>((const __nv_bfloat16*)src, (__nv_bfloat16*)dst, rows, cols, accumulate);

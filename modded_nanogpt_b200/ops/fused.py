@@ -270,7 +270,16 @@ class _SoftcapCE(torch.autograd.Function):
         fp8, x_s, w_s, g_s = ctx.cfg
         # dl already carries grad_scale: the caller reduces the losses with .sum() * grad_scale
         dx = gemm(dl, wq, alpha=g_s * w_s)                                           # dl W^T          (T, D)
-        dw = gemm(xq, dl, a_mn=True, b_mn=True, alpha=x_s * g_s)                     # x^T dl          (D, V)
+        if fp8:
+            # 8-bit MN-major operands run at about 60 % of the K-major rate on both sides: transposing the small
+            # [T, D] activation (38 MB) first makes A K-major and the GEMM 1.6x faster
+            if xq.shape[0] % 64 == 0 and xq.shape[1] % 64 == 0:
+                xt = _C().transpose_u8(xq)
+            else:
+                xt = xq.view(torch.uint8).t().contiguous().view(xq.dtype)
+            dw = gemm(xt, dl, b_mn=True, alpha=x_s * g_s)                            # x^T dl          (D, V)
+        else:
+            dw = gemm(xq, dl, a_mn=True, b_mn=True, alpha=x_s * g_s)
         return dx, dw, None, None, None, None, None, None, None, None, None, None
 
 
