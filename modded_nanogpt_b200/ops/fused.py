@@ -240,6 +240,38 @@ def quant_static_e4m3(x: Tensor, scale: float) -> Tensor:
     return (x.float() * (1.0 / scale)).clamp_(-448.0, 448.0).to(torch.float8_e4m3fn)
 
 
+class _Fp8LinearT(torch.autograd.Function):
+    """y = x @ w for a weight stored (in, out), with static per-tensor scales: the reference's `nanogpt::mm_t`
+    op (`train_gpt.py:68-162`).  Forward in e4m3 x e4m3, backward with the incoming gradient in e5m2:
+    grad_x = g w^T in bf16, grad_w = x^T g accumulated and returned in fp32."""
+
+    @staticmethod
+    def forward(ctx, x, w, x_s, w_s, grad_s):
+        x2 = x.reshape(-1, x.shape[-1])
+        x8, w8 = quant_static_e4m3(x2, x_s), quant_static_e4m3(w, w_s)
+        ctx.save_for_backward(x8, w8)
+        ctx.cfg = (x_s, w_s, grad_s, x.shape)
+        return gemm(x8, w8, b_mn=True, alpha=x_s * w_s).view(*x.shape[:-1], w.shape[1])
+
+    @staticmethod
+    def backward(ctx, g):
+        x8, w8 = ctx.saved_tensors
+        x_s, w_s, grad_s, xshape = ctx.cfg
+        g2 = g.reshape(-1, g.shape[-1])
+        g8 = (g2.float() * (1.0 / grad_s)).to(torch.float8_e5m2)
+        gx = gemm(g8, w8, alpha=grad_s * w_s)                                         # [T, out] x [in, out]^T
+        if x8.shape[0] % 64 == 0 and x8.shape[1] % 64 == 0:
+            xt = _C().transpose_u8(x8)
+        else:
+            xt = x8.view(torch.uint8).t().contiguous().view(x8.dtype)
+        gw = gemm(xt, g8, b_mn=True, alpha=x_s * grad_s, out_dtype=torch.float32)     # [in, T] x [T, out]
+        return gx.view(xshape), gw, None, None, None
+
+
+def fp8_linear_t(x: Tensor, w: Tensor, x_s: float, w_s: float, grad_s: float) -> Tensor:
+    return _Fp8LinearT.apply(x, w, float(x_s), float(w_s), float(grad_s))
+
+
 class _SoftcapCE(torch.autograd.Function):
     """x [T,D] bf16 (normed), w [D,V] bf16.  FP8 path: static per-tensor scales x_s, w_s and a
     gradient scale grad_s, as in the reference (`train_gpt.py:1225`)."""

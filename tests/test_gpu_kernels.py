@@ -233,6 +233,24 @@ def test_fused_lm_head_ce(fused, fp8):
     fused.check_status()
 
 
+def test_fp8_linear_t(fused):
+    torch.manual_seed(7)
+    T, D, V = 512, 256, 1024
+    x = (torch.randn(T, D, device="cuda") * 2).to(BF).requires_grad_(True)
+    w = (torch.randn(D, V, device="cuda") * 0.05).to(BF).requires_grad_(True)
+    x_s, w_s, g_s = 8 / 448, 0.25 / 448, 4 / 448
+    y = fused.fp8_linear_t(x, w, x_s, w_s, g_s)
+    g = torch.randn(T, V, device="cuda").to(BF)
+    y.backward(g)
+    xq = (x.float() / x_s).clamp(-448, 448).to(F8).float() * x_s
+    wq = (w.float() / w_s).clamp(-448, 448).to(F8).float() * w_s
+    gq = (g.float() / g_s).to(F8B).float() * g_s
+    assert _rel(y, xq @ wq) < 5e-3
+    assert _rel(x.grad, gq @ wq.T) < 5e-3
+    assert w.grad.dtype == torch.float32 and _rel(w.grad, xq.T @ gq) < 5e-3
+    _ok(fused)
+
+
 def test_adam_kernel(fused):
     from modded_nanogpt_b200.ops import native, reference as ref
     C = native.lib()
