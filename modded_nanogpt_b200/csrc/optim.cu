@@ -40,15 +40,25 @@ adam_kernel(PeerPtrs grads, PeerPtrs params, long long off, float* __restrict__ 
     float g[VEC], p[VEC];
 #pragma unroll
     for (int t = 0; t < VEC; ++t) g[t] = 0.f;
-    for (int r = 0; r < grads.n; ++r) {
-      if constexpr (F32) {
-        float4 x = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(grads.p[r]) + e);
-        g[0] += x.x; g[1] += x.y; g[2] += x.z; g[3] += x.w;
-      } else {
-        float f[8];
-        load8(reinterpret_cast<const __nv_bfloat16*>(grads.p[r]) + e, f);
+    // all peers' loads are issued before the first is consumed: one NVLink round trip instead of grads.n
+    uint4 raw[MNG_MAX_RANKS];
 #pragma unroll
-        for (int t = 0; t < 8; ++t) g[t] += f[t];
+    for (int r = 0; r < MNG_MAX_RANKS; ++r)
+      if (r < grads.n) raw[r] = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(grads.p[r]) + e * (F32 ? 4 : 2));
+#pragma unroll
+    for (int r = 0; r < MNG_MAX_RANKS; ++r) {
+      if (r < grads.n) {
+        if constexpr (F32) {
+          const float* x = reinterpret_cast<const float*>(&raw[r]);
+          g[0] += x[0]; g[1] += x[1]; g[2] += x[2]; g[3] += x[3];
+        } else {
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[r]);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const float2 v2 = __bfloat1622float2(h[t]);
+            g[2 * t] += v2.x; g[2 * t + 1] += v2.y;
+          }
+        }
       }
     }
     if constexpr (F32) {
@@ -105,11 +115,20 @@ nesterov_kernel(PeerPtrs grads, long long off, float* __restrict__ buf, __nv_bfl
     if (i < nvec) {
       mat = i / vec_per_mat;
       float g[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (int r = 0; r < grads.n; ++r) {
-        float f[8];
-        load8(reinterpret_cast<const __nv_bfloat16*>(grads.p[r]) + off + i * 8, f);
+      uint4 raw[MNG_MAX_RANKS];
 #pragma unroll
-        for (int t = 0; t < 8; ++t) g[t] += f[t];
+      for (int r = 0; r < MNG_MAX_RANKS; ++r)
+        if (r < grads.n) raw[r] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(grads.p[r]) + off + i * 8);
+#pragma unroll
+      for (int r = 0; r < MNG_MAX_RANKS; ++r) {
+        if (r < grads.n) {
+          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw[r]);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const float2 v2 = __bfloat1622float2(h2[t]);
+            g[2 * t] += v2.x; g[2 * t + 1] += v2.y;
+          }
+        }
       }
       float b[8], u[8];
       float4 b0 = *reinterpret_cast<const float4*>(buf + i * 8), b1 = *reinterpret_cast<const float4*>(buf + i * 8 + 4);
