@@ -117,11 +117,11 @@ int mng_lincomb_bwd(const LinCombArgs* a, const LinCombGrads* g, const void* gou
 
 int mng_qkv_post_fwd(const void* qkv, const float* cos_t, const float* sin_t, const void* ve, const void* vgate,
                      int vgate_stride, const void* vadd, void* q, void* k, void* v, float* rstd_q, float* rstd_k,
-                     long long T, int H, int paired, int key_offset, void* stream);
+                     long long T, int H, int paired, int key_offset, int split, void* stream);
 int mng_qkv_post_bwd(const void* qkv, const float* cos_t, const float* sin_t, const float* rstd_q, const float* rstd_k,
                      const void* dq, const void* dk, const void* dv, const void* ve, const void* vgate, int vgate_stride,
                      void* d_qkv, void* d_ve, void* d_vgate, int d_vgate_stride, long long T, int H, int paired,
-                     int key_offset, void* stream);
+                     int key_offset, int split, void* stream);
 int mng_xsa_gate_fwd(const void* y, const void* v, const void* alpha, int alpha_stride, const void* gate, int gate_stride,
                      void* out, long long T, int H, void* stream);
 int mng_xsa_gate_bwd(const void* y, const void* v, const void* alpha, int alpha_stride, const void* gate, int gate_stride,

@@ -345,7 +345,7 @@ const void* optr(const OptT& t) { return (t.has_value() && t->defined()) ? t->da
 
 // qkv [T, 3*H*128] bf16 -> q, k, v [T, H, 128] (+ rstd_q, rstd_k [T*H]).  cos/sin fp32 [positions, 32].
 std::vector<Tensor> qkv_post_fwd(const Tensor& qkv, const Tensor& cos_t, const Tensor& sin_t, const OptT& ve, const OptT& vgate,
-                                 const OptT& vadd, int64_t H, bool paired, bool key_offset) {
+                                 const OptT& vadd, int64_t H, bool paired, bool key_offset, bool split) {
   TORCH_CHECK(qkv.dim() == 2 && qkv.is_contiguous() && qkv.scalar_type() == torch::kBFloat16 && qkv.size(1) == 3 * H * 128);
   TORCH_CHECK(cos_t.scalar_type() == torch::kFloat32 && cos_t.is_contiguous() && cos_t.size(1) == 32 && sin_t.sizes() == cos_t.sizes());
   const int64_t T = qkv.size(0);
@@ -363,7 +363,7 @@ std::vector<Tensor> qkv_post_fwd(const Tensor& qkv, const Tensor& cos_t, const T
   if (vadd.has_value() && vadd->defined()) TORCH_CHECK(vadd->is_contiguous() && vadd->numel() == T * H * 128 && vadd->scalar_type() == torch::kBFloat16);
   check(mng_qkv_post_fwd(qkv.data_ptr(), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), optr(ve), optr(vgate), vstride,
                          optr(vadd), q.data_ptr(), k.data_ptr(), v.data_ptr(), rq.data_ptr<float>(), rk.data_ptr<float>(), T,
-                         (int)H, paired, key_offset, cur_stream()),
+                         (int)H, paired, key_offset, split, cur_stream()),
         "mng_qkv_post_fwd");
   g_launches += 1;
   return {q, k, v, rq, rk};
@@ -372,7 +372,7 @@ std::vector<Tensor> qkv_post_fwd(const Tensor& qkv, const Tensor& cos_t, const T
 // Returns d_qkv, d_ve (or undefined), d_vgate [T, H] bf16 (or undefined).
 std::vector<Tensor> qkv_post_bwd(const Tensor& qkv, const Tensor& cos_t, const Tensor& sin_t, const Tensor& rq, const Tensor& rk,
                                  const Tensor& dq, const Tensor& dk, const Tensor& dv, const OptT& ve, const OptT& vgate,
-                                 int64_t H, bool paired, bool key_offset, bool need_dve, bool need_dvgate) {
+                                 int64_t H, bool paired, bool key_offset, bool need_dve, bool need_dvgate, bool split) {
   const int64_t T = qkv.size(0);
   TORCH_CHECK(dq.is_contiguous() && dk.is_contiguous() && dv.is_contiguous());
   c10::cuda::CUDAGuard guard(qkv.device());
@@ -384,7 +384,7 @@ std::vector<Tensor> qkv_post_bwd(const Tensor& qkv, const Tensor& cos_t, const T
   check(mng_qkv_post_bwd(qkv.data_ptr(), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), rq.data_ptr<float>(),
                          rk.data_ptr<float>(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), optr(ve), optr(vgate), vstride,
                          dqkv.data_ptr(), dve.defined() ? dve.data_ptr() : nullptr, dvg.defined() ? dvg.data_ptr() : nullptr,
-                         (int)H, T, (int)H, paired, key_offset, cur_stream()),
+                         (int)H, T, (int)H, paired, key_offset, split, cur_stream()),
         "mng_qkv_post_bwd");
   g_launches += 1;
   return {dqkv, dve, dvg};

@@ -128,8 +128,11 @@ lincomb_bwd_kernel(LinCombArgs a, LinCombGrads gr, const __nv_bfloat16* __restri
 
 // =====================================================================================================
 // QKV post-processing.  One warp per (token, head) row of 128 elements; lane l owns dims 4l..4l+3.
-//   q,k: RMSNorm over the head (eps = fp32 epsilon), rotary on dims 0..63 with interleaved pairs,
-//        optional key offset: k[t, 64:] <- k_normed[t-1, 64:] for t >= 1;
+//   q,k: RMSNorm over the head (eps = fp32 epsilon), rotary, optional key offset;
+//        layout 0 (track 1): dims 0..63 rotate as interleaved pairs (2i, 2i+1), dims 64..127 are stationary;
+//                            key offset: k[t, 64:] <- k_normed[t-1, 64:] for t >= 1;
+//        layout 1 (track 2, split halves): dim d < 32 rotates with dim d + 64, dims 32..63 and 96..127 are
+//                            stationary and are the ones the key offset takes from the previous token;
 //   v  : v + vgate[t,h] * ve[t,h,:] + vadd[t,h,:]   (both optional).
 // cos/sin: fp32 [positions, 32].  position = t, or 2t + (h & 1) for paired-head layers.
 constexpr int QP_WARPS = 8;
@@ -140,7 +143,7 @@ qkv_post_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, const float* __restri
                     const __nv_bfloat16* __restrict__ ve, const __nv_bfloat16* __restrict__ vgate, int vgate_stride,
                     const __nv_bfloat16* __restrict__ vadd, __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ k,
                     __nv_bfloat16* __restrict__ v, float* __restrict__ rstd_q, float* __restrict__ rstd_k, long long T, int H,
-                    int paired, int key_offset) {
+                    int paired, int key_offset, int split) {
   const int lane = threadIdx.x & 31;
   const long long idx = (long long)blockIdx.x * QP_WARPS + (threadIdx.x >> 5);     // (t, h)
   if (idx >= T * H) return;
@@ -149,9 +152,17 @@ qkv_post_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, const float* __restri
   const long long ld = 3LL * H * 128;
   const long long pos = paired ? 2 * t + (h & 1) : t;
   float cs[2] = {1.f, 1.f}, sn[2] = {0.f, 0.f};
-  if (lane < 16) {
+  float c4[4] = {1.f, 1.f, 1.f, 1.f}, s4[4] = {0.f, 0.f, 0.f, 0.f};
+  const bool rot = split ? ((lane & 15) < 8) : (lane < 16);      // lanes whose dims rotate
+  if (!split && lane < 16) {
     cs[0] = cos_t[pos * 32 + 2 * lane]; cs[1] = cos_t[pos * 32 + 2 * lane + 1];
     sn[0] = sin_t[pos * 32 + 2 * lane]; sn[1] = sin_t[pos * 32 + 2 * lane + 1];
+  }
+  if (split && rot) {
+    const float4 c = *reinterpret_cast<const float4*>(cos_t + pos * 32 + 4 * (lane & 7));
+    const float4 s = *reinterpret_cast<const float4*>(sin_t + pos * 32 + 4 * (lane & 7));
+    c4[0] = c.x; c4[1] = c.y; c4[2] = c.z; c4[3] = c.w;
+    s4[0] = s.x; s4[1] = s.y; s4[2] = s.z; s4[3] = s.w;
   }
 #pragma unroll
   for (int which = 0; which < 2; ++which) {        // 0 = q, 1 = k
@@ -166,7 +177,14 @@ qkv_post_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, const float* __restri
     float n0 = __bfloat162float(__float2bfloat16(a.x * r)), n1 = __bfloat162float(__float2bfloat16(a.y * r));
     float n2 = __bfloat162float(__float2bfloat16(b.x * r)), n3 = __bfloat162float(__float2bfloat16(b.y * r));
     float o0, o1, o2, o3;
-    if (lane < 16) {      // pairs (x0,x1): x0' = c x0 + s x1, x1' = c x1 - s x0
+    // split layout: the partner values live 16 lanes away (dims d and d + 64)
+    const float p0 = __shfl_xor_sync(0xffffffffu, n0, 16), p1 = __shfl_xor_sync(0xffffffffu, n1, 16);
+    const float p2 = __shfl_xor_sync(0xffffffffu, n2, 16), p3 = __shfl_xor_sync(0xffffffffu, n3, 16);
+    if (split && rot) {   // x1' = c x1 + s x2 (lanes 0-7), x2' = c x2 - s x1 (lanes 16-23)
+      const float sg = lane < 16 ? 1.f : -1.f;
+      o0 = c4[0] * n0 + sg * s4[0] * p0; o1 = c4[1] * n1 + sg * s4[1] * p1;
+      o2 = c4[2] * n2 + sg * s4[2] * p2; o3 = c4[3] * n3 + sg * s4[3] * p3;
+    } else if (!split && lane < 16) {      // pairs (x0,x1): x0' = c x0 + s x1, x1' = c x1 - s x0
       o0 = cs[0] * n0 + sn[0] * n1; o1 = cs[0] * n1 - sn[0] * n0;
       o2 = cs[1] * n2 + sn[1] * n3; o3 = cs[1] * n3 - sn[1] * n2;
     } else {
@@ -188,7 +206,7 @@ qkv_post_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, const float* __restri
       float2 pa = __bfloat1622float2(ph[0]), pb = __bfloat1622float2(ph[1]);
       const float pss = warp_sum(pa.x * pa.x + pa.y * pa.y + pb.x * pb.x + pb.y * pb.y);
       const float pr = rsqrtf(pss * (1.f / 128.f) + HEAD_EPS);
-      if (lane >= 16) { o0 *= pr; o1 *= pr; o2 *= pr; o3 *= pr; }
+      if (!rot) { o0 *= pr; o1 *= pr; o2 *= pr; o3 *= pr; }
     }
     uint2 w;
     w.x = pack_bf16x2(o0, o1); w.y = pack_bf16x2(o2, o3);
@@ -226,7 +244,7 @@ qkv_post_bwd_kernel(const __nv_bfloat16* __restrict__ qkv, const float* __restri
                     const __nv_bfloat16* __restrict__ dk, const __nv_bfloat16* __restrict__ dv, const __nv_bfloat16* __restrict__ ve,
                     const __nv_bfloat16* __restrict__ vgate, int vgate_stride, __nv_bfloat16* __restrict__ d_qkv,
                     __nv_bfloat16* __restrict__ d_ve, __nv_bfloat16* __restrict__ d_vgate, int d_vgate_stride, long long T, int H,
-                    int paired, int key_offset) {
+                    int paired, int key_offset, int split) {
   const int lane = threadIdx.x & 31;
   const long long idx = (long long)blockIdx.x * QP_WARPS + (threadIdx.x >> 5);
   if (idx >= T * H) return;
@@ -235,9 +253,17 @@ qkv_post_bwd_kernel(const __nv_bfloat16* __restrict__ qkv, const float* __restri
   const long long ld = 3LL * H * 128;
   const long long pos = paired ? 2 * t + (h & 1) : t;
   float cs[2] = {1.f, 1.f}, sn[2] = {0.f, 0.f};
-  if (lane < 16) {
+  float c4[4] = {1.f, 1.f, 1.f, 1.f}, s4[4] = {0.f, 0.f, 0.f, 0.f};
+  const bool rot = split ? ((lane & 15) < 8) : (lane < 16);
+  if (!split && lane < 16) {
     cs[0] = cos_t[pos * 32 + 2 * lane]; cs[1] = cos_t[pos * 32 + 2 * lane + 1];
     sn[0] = sin_t[pos * 32 + 2 * lane]; sn[1] = sin_t[pos * 32 + 2 * lane + 1];
+  }
+  if (split && rot) {
+    const float4 c = *reinterpret_cast<const float4*>(cos_t + pos * 32 + 4 * (lane & 7));
+    const float4 s = *reinterpret_cast<const float4*>(sin_t + pos * 32 + 4 * (lane & 7));
+    c4[0] = c.x; c4[1] = c.y; c4[2] = c.z; c4[3] = c.w;
+    s4[0] = s.x; s4[1] = s.y; s4[2] = s.z; s4[3] = s.w;
   }
 #pragma unroll
   for (int which = 0; which < 2; ++which) {
@@ -246,7 +272,13 @@ qkv_post_bwd_kernel(const __nv_bfloat16* __restrict__ qkv, const float* __restri
     const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&gu);
     float2 ga = __bfloat1622float2(gh[0]), gb = __bfloat1622float2(gh[1]);
     float d0, d1, d2, d3;                    // gradient w.r.t. the normalised (pre-rotary) values
-    if (lane < 16) {                         // transpose of the rotation
+    const float q0 = __shfl_xor_sync(0xffffffffu, ga.x, 16), q1 = __shfl_xor_sync(0xffffffffu, ga.y, 16);
+    const float q2 = __shfl_xor_sync(0xffffffffu, gb.x, 16), q3 = __shfl_xor_sync(0xffffffffu, gb.y, 16);
+    if (split && rot) {                      // transpose of [c s; -s c] over the (d, d + 64) pairs
+      const float sg = lane < 16 ? -1.f : 1.f;
+      d0 = c4[0] * ga.x + sg * s4[0] * q0; d1 = c4[1] * ga.y + sg * s4[1] * q1;
+      d2 = c4[2] * gb.x + sg * s4[2] * q2; d3 = c4[3] * gb.y + sg * s4[3] * q3;
+    } else if (!split && lane < 16) {        // transpose of the rotation
       d0 = cs[0] * ga.x - sn[0] * ga.y; d1 = cs[0] * ga.y + sn[0] * ga.x;
       d2 = cs[1] * gb.x - sn[1] * gb.y; d3 = cs[1] * gb.y + sn[1] * gb.x;
     } else if (which == 1 && key_offset) {
@@ -423,25 +455,25 @@ extern "C" int mng_lincomb_bwd(const LinCombArgs* a, const LinCombGrads* g, cons
 
 extern "C" int mng_qkv_post_fwd(const void* qkv, const float* cos_t, const float* sin_t, const void* ve, const void* vgate,
                                 int vgate_stride, const void* vadd, void* q, void* k, void* v, float* rstd_q, float* rstd_k,
-                                long long T, int H, int paired, int key_offset, void* stream) {
+                                long long T, int H, int paired, int key_offset, int split, void* stream) {
   if (T == 0) return 0;
   const unsigned grid = (unsigned)((T * H + QP_WARPS - 1) / QP_WARPS);
   qkv_post_fwd_kernel<<<grid, QP_WARPS * 32, 0, (cudaStream_t)stream>>>(
       (const __nv_bfloat16*)qkv, cos_t, sin_t, (const __nv_bfloat16*)ve, (const __nv_bfloat16*)vgate, vgate_stride,
-      (const __nv_bfloat16*)vadd, (__nv_bfloat16*)q, (__nv_bfloat16*)k, (__nv_bfloat16*)v, rstd_q, rstd_k, T, H, paired, key_offset);
+      (const __nv_bfloat16*)vadd, (__nv_bfloat16*)q, (__nv_bfloat16*)k, (__nv_bfloat16*)v, rstd_q, rstd_k, T, H, paired, key_offset, split);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
 extern "C" int mng_qkv_post_bwd(const void* qkv, const float* cos_t, const float* sin_t, const float* rstd_q, const float* rstd_k,
                                 const void* dq, const void* dk, const void* dv, const void* ve, const void* vgate,
                                 int vgate_stride, void* d_qkv, void* d_ve, void* d_vgate, int d_vgate_stride, long long T, int H,
-                                int paired, int key_offset, void* stream) {
+                                int paired, int key_offset, int split, void* stream) {
   if (T == 0) return 0;
   const unsigned grid = (unsigned)((T * H + QP_WARPS - 1) / QP_WARPS);
   qkv_post_bwd_kernel<<<grid, QP_WARPS * 32, 0, (cudaStream_t)stream>>>(
       (const __nv_bfloat16*)qkv, cos_t, sin_t, rstd_q, rstd_k, (const __nv_bfloat16*)dq, (const __nv_bfloat16*)dk,
       (const __nv_bfloat16*)dv, (const __nv_bfloat16*)ve, (const __nv_bfloat16*)vgate, vgate_stride, (__nv_bfloat16*)d_qkv,
-      (__nv_bfloat16*)d_ve, (__nv_bfloat16*)d_vgate, d_vgate_stride, T, H, paired, key_offset);
+      (__nv_bfloat16*)d_ve, (__nv_bfloat16*)d_vgate, d_vgate_stride, T, H, paired, key_offset, split);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 

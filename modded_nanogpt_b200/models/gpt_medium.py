@@ -149,6 +149,8 @@ class GPTMedium(nn.Module):
     # -- forward ---------------------------------------------------------------------------------
     def forward(self, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, bigram_input_seq: Tensor | None,
                 schedule_cfg: ForwardScheduleConfig) -> Tensor:
+        if self._fused_ok(input_seq):
+            return self._forward_fused(input_seq, target_seq, seqlens, schedule_cfg)
         L, H, Dh, D, V = self.num_layers, self.num_heads, self.head_dim, self.model_dim, self.vocab_size
         T = input_seq.size(0)
         max_len = schedule_cfg.train_max_seq_len if self.training else self.eval_seq_len
@@ -208,6 +210,100 @@ class GPTMedium(nn.Module):
         a, b, c = self.softcap
         if self.training:
             return ops.softcap_ce(x, self.lm_head.weight, target_seq, schedule_cfg.mtp_weights, None, None, a, b, c,
+                                  grad_scale=self.grad_scale, fp8=self.use_fp8)
+        return ops.softcap_ce_eval(x, self.lm_head.weight, target_seq, a, b, c)
+
+
+    # -- CUDA execution path: the same math through the fused sm_100a kernels --------------------------
+    def _fused_ok(self, x: Tensor) -> bool:
+        from .. import ops as ops_pkg
+        return (x.is_cuda and ops_pkg.get_backend() != "reference" and self.head_dim == 128 and self.model_dim % 256 == 0
+                and self.model_dim <= 1024 and self.lm_head.weight.dtype == torch.bfloat16 and ops_pkg.use_kernel("glue", x))
+
+    def _forward_fused(self, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, sc: ForwardScheduleConfig) -> Tensor:
+        """`forward` with every residual / gate / norm / rotary step on the fused kernels (`ops.glue`,
+        `ops.fused`) and, in training, weight and embedding gradients accumulated straight into the
+        parameters' `.grad` buffers (no full-bank temporaries from slicing the parameter banks)."""
+        from ..ops import fused
+        from ..ops.glue import Term, embed_direct, lincomb, qkv_post, xsa_gate
+        L, H, Dh, D, V = self.num_layers, self.num_heads, self.head_dim, self.model_dim, self.vocab_size
+        T = input_seq.size(0)
+        max_len = sc.train_max_seq_len if self.training else self.eval_seq_len
+        resid = self.scalars[:L]
+        sa = self.scalars[L:3 * L].view(L, 2)
+        smear_lambda, backout_lambda = self.scalars[3 * L], self.scalars[3 * L + 1]
+        skip_lambdas = self.scalars[3 * L + 2:3 * L + 5]
+        x0l = self.x0_lambdas.view(L, 2)
+        direct = self.training and torch.is_grad_enabled()
+        w_all = self.attn_bank[:4 * L].view(L, 4 * D, D)
+        g_all = None
+        if direct:
+            for p in (self.attn_bank, self.mlp_bank, self.embed.weight, self.embed2.weight, self.value_embeds):
+                if p.grad is None:
+                    p.grad = torch.zeros_like(p)
+            g_all = self.attn_bank.grad[:4 * L].view(L, 4 * D, D)
+        ids = input_seq.long()
+        gather = (lambda i, w: embed_direct(i, w, w.grad)) if direct else F.embedding
+        x = gather(ids, self.embed.weight)
+        offs = torch.arange(5, device=ids.device)[:, None] * V
+        ve = gather((ids[None, :] + offs).reshape(-1), self.value_embeds).view(5, T, D).unbind(0)
+        g = torch.zeros(T, 1, dtype=x.dtype, device=x.device)
+        g[1:] = smear_lambda * torch.sigmoid(F.linear(x[1:, :16], self.smear_gate.weight))
+        x = lincomb([Term(x), Term(torch.cat([x[:1], x[:-1]]), gate=g, col=0)])
+        x = x0 = fused.rms_norm(x)
+        x02 = fused.rms_norm(gather(ids, self.embed2.weight))
+        cos, sin = self.yarn.tables(T)
+        cos_t, sin_t = cos[:, :32].contiguous(), sin[:, :32].contiguous()
+        bounds = fused.doc_bounds(seqlens, T) if fused.ATTN_KERNEL else None
+        skips, x_backout, skip_idx = [], None, 0
+        for i in range(L):
+            terms = []
+            if i in SKIP_OUT:
+                sg = (torch.sigmoid(skip_lambdas[skip_idx]) * 2 * torch.sigmoid(F.linear(x0[:, :16], self.skip_gates[skip_idx]).float())
+                      ).to(x.dtype)                                                  # [T, 1]
+                skip_idx += 1
+                terms.append(Term(skips.pop(), scalar=resid[i].reshape(1), gate=sg, col=0))
+            if i == 0:
+                terms += [Term(x, scalar=(resid[0] + x0l[0, 0]).reshape(1)), Term(x02, scalar=x0l[0, 1].reshape(1))]
+            else:
+                terms += [Term(x, scalar=resid[i].reshape(1)), Term(x0, scalar=x0l[i, 0].reshape(1)),
+                          Term(x02, scalar=x0l[i, 1].reshape(1))]
+            x = lincomb(terms)
+            xin = fused.rms_norm(x)
+            is_long = i in LONG_LAYERS
+            if direct:
+                qkv = fused.bank_linear(xin, sa[i, 0], [w_all[i][:3 * D]], [g_all[i][:3 * D]])
+            else:
+                qkv = F.linear(xin, sa[i, 0] * w_all[i][:3 * D])
+            ve_t = vgate = None
+            if i in VE_LAYERS:
+                ve_t = ve[VE_LAYERS[i]]
+                vgate = (2 * torch.sigmoid(F.linear(xin[:, :16], self.value_embed_gate_bank[self._ve_slot[i]]))).contiguous()
+            q, k, v = qkv_post(qkv, cos_t, sin_t, ve_t, vgate, None, H, False, is_long, split=True)
+            window = sc.ws_long if is_long else sc.ws_short
+            y = ops.attention(q, k, v, seqlens, window, self.yarn.attn_scale, max_len, bounds)
+            agate = torch.sigmoid(F.linear(xin[:, :16], self.attn_gate_bank[i])).contiguous()
+            y = xsa_gate(y, v, None, agate)
+            if direct:
+                attn_out = fused.bank_linear(y.reshape(T, D), sa[i, 1], [w_all[i][3 * D:]], [g_all[i][3 * D:]])
+            else:
+                attn_out = F.linear(y.reshape(T, D), sa[i, 1] * w_all[i][3 * D:])
+            x = lincomb([Term(x), Term(attn_out)])
+            st = self._fp8_state.layer(i) if (self.training and self.use_fp8 and self._fp8_state is not None) else None
+            if direct:
+                h = fused.norm_relu2_mlp(x, self.mlp_bank[i, 0], self.mlp_bank[i, 1], st, (self.mlp_bank.grad[i, 0], self.mlp_bank.grad[i, 1]))
+            else:
+                h = ops.norm_relu2_mlp(x, self.mlp_bank[i, 0], self.mlp_bank[i, 1], st)
+            x = lincomb([Term(x), Term(h)])
+            if i in SKIP_IN:
+                skips.append(x)
+            if i == BACKOUT_LAYER:
+                x_backout = x
+        x = lincomb([Term(x), Term(x_backout, scalar=(-backout_lambda).reshape(1))])
+        x = fused.rms_norm(x)
+        a, b, c = self.softcap
+        if self.training:
+            return ops.softcap_ce(x, self.lm_head.weight, target_seq, sc.mtp_weights, None, None, a, b, c,
                                   grad_scale=self.grad_scale, fp8=self.use_fp8)
         return ops.softcap_ce_eval(x, self.lm_head.weight, target_seq, a, b, c)
 

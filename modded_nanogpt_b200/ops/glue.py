@@ -91,34 +91,35 @@ def lincomb(terms: list[Term]) -> Tensor:
 
 class _QkvPost(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, qkv, cos_t, sin_t, ve, vgate, vadd, H, paired, key_offset):
+    def forward(ctx, qkv, cos_t, sin_t, ve, vgate, vadd, H, paired, key_offset, split=False):
         qkv = qkv.contiguous()
         if ve is not None:
             ve = ve.contiguous()
         if vadd is not None:
             vadd = vadd.contiguous()
-        q, k, v, rq, rk = lib().qkv_post_fwd(qkv, cos_t, sin_t, ve, vgate, vadd, H, paired, key_offset)
+        q, k, v, rq, rk = lib().qkv_post_fwd(qkv, cos_t, sin_t, ve, vgate, vadd, H, paired, key_offset, split)
         ctx.save_for_backward(qkv, cos_t, sin_t, rq, rk, ve, vgate)
-        ctx.cfg = (H, paired, key_offset, vadd is not None)
+        ctx.cfg = (H, paired, key_offset, vadd is not None, split)
         return q, k, v
 
     @staticmethod
     def backward(ctx, dq, dk, dv):
         qkv, cos_t, sin_t, rq, rk, ve, vgate = ctx.saved_tensors
-        H, paired, key_offset, has_vadd = ctx.cfg
+        H, paired, key_offset, has_vadd, split = ctx.cfg
         dv = dv.contiguous()
         need_dve = ve is not None and ctx.needs_input_grad[3]
         need_dvg = vgate is not None and ctx.needs_input_grad[4]
         dqkv, dve, dvg = lib().qkv_post_bwd(qkv, cos_t, sin_t, rq, rk, dq.contiguous(), dk.contiguous(), dv, ve, vgate, H,
-                                            paired, key_offset, need_dve, need_dvg)
+                                            paired, key_offset, need_dve, need_dvg, split)
         dvadd = dv.view(qkv.shape[0], -1) if has_vadd else None
-        return dqkv, None, None, dve, dvg, dvadd, None, None, None
+        return dqkv, None, None, dve, dvg, dvadd, None, None, None, None
 
 
 def qkv_post(qkv: Tensor, cos_t: Tensor, sin_t: Tensor, ve: Tensor | None, vgate: Tensor | None, vadd: Tensor | None,
-             H: int, paired: bool, key_offset: bool):
-    """qkv [T, 3*H*128] -> q, k, v [T, H, 128].  v = v + vgate[t,h]*ve[t,h,:] + vadd[t,h,:]."""
-    return _QkvPost.apply(qkv, cos_t, sin_t, ve, vgate, vadd, H, paired, key_offset)
+             H: int, paired: bool, key_offset: bool, split: bool = False):
+    """qkv [T, 3*H*128] -> q, k, v [T, H, 128].  v = v + vgate[t,h]*ve[t,h,:] + vadd[t,h,:].
+    `split`: rotary pairs are (d, d + 64) for d < 32 (track-2 layout) instead of interleaved (2i, 2i+1) for i < 32."""
+    return _QkvPost.apply(qkv, cos_t, sin_t, ve, vgate, vadd, H, paired, key_offset, split)
 
 
 class _XsaGate(torch.autograd.Function):
