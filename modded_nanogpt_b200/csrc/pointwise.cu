@@ -183,13 +183,39 @@ transpose_bf16_kernel(const __nv_bfloat16* __restrict__ src, __nv_bfloat16* __re
 // Column amax of a [rows, cols] bf16 matrix (atomic max on float bits), then quantise the transpose.
 __global__ void __launch_bounds__(256)
 col_amax_kernel(const __nv_bfloat16* __restrict__ src, unsigned int* __restrict__ amax_bits, long long rows, long long cols) {
-  const long long c = (long long)blockIdx.x * 64 + (threadIdx.x & 63);
-  const int ty = threadIdx.x >> 6;
-  const long long r_begin = (long long)blockIdx.y * 256;
-  float m = 0.f;
-  if (c < cols)
-    for (long long r = r_begin + ty; r < rows && r < r_begin + 256; r += 4) m = fmaxf(m, fabsf(__bfloat162float(src[r * cols + c])));
-  if (c < cols && m > 0.f) atomicMax(amax_bits + c, __float_as_uint(m));
+  // Block = 256 columns x 64 rows; a warp reads one row segment of 256 columns with 16-byte loads, the eight
+  // warps' maxima are combined in shared memory, one atomic per column and block.  Ragged column edges (cols
+  // not a multiple of 8) take the scalar path.
+  __shared__ float part[8][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long c0 = (long long)blockIdx.x * 256 + lane * 8;
+  const long long r_begin = (long long)blockIdx.y * 64;
+  float m[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  const bool vec = (cols % 8 == 0) && c0 + 8 <= cols;
+  for (long long r = r_begin + warp; r < rows && r < r_begin + 64; r += 8) {
+    if (vec) {
+      const uint4 u = *reinterpret_cast<const uint4*>(src + r * cols + c0);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float2 f = __bfloat1622float2(h[t]);
+        m[2 * t] = fmaxf(m[2 * t], fabsf(f.x));
+        m[2 * t + 1] = fmaxf(m[2 * t + 1], fabsf(f.y));
+      }
+    } else {
+#pragma unroll
+      for (int t = 0; t < 8; ++t)
+        if (c0 + t < cols) m[t] = fmaxf(m[t], fabsf(__bfloat162float(src[r * cols + c0 + t])));
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < 8; ++t) part[warp][lane * 8 + t] = m[t];
+  __syncthreads();
+  float best = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) best = fmaxf(best, part[w][threadIdx.x]);
+  const long long c = (long long)blockIdx.x * 256 + threadIdx.x;
+  if (c < cols && best > 0.f) atomicMax(amax_bits + c, __float_as_uint(best));
 }
 
 __global__ void __launch_bounds__(256)
@@ -282,7 +308,7 @@ extern "C" int mng_quant_transpose_e4m3(const void* src, void* q, float* scale, 
                                         long long cols, void* stream) {
   cudaStream_t s = (cudaStream_t)stream;
   if (cudaMemsetAsync(amax_scratch, 0, sizeof(unsigned int) * cols, s) != cudaSuccess) return -3;
-  dim3 g1((unsigned)((cols + 63) / 64), (unsigned)((rows + 255) / 256));
+  dim3 g1((unsigned)((cols + 255) / 256), (unsigned)((rows + 63) / 64));
   col_amax_kernel<<<g1, 256, 0, s>>>((const __nv_bfloat16*)src, amax_scratch, rows, cols);
   dim3 g2((unsigned)((cols + 63) / 64), (unsigned)((rows + 63) / 64));
   quant_transpose_kernel<<<g2, 256, 0, s>>>((const __nv_bfloat16*)src, (uint8_t*)q, amax_scratch, scale, rows, cols);
@@ -329,7 +355,7 @@ extern "C" int mng_quant_transpose_e4m3_static(const void* src, void* q, float* 
   cudaStream_t s = (cudaStream_t)stream;
   // the array still holds the previous call's maxima: clear the words this call will use
   if (cudaMemsetAsync(scratch, 0, sizeof(unsigned int) * cols, s) != cudaSuccess) return MNG_ERR_LAUNCH;
-  dim3 g1((unsigned)((cols + 63) / 64), (unsigned)((rows + 255) / 256));
+  dim3 g1((unsigned)((cols + 255) / 256), (unsigned)((rows + 63) / 64));
   mng::col_amax_kernel<<<g1, 256, 0, s>>>((const __nv_bfloat16*)src, scratch, rows, cols);
   dim3 g2((unsigned)((cols + 63) / 64), (unsigned)((rows + 63) / 64));
   mng::quant_transpose_kernel<<<g2, 256, 0, s>>>((const __nv_bfloat16*)src, (uint8_t*)q, scratch, scale, rows, cols);
