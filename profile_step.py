@@ -13,11 +13,48 @@ import time
 sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
 
+def phases(tr, env, n_steps):
+    """Device time (CUDA events, this rank) of: first input copy + bookkeeping, micro-steps, optimizer step, FP8 weight
+    refresh; averaged separately over Adam steps (odd) and NorMuon-only steps (even)."""
+    import json
+    import torch
+    m = tr.manager
+    rows, step = [], 850
+    for _ in range(n_steps):
+        env.barrier()
+        torch.cuda.synchronize()
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        e[0].record()
+        m.advance_schedule(step)
+        b = tr.train_loader.next_batch()
+        e[1].record()
+        for i in range(env.grad_accum_steps):
+            tr.micro_step(b, step)
+            if i + 1 < env.grad_accum_steps:
+                b = tr.train_loader.next_batch()
+        e[2].record()
+        m.step_optimizers(step)
+        e[3].record()
+        tr.model.quantize_mlp_fp8(bootstrap_down=False)
+        e[4].record()
+        torch.cuda.synchronize()
+        rows.append(dict(adam=step % 2, inputs=e[0].elapsed_time(e[1]), micro_steps=e[1].elapsed_time(e[2]),
+                         optimizer=e[2].elapsed_time(e[3]), fp8_refresh=e[3].elapsed_time(e[4]), total=e[0].elapsed_time(e[4])))
+        step += 1
+    if env.master:
+        for parity, name in ((1, "adam step"), (0, "normuon-only step")):
+            sel = [r for r in rows if r["adam"] == parity]
+            if sel:
+                print(name, json.dumps({k: round(sum(r[k] for r in sel) / len(sel), 3) for k in sel[0] if k != "adam"}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--micro-steps", type=int, default=2)
     ap.add_argument("--rows", type=int, default=60)
     ap.add_argument("--eager", action="store_true", help="profile the eager micro-step instead of the graph replay")
+    ap.add_argument("--phases", type=int, default=0,
+                    help="instead of the kernel table: CUDA-event time of the phases of N full steps (works under torchrun)")
     a = ap.parse_args()
     import torch
     from torch.autograd import DeviceType
@@ -31,7 +68,10 @@ def main():
     env = init_distributed(accum_base=8)
     sched = TrainingSchedule(track1_stages(), 1270, 15, cooldown_frac=0.6)
     root = "/tmp/mng_profile_data"
-    write_synthetic_corpus(root, train_tokens=12_000_000, val_tokens=1_000_000, seed=0, max_doc_len=2048)
+    if env.master:
+        write_synthetic_corpus(root, train_tokens=12_000_000 if not a.phases else 393216 * (a.phases + 8), val_tokens=1_000_000,
+                               seed=0, max_doc_len=2048)
+    env.barrier()
     hp = Hyperparameters(data_path=root, val_loss_every=0)
     tr = Trainer(track1_model(262144), sched, hp, env, use_cuda_graphs=not a.eager,
                  logger=RunLogger("profile", True, log_dir="/tmp/mng_logs", quiet=True))
@@ -39,7 +79,7 @@ def main():
         tr.manager.advance_schedule(b0)
     tr.manager.optimizer.split_embed = True
     tr.train_loader = tr.make_train_loader()
-    tr.train_loader.reparameterise(393216, 2048, 8)
+    tr.train_loader.reparameterise(393216, 2048, env.grad_accum_steps)
     m = tr.manager
 
     def micro(step):
@@ -50,6 +90,8 @@ def main():
     m.step_optimizers(849)
     tr.model.quantize_mlp_fp8(False)
     torch.cuda.synchronize()
+    if a.phases:
+        return phases(tr, env, a.phases)
     t = time.time()
     for _ in range(4):
         micro(850)
