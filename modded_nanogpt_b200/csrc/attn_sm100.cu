@@ -510,15 +510,19 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tx1, const __grid_constant__
           const uint64_t dY1 = dYk + ((st * 2 * ATB_YTILE) >> 4), dY2 = dY1 + (ATB_YTILE >> 4);
           if (!mbar_wait(&y_full[st], (n / ATB_STAGES) & 1, abort_flag)) { ATB_FAIL(ERR_WAIT_TMA_FULL); ok = false; break; }
           tc_fence_after();
+          {
+            const uint32_t x1l = (uint32_t)dX1, x1h = (uint32_t)(dX1 >> 32), x2l = (uint32_t)dX2, x2h = (uint32_t)(dX2 >> 32);
+            const uint32_t y1l = (uint32_t)dY1, y1h = (uint32_t)(dY1 >> 32), y2l = (uint32_t)dY2, y2h = (uint32_t)(dY2 >> 32);
+            const uint32_t dS = tm_S + b * ATB_BLK, dD = tm_dP + b * ATB_BLK;
+#define ATB_XO(k) ((((k) >> 2) * 16384 + ((k) & 3) * 32) >> 4)
+#define ATB_YO(k) ((((k) >> 2) * (ATB_YTILE / 2) + ((k) & 3) * 32) >> 4)
+            umma_f16_lo<false>(dS, x1l + ATB_XO(0), x1h, y1l + ATB_YO(0), y1h, IDESC_SS);
+            umma_f16_lo<false>(dD, x2l + ATB_XO(0), x2h, y2l + ATB_YO(0), y2h, IDESC_SS);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const uint32_t xo = ((k >> 2) * 16384 + (k & 3) * 32) >> 4, yo = ((k >> 2) * (ATB_YTILE / 2) + (k & 3) * 32) >> 4;
-            umma_f16(tm_S + b * ATB_BLK, dX1 + xo, dY1 + yo, IDESC_SS, k != 0);
-          }
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const uint32_t xo = ((k >> 2) * 16384 + (k & 3) * 32) >> 4, yo = ((k >> 2) * (ATB_YTILE / 2) + (k & 3) * 32) >> 4;
-            umma_f16(tm_dP + b * ATB_BLK, dX2 + xo, dY2 + yo, IDESC_SS, k != 0);
+            for (int k = 1; k < 8; ++k) {
+              umma_f16_lo<true>(dS, x1l + ATB_XO(k), x1h, y1l + ATB_YO(k), y1h, IDESC_SS);
+              umma_f16_lo<true>(dD, x2l + ATB_XO(k), x2h, y2l + ATB_YO(k), y2h, IDESC_SS);
+            }
           }
           umma_commit(&sdp_full[b]);
         }
@@ -527,14 +531,20 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tx1, const __grid_constant__
           const uint64_t dY1 = dYm + ((st * 2 * ATB_YTILE) >> 4), dY2 = dY1 + (ATB_YTILE >> 4);
           if (!mbar_wait(&pds_ready[b], (m >> 1) & 1, abort_flag)) { ATB_FAIL(ERR_WAIT_TMEM_EMPTY); ok = false; break; }
           tc_fence_after();
-#pragma unroll
-          for (int k = 0; k < ATB_BLK / 16; ++k) {           // 16 stream rows per MMA: 8 TMEM columns of packed bf16
-            const uint32_t acol = b * ATB_BLK + k * 16;          // warp quarter k packed its 16 columns into 8
-            if (DKV) {
-              umma_f16_ts(tm_A2, tm_S + acol, dY2 + ((k * 2048) >> 4), IDESC_TS, (m | k) != 0);    // dV += P^T dO
-              umma_f16_ts(tm_A1, tm_dP + acol, dY1 + ((k * 2048) >> 4), IDESC_TS, (m | k) != 0);   // dK += dS^T Q
+          {                                                   // 16 stream rows per MMA: 8 TMEM columns of packed bf16
+            const uint32_t y1l = (uint32_t)dY1, y1h = (uint32_t)(dY1 >> 32), y2l = (uint32_t)dY2, y2h = (uint32_t)(dY2 >> 32);
+#define ATB_ACOL(k) (b * ATB_BLK + (k) * 16)
+            if (m == 0) {
+              if (DKV) umma_f16_ts_lo<false>(tm_A2, tm_S + ATB_ACOL(0), y2l, y2h, IDESC_TS);
+              umma_f16_ts_lo<false>(tm_A1, tm_dP + ATB_ACOL(0), y1l, y1h, IDESC_TS);
             } else {
-              umma_f16_ts(tm_A1, tm_dP + acol, dY1 + ((k * 2048) >> 4), IDESC_TS, (m | k) != 0);   // dQ += dS K
+              if (DKV) umma_f16_ts_lo<true>(tm_A2, tm_S + ATB_ACOL(0), y2l, y2h, IDESC_TS);
+              umma_f16_ts_lo<true>(tm_A1, tm_dP + ATB_ACOL(0), y1l, y1h, IDESC_TS);
+            }
+#pragma unroll
+            for (int k = 1; k < ATB_BLK / 16; ++k) {
+              if (DKV) umma_f16_ts_lo<true>(tm_A2, tm_S + ATB_ACOL(k), y2l + ((k * 2048) >> 4), y2h, IDESC_TS);   // dV += P^T dO
+              umma_f16_ts_lo<true>(tm_A1, tm_dP + ATB_ACOL(k), y1l + ((k * 2048) >> 4), y1h, IDESC_TS);           // dK += dS^T Q / dQ += dS K
             }
           }
           umma_commit(&y_empty[st]);
