@@ -235,6 +235,12 @@ gemm_tcgen05_pair_kernel(const __grid_constant__ PairMaps maps, GemmShape shape,
         cin_phase ^= 1;
       }
       tc_fence_after();
+      if constexpr (!Epi::kCin) {
+        // the previous tile's bulk stores have had a whole tile of MMA time to read the staging boxes: waiting
+        // here, not right after issuing them, keeps the warp from idling on the store engine
+        if (lane == 0) tma_store_wait_read<0>();
+        __syncwarp();
+      }
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + half * 128;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
@@ -276,8 +282,8 @@ gemm_tcgen05_pair_kernel(const __grid_constant__ PairMaps maps, GemmShape shape,
           }
         }
         tma_store_commit();
-        tma_store_wait_read<0>();                              // boxes may be overwritten
         if constexpr (Epi::kCin) {
+          tma_store_wait_read<0>();                            // boxes may be overwritten: by the next addend tile
           if (tile + num_pairs < num_tiles) load_cin(tile + num_pairs);
         }
       }
