@@ -380,6 +380,3 @@ def attention(q: Tensor, k: Tensor, v: Tensor, cu_seqlens: Tensor, window: int, 
         bounds = doc_bounds(cu_seqlens, q.shape[0])
     return _Attention.apply(q, k, v, cu_seqlens, bounds, int(window), float(scale), int(max_len))
 
-
-def dc_supported(q: Tensor, window: int) -> bool:
-    return False
