@@ -22,7 +22,9 @@
 #include "api.h"
 #include "ptx.cuh"
 
+#include <cstdlib>
 #include <mutex>
+#include <string>
 
 namespace mng {
 
@@ -367,7 +369,12 @@ struct AttnBwdParams {
   __nv_bfloat16* out2;      // DKV: dV
   int T, H, window;
   float scale_log2, scale;
+  int* work_counter;        // items beyond the first of each CTA are claimed here; null = static stride of gridDim.x
 };
+
+// Work counters of the two backward kernels of one call (dK/dV, dQ); the prep kernel, which precedes both on the stream,
+// zeroes them.  One set per device: backward calls on different streams of one device must not overlap.
+static __device__ int g_atb_work[2];
 
 __global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
                                      const float* __restrict__ lse, float* __restrict__ delta, float* __restrict__ lse2, int T,
@@ -375,6 +382,7 @@ __global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, const 
   const long long row = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 4;      // (token, head) pair: 16 lanes each
   const int part = threadIdx.x & 15;
   float acc = 0.f;
+  if (blockIdx.x == 0 && threadIdx.x < 2) g_atb_work[threadIdx.x] = 0;
   if (row < (long long)T * H) {
     const uint4 a = *reinterpret_cast<const uint4*>(o + row * 128 + part * 8);
     const uint4 b = *reinterpret_cast<const uint4*>(dout + row * 128 + part * 8);
@@ -407,6 +415,9 @@ __global__ void __launch_bounds__(ATB_THREADS, 1)
 attn_bwd_kernel(const __grid_constant__ CUtensorMap tx1, const __grid_constant__ CUtensorMap tx2,
                 const __grid_constant__ CUtensorMap ty1, const __grid_constant__ CUtensorMap ty2, AttnBwdParams p,
                 uint32_t* status) {
+  // Persistent: CTA c works on items c, c + gridDim.x, ...; item = (128-row owner tile, head), heads fastest.  TMEM is
+  // allocated once; the stream ring, the score buffers and every barrier phase run on counters that continue across
+  // items, so the next item's owner-tile load and first score MMAs overlap the previous item's accumulator drain.
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sX1 = smem;
@@ -419,23 +430,34 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tx1, const __grid_constant__
   uint64_t* y_empty = y_full + ATB_STAGES;         // [4]
   uint64_t* sdp_full = y_empty + ATB_STAGES;       // [2]
   uint64_t* pds_ready = sdp_full + 2;              // [2]
-  uint64_t* acc_done = pds_ready + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_done + 1);
+  uint64_t* acc_done = pds_ready + 2;              // accumulators of the item complete
+  uint64_t* x_free = acc_done + 1;                 // owner tiles no longer read by any MMA
+  uint64_t* acc_free = x_free + 1;                 // accumulators drained by the 16 element-wise warps
+  uint64_t* item_full = acc_free + 1;              // [2] item ring: the producer publishes the ids it claimed
+  uint64_t* item_empty = item_full + 2;            // [2] read by the MMA thread and the 16 element-wise warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_empty + 2);
   volatile uint32_t* abort_flag = tmem_slot + 1;
+  volatile int* item_slot = reinterpret_cast<volatile int*>(tmem_slot + 2);    // [2], -1 = no more work
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.y;
-  const int r0 = (DKV ? (int)blockIdx.x : (int)(gridDim.x - 1 - blockIdx.x)) * 128;    // owner tile start
-  const int r_last = min(r0 + 127, p.T - 1);
-  int s0, nb;                                                // stream start row and number of 64-row blocks
-  if (DKV) {
-    s0 = r0;
-    const int i_max = min(min(r_last + p.window, p.doc_end[r_last] - 1), p.T - 1);
-    nb = (i_max - s0) / ATB_BLK + 1;
-  } else {
-    s0 = max(p.doc_start[r0], r0 - p.window);
-    nb = (r_last - s0) / ATB_BLK + 1;
-  }
+  const int tiles = (p.T + 127) / 128;
+  const int items = tiles * p.H;
+
+  // owner tile start, head, stream start row and number of 64-row blocks of an item
+  auto item_geom = [&](int item, int& h, int& r0, int& s0, int& nb) {
+    const int tile = item / p.H;
+    h = item - tile * p.H;
+    r0 = (DKV ? tile : tiles - 1 - tile) * 128;
+    const int r_last = min(r0 + 127, p.T - 1);
+    if (DKV) {
+      s0 = r0;
+      const int i_max = min(min(r_last + p.window, p.doc_end[r_last] - 1), p.T - 1);
+      nb = (i_max - s0) / ATB_BLK + 1;
+    } else {
+      s0 = max(p.doc_start[r0], r0 - p.window);
+      nb = (r_last - s0) / ATB_BLK + 1;
+    }
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(x_full, 1);
@@ -448,6 +470,12 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tx1, const __grid_constant__
       mbar_init(&pds_ready[s], 16);
     }
     mbar_init(acc_done, 1);
+    mbar_init(x_free, 1);
+    mbar_init(acc_free, 16);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&item_full[s], 1);
+      mbar_init(&item_empty[s], 17);
+    }
     *abort_flag = 0;
     mbar_fence_init();
     tma_prefetch_desc(&tx1);
@@ -471,27 +499,40 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tx1, const __grid_constant__
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_expect_tx(x_full, 2 * ATT_TILE_BYTES);
-      tma_load_3d(sX1, &tx1, x_full, 0, h, r0);
-      tma_load_3d(sX1 + 16384, &tx1, x_full, 64, h, r0);
-      tma_load_3d(sX2, &tx2, x_full, 0, h, r0);
-      tma_load_3d(sX2 + 16384, &tx2, x_full, 64, h, r0);
-      for (int n = 0; n < nb; ++n) {
-        const int st = n % ATB_STAGES, srow = s0 + n * ATB_BLK;
-        if (!mbar_wait(&y_empty[st], ((n / ATB_STAGES) & 1) ^ 1, abort_flag)) { ATB_FAIL(ERR_WAIT_SMEM_EMPTY); break; }
-        uint8_t* y1 = sY + st * 2 * ATB_YTILE;
-        uint8_t* y2 = y1 + ATB_YTILE;
-        uint32_t bytes = 2 * ATB_YTILE;
-        const int cnt = min(ATB_BLK, p.T - srow);
-        if (DKV) bytes += 2u * cnt * 4u;
-        mbar_expect_tx(&y_full[st], bytes);
-        tma_load_3d(y1, &ty1, &y_full[st], 0, h, srow);
-        tma_load_3d(y1 + ATB_YTILE / 2, &ty1, &y_full[st], 64, h, srow);
-        tma_load_3d(y2, &ty2, &y_full[st], 0, h, srow);
-        tma_load_3d(y2 + ATB_YTILE / 2, &ty2, &y_full[st], 64, h, srow);
-        if (DKV) {
-          attn_bulk_load(vec + st * 2 * ATB_BLK, p.lse2 + (size_t)h * p.T + srow, cnt * 4, &y_full[st]);
-          attn_bulk_load(vec + st * 2 * ATB_BLK + ATB_BLK, p.delta + (size_t)h * p.T + srow, cnt * 4, &y_full[st]);
+      int gn = 0, it = 0, next = blockIdx.x;
+      bool ok = true;
+      for (; ok; ++it) {
+        const int item = next < items ? next : -1;
+        if (!mbar_wait(&item_empty[it & 1], ((it >> 1) & 1) ^ 1, abort_flag)) { ATB_FAIL(ERR_WAIT_SMEM_EMPTY); break; }
+        item_slot[it & 1] = item;
+        mbar_arrive(&item_full[it & 1]);
+        if (item < 0) break;
+        next = p.work_counter ? (int)gridDim.x + atomicAdd(p.work_counter, 1) : item + (int)gridDim.x;   // claimed early, used next round
+        int h, r0, s0, nb;
+        item_geom(item, h, r0, s0, nb);
+        if (!mbar_wait(x_free, (it & 1) ^ 1, abort_flag)) { ATB_FAIL(ERR_WAIT_SMEM_EMPTY); break; }
+        mbar_expect_tx(x_full, 2 * ATT_TILE_BYTES);
+        tma_load_3d(sX1, &tx1, x_full, 0, h, r0);
+        tma_load_3d(sX1 + 16384, &tx1, x_full, 64, h, r0);
+        tma_load_3d(sX2, &tx2, x_full, 0, h, r0);
+        tma_load_3d(sX2 + 16384, &tx2, x_full, 64, h, r0);
+        for (int n = 0; n < nb; ++n, ++gn) {
+          const int st = gn % ATB_STAGES, srow = s0 + n * ATB_BLK;
+          if (!mbar_wait(&y_empty[st], ((gn / ATB_STAGES) & 1) ^ 1, abort_flag)) { ATB_FAIL(ERR_WAIT_SMEM_EMPTY); ok = false; break; }
+          uint8_t* y1 = sY + st * 2 * ATB_YTILE;
+          uint8_t* y2 = y1 + ATB_YTILE;
+          uint32_t bytes = 2 * ATB_YTILE;
+          const int cnt = min(ATB_BLK, p.T - srow);
+          if (DKV) bytes += 2u * cnt * 4u;
+          mbar_expect_tx(&y_full[st], bytes);
+          tma_load_3d(y1, &ty1, &y_full[st], 0, h, srow);
+          tma_load_3d(y1 + ATB_YTILE / 2, &ty1, &y_full[st], 64, h, srow);
+          tma_load_3d(y2, &ty2, &y_full[st], 0, h, srow);
+          tma_load_3d(y2 + ATB_YTILE / 2, &ty2, &y_full[st], 64, h, srow);
+          if (DKV) {
+            attn_bulk_load(vec + st * 2 * ATB_BLK, p.lse2 + (size_t)h * p.T + srow, cnt * 4, &y_full[st]);
+            attn_bulk_load(vec + st * 2 * ATB_BLK + ATB_BLK, p.delta + (size_t)h * p.T + srow, cnt * 4, &y_full[st]);
+          }
         }
       }
     }
@@ -502,16 +543,23 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tx1, const __grid_constant__
       const uint64_t dX1 = make_smem_desc(smem_u32(sX1), 16, 1024), dX2 = make_smem_desc(smem_u32(sX2), 16, 1024);
       const uint64_t dYk = make_smem_desc(smem_u32(sY), 16, 1024);                 // stream tile as K-major B (scores)
       const uint64_t dYm = make_smem_desc(smem_u32(sY), ATB_YTILE / 2, 1024);      // the same bytes as MN-major B (accumulation)
-      bool ok = mbar_wait(x_full, 0, abort_flag);
-      if (!ok) ATB_FAIL(ERR_WAIT_TMA_FULL);
-      for (int n = 0; ok && n <= nb; ++n) {
-        if (n < nb) {                                        // scores of block n into buffer n & 1
-          const int st = n % ATB_STAGES, b = n & 1;
-          const uint64_t dY1 = dYk + ((st * 2 * ATB_YTILE) >> 4), dY2 = dY1 + (ATB_YTILE >> 4);
-          if (!mbar_wait(&y_full[st], (n / ATB_STAGES) & 1, abort_flag)) { ATB_FAIL(ERR_WAIT_TMA_FULL); ok = false; break; }
-          tc_fence_after();
-          {
-            const uint32_t x1l = (uint32_t)dX1, x1h = (uint32_t)(dX1 >> 32), x2l = (uint32_t)dX2, x2h = (uint32_t)(dX2 >> 32);
+      const uint32_t x1l = (uint32_t)dX1, x1h = (uint32_t)(dX1 >> 32), x2l = (uint32_t)dX2, x2h = (uint32_t)(dX2 >> 32);
+      int gn0 = 0, it = 0;                                   // gn0: global index of the item's first block
+      bool ok = true;
+      for (; ok; ++it) {
+        if (!mbar_wait(&item_full[it & 1], (it >> 1) & 1, abort_flag)) { ATB_FAIL(ERR_WAIT_TMA_FULL); break; }
+        const int item = item_slot[it & 1];
+        mbar_arrive(&item_empty[it & 1]);
+        if (item < 0) break;
+        int h, r0, s0, nb;
+        item_geom(item, h, r0, s0, nb);
+        if (!mbar_wait(x_full, it & 1, abort_flag)) { ATB_FAIL(ERR_WAIT_TMA_FULL); break; }
+        for (int n = 0; ok && n <= nb; ++n) {
+          if (n < nb) {                                      // scores of block n into buffer gn & 1
+            const int gn = gn0 + n, st = gn % ATB_STAGES, b = gn & 1;
+            const uint64_t dY1 = dYk + ((st * 2 * ATB_YTILE) >> 4), dY2 = dY1 + (ATB_YTILE >> 4);
+            if (!mbar_wait(&y_full[st], (gn / ATB_STAGES) & 1, abort_flag)) { ATB_FAIL(ERR_WAIT_TMA_FULL); ok = false; break; }
+            tc_fence_after();
             const uint32_t y1l = (uint32_t)dY1, y1h = (uint32_t)(dY1 >> 32), y2l = (uint32_t)dY2, y2h = (uint32_t)(dY2 >> 32);
             const uint32_t dS = tm_S + b * ATB_BLK, dD = tm_dP + b * ATB_BLK;
 #define ATB_XO(k) ((((k) >> 2) * 16384 + ((k) & 3) * 32) >> 4)
@@ -523,15 +571,16 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tx1, const __grid_constant__
               umma_f16_lo<true>(dS, x1l + ATB_XO(k), x1h, y1l + ATB_YO(k), y1h, IDESC_SS);
               umma_f16_lo<true>(dD, x2l + ATB_XO(k), x2h, y2l + ATB_YO(k), y2h, IDESC_SS);
             }
+            umma_commit(&sdp_full[b]);
           }
-          umma_commit(&sdp_full[b]);
-        }
-        if (n >= 1) {                                        // accumulate block n-1 from its bf16 operands in TMEM
-          const int m = n - 1, st = m % ATB_STAGES, b = m & 1;
-          const uint64_t dY1 = dYm + ((st * 2 * ATB_YTILE) >> 4), dY2 = dY1 + (ATB_YTILE >> 4);
-          if (!mbar_wait(&pds_ready[b], (m >> 1) & 1, abort_flag)) { ATB_FAIL(ERR_WAIT_TMEM_EMPTY); ok = false; break; }
-          tc_fence_after();
-          {                                                   // 16 stream rows per MMA: 8 TMEM columns of packed bf16
+          if (n >= 1) {                                      // accumulate block n-1 from its bf16 operands in TMEM
+            const int m = n - 1, gm = gn0 + m, st = gm % ATB_STAGES, b = gm & 1;
+            const uint64_t dY1 = dYm + ((st * 2 * ATB_YTILE) >> 4), dY2 = dY1 + (ATB_YTILE >> 4);
+            if (m == 0 && it > 0) {                          // the previous item's accumulators must have been drained
+              if (!mbar_wait(acc_free, (it - 1) & 1, abort_flag)) { ATB_FAIL(ERR_WAIT_TMEM_EMPTY); ok = false; break; }
+            }
+            if (!mbar_wait(&pds_ready[b], (gm >> 1) & 1, abort_flag)) { ATB_FAIL(ERR_WAIT_TMEM_EMPTY); ok = false; break; }
+            tc_fence_after();
             const uint32_t y1l = (uint32_t)dY1, y1h = (uint32_t)(dY1 >> 32), y2l = (uint32_t)dY2, y2h = (uint32_t)(dY2 >> 32);
 #define ATB_ACOL(k) (b * ATB_BLK + (k) * 16)
             if (m == 0) {
@@ -542,126 +591,136 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tx1, const __grid_constant__
               umma_f16_ts_lo<true>(tm_A1, tm_dP + ATB_ACOL(0), y1l, y1h, IDESC_TS);
             }
 #pragma unroll
-            for (int k = 1; k < ATB_BLK / 16; ++k) {
+            for (int k = 1; k < ATB_BLK / 16; ++k) {          // 16 stream rows per MMA: 8 TMEM columns of packed bf16
               if (DKV) umma_f16_ts_lo<true>(tm_A2, tm_S + ATB_ACOL(k), y2l + ((k * 2048) >> 4), y2h, IDESC_TS);   // dV += P^T dO
               umma_f16_ts_lo<true>(tm_A1, tm_dP + ATB_ACOL(k), y1l + ((k * 2048) >> 4), y1h, IDESC_TS);           // dK += dS^T Q / dQ += dS K
             }
+            umma_commit(&y_empty[st]);
           }
-          umma_commit(&y_empty[st]);
         }
+        if (ok) {
+          umma_commit(x_free);
+          umma_commit(acc_done);
+        }
+        gn0 += nb;
       }
-      if (ok) umma_commit(acc_done);
     }
   } else {
     const int sub = warp & 3, quarter = (warp - 2) >> 2;     // TMEM lanes sub*32.., block columns quarter*16..
     const int r = sub * 32 + lane;
-    const int g = r0 + r;                                    // owner row: a key (DKV) or a query
-    const bool row_ok = g < p.T;
-    int lo, hi;                                              // visible stream rows for this owner row
-    float my_lse2 = 0.f, my_delta = 0.f;
-    if (DKV) {
-      lo = g;
-      hi = row_ok ? min(min(g + p.window, p.doc_end[g] - 1), p.T - 1) : -1;
-    } else {
-      lo = row_ok ? max(p.doc_start[g], g - p.window) : 0;
-      hi = row_ok ? g : -1;
-      if (row_ok) {
-        my_lse2 = p.lse2[(size_t)h * p.T + g];
-        my_delta = p.delta[(size_t)h * p.T + g];
-      }
-    }
-    const bool any_vis = hi >= lo;
-    const unsigned span = (unsigned)(hi - lo);
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
     const float c = p.scale_log2, sc = p.scale;
     bool alive = true;
-    for (int n = 0; n < nb; ++n) {
-      const int st = n % ATB_STAGES, b = n & 1, srow = s0 + n * ATB_BLK;
-      if (!mbar_wait(&sdp_full[b], (n >> 1) & 1, abort_flag)) { ATB_FAIL(ERR_WAIT_TMEM_FULL); alive = false; break; }
-      tc_fence_after();
-      const float* vl = vec + st * 2 * ATB_BLK + quarter * 16;
-      const float* vd = vl + ATB_BLK;
-      const uint32_t col = lane_off + b * ATB_BLK + quarter * 16;
-      uint32_t s[16], d[16];
-      tmem_ld16(tm_S + col, s);
-      tmem_ld16(tm_dP + col, d);
-      tmem_ld_wait();
-      uint32_t pk_p[8], pk_ds[8];
-      const int col0 = srow + quarter * 16 - lo;
-      const bool full = any_vis && col0 >= 0 && (unsigned)(col0 + 15) <= span;     // all 16 columns visible for this row
-      if (__all_sync(0xffffffffu, full)) {
-#pragma unroll
-        for (int t = 0; t < 16; t += 4) {
-          float l2[4], dl[4];
-          if (DKV) {
-            *reinterpret_cast<float4*>(l2) = *reinterpret_cast<const float4*>(vl + t);
-            *reinterpret_cast<float4*>(dl) = *reinterpret_cast<const float4*>(vd + t);
-          } else {
-#pragma unroll
-            for (int u = 0; u < 4; ++u) { l2[u] = my_lse2; dl[u] = my_delta; }
-          }
-          float pv[4], dv[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            pv[u] = exp2f(fmaf(__uint_as_float(s[t + u]), c, -l2[u]));
-            dv[u] = pv[u] * fmaf(__uint_as_float(d[t + u]), sc, -dl[u]);
-          }
-          pk_p[t >> 1] = pack_bf16x2(pv[0], pv[1]);
-          pk_p[(t >> 1) + 1] = pack_bf16x2(pv[2], pv[3]);
-          pk_ds[t >> 1] = pack_bf16x2(dv[0], dv[1]);
-          pk_ds[(t >> 1) + 1] = pack_bf16x2(dv[2], dv[3]);
-        }
-      } else {
-#pragma unroll
-        for (int t = 0; t < 16; t += 2) {
-          float pv[2], dv[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const float l2 = DKV ? vl[t + u] : my_lse2;
-            const float dl = DKV ? vd[t + u] : my_delta;
-            const bool vis = any_vis && (unsigned)(col0 + t + u) <= span;
-            const float pe = exp2f(fmaf(__uint_as_float(s[t + u]), c, -l2));
-            pv[u] = vis ? pe : 0.f;
-            dv[u] = vis ? pe * fmaf(__uint_as_float(d[t + u]), sc, -dl) : 0.f;
-          }
-          pk_p[t >> 1] = pack_bf16x2(pv[0], pv[1]);
-          pk_ds[t >> 1] = pack_bf16x2(dv[0], dv[1]);
-        }
-      }
-      if (DKV) tmem_st8(tm_S + col, pk_p);
-      tmem_st8(tm_dP + col, pk_ds);
-      tmem_st_wait();
-      tc_fence_before();
+    int gn = 0, it = 0;
+    for (; alive; ++it) {
+      if (!mbar_wait(&item_full[it & 1], (it >> 1) & 1, abort_flag)) { ATB_FAIL(ERR_WAIT_TMA_FULL); break; }
+      const int item = item_slot[it & 1];
       __syncwarp();
-      if (lane == 0) mbar_arrive(&pds_ready[b]);
-    }
-    if (alive) {
-      if (!mbar_wait(acc_done, 0, abort_flag)) {
-        ATB_FAIL(ERR_WAIT_TMEM_FULL);
+      if (lane == 0) mbar_arrive(&item_empty[it & 1]);
+      if (item < 0) break;
+      int h, r0, s0, nb;
+      item_geom(item, h, r0, s0, nb);
+      const int g = r0 + r;                                  // owner row: a key (DKV) or a query
+      const bool row_ok = g < p.T;
+      int lo, hi;                                            // visible stream rows for this owner row
+      float my_lse2 = 0.f, my_delta = 0.f;
+      if (DKV) {
+        lo = g;
+        hi = row_ok ? min(min(g + p.window, p.doc_end[g] - 1), p.T - 1) : -1;
       } else {
+        lo = row_ok ? max(p.doc_start[g], g - p.window) : 0;
+        hi = row_ok ? g : -1;
+        if (row_ok) {
+          my_lse2 = p.lse2[(size_t)h * p.T + g];
+          my_delta = p.delta[(size_t)h * p.T + g];
+        }
+      }
+      const bool any_vis = hi >= lo;
+      const unsigned span = (unsigned)(hi - lo);
+      for (int n = 0; n < nb; ++n, ++gn) {
+        const int st = gn % ATB_STAGES, b = gn & 1, srow = s0 + n * ATB_BLK;
+        if (!mbar_wait(&sdp_full[b], (gn >> 1) & 1, abort_flag)) { ATB_FAIL(ERR_WAIT_TMEM_FULL); alive = false; break; }
         tc_fence_after();
-#pragma unroll 1
-        for (int which = 0; which < (DKV ? 2 : 1); ++which) {
-          __nv_bfloat16* orow = (which == 0 ? p.out1 : p.out2) + ((size_t)g * p.H + h) * 128 + quarter * 32;
-#pragma unroll 1
-          for (int cc = 0; cc < 1; ++cc) {
-            uint32_t v[32];
-            tmem_ld32((which == 0 ? tm_A1 : tm_A2) + lane_off + quarter * 32, v);
-            tmem_ld_wait();
-            if (row_ok) {
+        const float* vl = vec + st * 2 * ATB_BLK + quarter * 16;
+        const float* vd = vl + ATB_BLK;
+        const uint32_t col = lane_off + b * ATB_BLK + quarter * 16;
+        uint32_t s[16], d[16];
+        tmem_ld16(tm_S + col, s);
+        tmem_ld16(tm_dP + col, d);
+        tmem_ld_wait();
+        uint32_t pk_p[8], pk_ds[8];
+        const int col0 = srow + quarter * 16 - lo;
+        const bool full = any_vis && col0 >= 0 && (unsigned)(col0 + 15) <= span;     // all 16 columns visible for this row
+        if (__all_sync(0xffffffffu, full)) {
 #pragma unroll
-              for (int t = 0; t < 4; ++t) {
-                uint4 w;
-                w.x = pack_bf16x2(__uint_as_float(v[8 * t]), __uint_as_float(v[8 * t + 1]));
-                w.y = pack_bf16x2(__uint_as_float(v[8 * t + 2]), __uint_as_float(v[8 * t + 3]));
-                w.z = pack_bf16x2(__uint_as_float(v[8 * t + 4]), __uint_as_float(v[8 * t + 5]));
-                w.w = pack_bf16x2(__uint_as_float(v[8 * t + 6]), __uint_as_float(v[8 * t + 7]));
-                *reinterpret_cast<uint4*>(orow + cc * 32 + t * 8) = w;
-              }
+          for (int t = 0; t < 16; t += 4) {
+            float l2[4], dl[4];
+            if (DKV) {
+              *reinterpret_cast<float4*>(l2) = *reinterpret_cast<const float4*>(vl + t);
+              *reinterpret_cast<float4*>(dl) = *reinterpret_cast<const float4*>(vd + t);
+            } else {
+#pragma unroll
+              for (int u = 0; u < 4; ++u) { l2[u] = my_lse2; dl[u] = my_delta; }
             }
+            float pv[4], dv[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              pv[u] = exp2f(fmaf(__uint_as_float(s[t + u]), c, -l2[u]));
+              dv[u] = pv[u] * fmaf(__uint_as_float(d[t + u]), sc, -dl[u]);
+            }
+            pk_p[t >> 1] = pack_bf16x2(pv[0], pv[1]);
+            pk_p[(t >> 1) + 1] = pack_bf16x2(pv[2], pv[3]);
+            pk_ds[t >> 1] = pack_bf16x2(dv[0], dv[1]);
+            pk_ds[(t >> 1) + 1] = pack_bf16x2(dv[2], dv[3]);
+          }
+        } else {
+#pragma unroll
+          for (int t = 0; t < 16; t += 2) {
+            float pv[2], dv[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const float l2 = DKV ? vl[t + u] : my_lse2;
+              const float dl = DKV ? vd[t + u] : my_delta;
+              const bool vis = any_vis && (unsigned)(col0 + t + u) <= span;
+              const float pe = exp2f(fmaf(__uint_as_float(s[t + u]), c, -l2));
+              pv[u] = vis ? pe : 0.f;
+              dv[u] = vis ? pe * fmaf(__uint_as_float(d[t + u]), sc, -dl) : 0.f;
+            }
+            pk_p[t >> 1] = pack_bf16x2(pv[0], pv[1]);
+            pk_ds[t >> 1] = pack_bf16x2(dv[0], dv[1]);
+          }
+        }
+        if (DKV) tmem_st8(tm_S + col, pk_p);
+        tmem_st8(tm_dP + col, pk_ds);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pds_ready[b]);
+      }
+      if (!alive) break;
+      if (!mbar_wait(acc_done, it & 1, abort_flag)) { ATB_FAIL(ERR_WAIT_TMEM_FULL); alive = false; break; }
+      tc_fence_after();
+#pragma unroll 1
+      for (int which = 0; which < (DKV ? 2 : 1); ++which) {
+        __nv_bfloat16* orow = (which == 0 ? p.out1 : p.out2) + ((size_t)g * p.H + h) * 128 + quarter * 32;
+        uint32_t v[32];
+        tmem_ld32((which == 0 ? tm_A1 : tm_A2) + lane_off + quarter * 32, v);
+        tmem_ld_wait();
+        if (row_ok) {
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(v[8 * t]), __uint_as_float(v[8 * t + 1]));
+            w.y = pack_bf16x2(__uint_as_float(v[8 * t + 2]), __uint_as_float(v[8 * t + 3]));
+            w.z = pack_bf16x2(__uint_as_float(v[8 * t + 4]), __uint_as_float(v[8 * t + 5]));
+            w.w = pack_bf16x2(__uint_as_float(v[8 * t + 6]), __uint_as_float(v[8 * t + 7]));
+            *reinterpret_cast<uint4*>(orow + t * 8) = w;
           }
         }
       }
+      tc_fence_before();                                     // accumulator reads done before the next item's first accumulating MMA
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_free);
     }
   }
 #undef ATB_FAIL
@@ -704,11 +763,24 @@ extern "C" int mng_attn_bwd(const void* q, const void* k, const void* v, const v
   attn_bwd_prep_kernel<<<(unsigned)((rows * 16 + 255) / 256), 256, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(out), reinterpret_cast<const __nv_bfloat16*>(dout), lse, delta, lse2, T, H, scale);
   const float c = scale * 1.4426950408889634f;
-  dim3 grid((T + 127) / 128, H);
+  // one persistent CTA per SM; MNG_ATTN_BWD=tile launches one CTA per (tile, head) item instead (same kernel)
+  // MNG_ATTN_BWD=static keeps the persistent grid but strides the items instead of claiming them from the counter
+  static const std::string mode = [] { const char* e = getenv("MNG_ATTN_BWD"); return std::string(e ? e : ""); }();
+  static const bool per_item = mode == "tile";
+  static int* work = nullptr;
+  if (!work && cudaGetSymbolAddress(reinterpret_cast<void**>(&work), g_atb_work) != cudaSuccess) return -6;
+  int* const w0 = mode == "static" ? nullptr : work;
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -6;
+  }
+  const int items = ((T + 127) / 128) * H;
+  dim3 grid(per_item ? items : (items < sms ? items : sms));
   AttnBwdParams pa{doc_start, doc_end, lse2, delta, reinterpret_cast<__nv_bfloat16*>(dk), reinterpret_cast<__nv_bfloat16*>(dv),
-                   T, H, window, c, scale};
+                   T, H, window, c, scale, w0};
   attn_bwd_kernel<true><<<grid, ATB_THREADS, ATB_SMEM, st>>>(tk, tv, sq, sdo, pa, status);
-  AttnBwdParams pb{doc_start, doc_end, lse2, delta, reinterpret_cast<__nv_bfloat16*>(dq), nullptr, T, H, window, c, scale};
+  AttnBwdParams pb{doc_start, doc_end, lse2, delta, reinterpret_cast<__nv_bfloat16*>(dq), nullptr, T, H, window, c, scale, w0 ? w0 + 1 : nullptr};
   attn_bwd_kernel<false><<<grid, ATB_THREADS, ATB_SMEM, st>>>(tq, tdo, sk, sv, pb, status);
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
