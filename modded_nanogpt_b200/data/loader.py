@@ -191,15 +191,20 @@ class TokenLoader:
 
     # -- staging ------------------------------------------------------------------------
     def _buffers(self, T: int, ndocs: int):
+        """A pinned staging set that no copy still reads: the sets rotate, and each carries the event recorded after
+        its last host-to-device copies, which is waited for before the host overwrites the set (the host can run
+        several micro-batches ahead of the device, so rotation alone would not protect a pending copy)."""
         key = (T, ndocs)
         if key not in self._stage:
             mk = lambda n, dt: torch.empty(n, dtype=dt, pin_memory=self._pin)
-            # two sets so that a batch still in flight to the device is not overwritten
             self._stage[key] = [dict(inp=mk(T, torch.int32), tgt=mk(T, torch.int64), cu=mk(ndocs, torch.int32),
-                                     bg=mk(T, torch.int32)) for _ in range(2)]
+                                     bg=mk(T, torch.int32), done=None) for _ in range(3)]
             self._flip = 0
-        self._flip ^= 1
-        return self._stage[key][self._flip]
+        self._flip = (self._flip + 1) % 3
+        st = self._stage[key][self._flip]
+        if st["done"] is not None:
+            st["done"].synchronize()
+        return st
 
     def reparameterise(self, num_tokens: int, max_seq_len: int, grad_accum_steps: int):
         assert num_tokens % (self.world_size * grad_accum_steps) == 0
@@ -254,7 +259,12 @@ class TokenLoader:
         nbytes = sum(st[k].numel() * st[k].element_size() for k in ("inp", "tgt", "cu", "bg"))
         if self.count_bytes and dev.type == "cuda":
             self.bytes_copied += nbytes
-        return Batch(to(st["inp"]), to(st["tgt"]), to(st["cu"]), to(st["bg"]), st["bg"].numpy().copy(), nbytes)
+        batch = Batch(to(st["inp"]), to(st["tgt"]), to(st["cu"]), to(st["bg"]), st["bg"].numpy().copy(), nbytes)
+        if dev.type == "cuda":
+            if st["done"] is None:
+                st["done"] = torch.cuda.Event()
+            st["done"].record()
+        return batch
 
     __next__ = next_batch
 

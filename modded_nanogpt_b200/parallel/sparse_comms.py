@@ -44,15 +44,26 @@ class SparseRowExchange:
         self.device = torch.device(device)
         self.cpu_group, self.group = cpu_group, group
         pin = self.device.type == "cuda"
-        self._stage = torch.empty(num_rows, dtype=torch.int32, pin_memory=pin)
+        # two pinned staging buffers, each with the event recorded after its last copy to the device: the host may run
+        # more than a step ahead of the device, and must not overwrite a buffer whose copy has not run yet
+        self._stages = [[torch.empty(num_rows, dtype=torch.int32, pin_memory=pin), None] for _ in range(2)]
+        self._flip = 0
         self._state = None
 
     @torch.no_grad()
     def start(self, rows_np: np.ndarray):
         n = rows_np.shape[0]
-        stage = self._stage[:n]
+        self._flip ^= 1
+        slot = self._stages[self._flip]
+        if slot[1] is not None:
+            slot[1].synchronize()
+        stage = slot[0][:n]
         stage.copy_(torch.from_numpy(rows_np))
         send_idx = stage.to(self.device, non_blocking=True)
+        if self.device.type == "cuda":
+            if slot[1] is None:
+                slot[1] = torch.cuda.Event()
+            slot[1].record()
         bounds = np.arange(0, self.rows_per_rank * (self.world + 1), self.rows_per_rank, dtype=np.int64)
         ins = np.searchsorted(rows_np, bounds)
         send_counts = torch.from_numpy((ins[1:] - ins[:-1]).astype(np.int64))
