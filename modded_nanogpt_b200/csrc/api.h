@@ -46,6 +46,8 @@ int mng_gemm(const GemmDesc* g);
 int mng_rmsnorm_fwd(const void* x, void* y, void* y8, float* row_scale, float* rstd, long long rows, int cols, void* stream);
 int mng_rmsnorm_bwd(const void* x, const void* dy, const float* rstd, void* dx, long long rows, int cols, int accumulate,
                     void* stream);
+int mng_rmsnorm_bwd_add(const void* x, const void* dy, const float* rstd, const void* addend, void* dx, long long rows,
+                        int cols, void* stream);
 // Row-wise e4m3 quantisation: q = x / s, s[r] = amax(x[r,:])/448 (bf16 in).
 int mng_quant_rows_e4m3(const void* x, void* q, float* scale, long long rows, int cols, void* stream);
 // dst[c, r] = src[r, c] (optionally += ), bf16; 32x32 tiles through shared memory.
@@ -106,6 +108,7 @@ typedef struct {
 typedef struct { LinTerm t[LC_MAX_TERMS]; int k; } LinCombArgs;
 typedef struct {
   void* dx;                 // [rows, cols] bf16 or null
+  int dx_accumulate;        // 1: dx += coefficient * g (dx holds the contributions of earlier calls), 0: dx = ...
   void* dgate;              // bf16 buffer (zero-initialised by the caller) or null; written at [row*stride + col]
   long long dgate_stride;
   int dgate_col;

@@ -133,6 +133,20 @@ Tensor rmsnorm_bwd(const Tensor& x, const Tensor& dy, const c10::optional<Tensor
   return dx;
 }
 
+// dx = rmsnorm backward(x, dy) + addend, in one pass
+Tensor rmsnorm_bwd_add(const Tensor& x, const Tensor& dy, const c10::optional<Tensor>& rstd, const Tensor& addend) {
+  TORCH_CHECK(x.is_contiguous() && dy.is_contiguous() && addend.is_contiguous() && x.scalar_type() == torch::kBFloat16 &&
+              dy.scalar_type() == torch::kBFloat16 && addend.scalar_type() == torch::kBFloat16 && addend.numel() == x.numel());
+  c10::cuda::CUDAGuard guard(x.device());
+  const int cols = (int)x.size(-1);
+  const int64_t rows = x.numel() / cols;
+  Tensor dx = torch::empty_like(x);
+  check(mng_rmsnorm_bwd_add(x.data_ptr(), dy.data_ptr(), fptr(rstd), addend.data_ptr(), dx.data_ptr(), rows, cols, cur_stream()),
+        "mng_rmsnorm_bwd_add");
+  g_launches += 1;
+  return dx;
+}
+
 std::vector<Tensor> quant_rows(const Tensor& x) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.is_contiguous());
   c10::cuda::CUDAGuard guard(x.device());
@@ -310,11 +324,14 @@ Tensor lincomb_fwd(const std::vector<Tensor>& xs, const std::vector<OptT>& scala
   return out;
 }
 
-// need_dx[j]: allocate and return dx_j.  dgates[j]: bf16 [rows, C] buffer (zeroed by the caller; may be shared between
+// need_dx[j]: allocate and return dx_j; dx_into[j] (optional): use that tensor for this term's gradient instead, adding
+// to what it holds where dx_acc[j] (terms run in order, so a later term may add to what an earlier one of the same call wrote).
+// dgates[j]: bf16 [rows, C] buffer (zeroed by the caller; may be shared between
 // terms) written at column cols[j].  dscalars[j]: fp32 one-element accumulator (zeroed by the caller).
 std::vector<Tensor> lincomb_bwd(const std::vector<Tensor>& xs, const std::vector<OptT>& scalars, const std::vector<OptT>& gates,
                                 const std::vector<int64_t>& cols, const std::vector<double>& addc, const Tensor& gout,
-                                const std::vector<bool>& need_dx, const std::vector<OptT>& dgates, const std::vector<OptT>& dscalars) {
+                                const std::vector<bool>& need_dx, const std::vector<OptT>& dgates, const std::vector<OptT>& dscalars,
+                                const std::vector<OptT>& dx_into, const std::vector<bool>& dx_acc) {
   c10::cuda::CUDAGuard guard(xs[0].device());
   LinCombArgs a = make_lincomb(xs, scalars, gates, cols, addc);
   TORCH_CHECK(gout.is_contiguous() && gout.scalar_type() == torch::kBFloat16 && gout.numel() == xs[0].numel());
@@ -322,7 +339,12 @@ std::vector<Tensor> lincomb_bwd(const std::vector<Tensor>& xs, const std::vector
   std::vector<Tensor> dxs;
   for (int j = 0; j < a.k; ++j) {
     Tensor dx;
-    if (need_dx[j]) {
+    if (j < (int)dx_into.size() && dx_into[j].has_value() && dx_into[j]->defined()) {
+      const Tensor& acc = *dx_into[j];
+      TORCH_CHECK(acc.is_contiguous() && acc.scalar_type() == torch::kBFloat16 && acc.numel() == xs[j].numel());
+      g.t[j].dx = acc.data_ptr();
+      g.t[j].dx_accumulate = (j < (int)dx_acc.size() && dx_acc[j]) ? 1 : 0;
+    } else if (need_dx[j]) {
       dx = torch::empty_like(xs[j]);
       g.t[j].dx = dx.data_ptr();
     }
@@ -523,6 +545,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("rmsnorm_bwd_add", &rmsnorm_bwd_add);
   m.def("quant_rows", &quant_rows);
   m.def("transpose", &transpose);
   m.def("quant_transpose", &quant_transpose);

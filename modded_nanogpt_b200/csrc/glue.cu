@@ -102,8 +102,14 @@ lincomb_bwd_kernel(LinCombArgs a, LinCombGrads gr, const __nv_bfloat16* __restri
           }
           if (dx) {
             float o[8];
+            if (og.dx_accumulate) {
+              ld8(dx + (i * 32 + lane) * 8, o);
 #pragma unroll
-            for (int t = 0; t < 8; ++t) o[t] = c * gv[i][t];
+              for (int t = 0; t < 8; ++t) o[t] = fmaf(c, gv[i][t], o[t]);
+            } else {
+#pragma unroll
+              for (int t = 0; t < 8; ++t) o[t] = c * gv[i][t];
+            }
             st8(dx + (i * 32 + lane) * 8, o);
           }
         }

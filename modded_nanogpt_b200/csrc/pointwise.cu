@@ -68,11 +68,11 @@ rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restric
   }
 }
 
-// dx = rstd * (dy - xhat * mean(dy * xhat)),  xhat = x * rstd.   accumulate: dx += ...
+// dx = rstd * (dy - xhat * mean(dy * xhat)) [+ addend],  xhat = x * rstd.   `addend` may be `dx` itself (accumulate).
 template <int MAXV>
 __global__ void __launch_bounds__(ROW_WARPS * 32)
 rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ dy, const float* __restrict__ rstd_in,
-                   __nv_bfloat16* __restrict__ dx, long long rows, int cols, int accumulate, float eps) {
+                   const __nv_bfloat16* addend, __nv_bfloat16* dx, long long rows, int cols, float eps) {
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -106,8 +106,8 @@ rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __r
       float r[8];
 #pragma unroll
       for (int t = 0; t < 8; ++t) r[t] = gv[i][t] * rstd - xv[i][t] * c;
-      if (accumulate) {
-        uint4 old = *reinterpret_cast<const uint4*>(o);
+      if (addend) {
+        uint4 old = *reinterpret_cast<const uint4*>(addend + row * cols + (i * 32 + lane) * 8);
         const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&old);
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
@@ -266,8 +266,17 @@ extern "C" int mng_rmsnorm_fwd(const void* x, void* y, void* y8, float* row_scal
 extern "C" int mng_rmsnorm_bwd(const void* x, const void* dy, const float* rstd, void* dx, long long rows, int cols,
                                int accumulate, void* stream) {
   if (rows == 0) return 0;
-  DISPATCH_COLS(rmsnorm_bwd_kernel, (const __nv_bfloat16*)x, (const __nv_bfloat16*)dy, rstd, (__nv_bfloat16*)dx, rows, cols,
-                accumulate, kRmsEps);
+  DISPATCH_COLS(rmsnorm_bwd_kernel, (const __nv_bfloat16*)x, (const __nv_bfloat16*)dy, rstd,
+                accumulate ? (const __nv_bfloat16*)dx : nullptr, (__nv_bfloat16*)dx, rows, cols, kRmsEps);
+}
+
+// dx = norm backward + addend: the sum autograd would otherwise form with a separate pass when the normalised tensor
+// also feeds a residual path.
+extern "C" int mng_rmsnorm_bwd_add(const void* x, const void* dy, const float* rstd, const void* addend, void* dx,
+                                   long long rows, int cols, void* stream) {
+  if (rows == 0) return 0;
+  DISPATCH_COLS(rmsnorm_bwd_kernel, (const __nv_bfloat16*)x, (const __nv_bfloat16*)dy, rstd, (const __nv_bfloat16*)addend,
+                (__nv_bfloat16*)dx, rows, cols, kRmsEps);
 }
 
 extern "C" int mng_quant_rows_e4m3(const void* x, void* q, float* scale, long long rows, int cols, void* stream) {

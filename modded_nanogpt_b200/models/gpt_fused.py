@@ -10,7 +10,7 @@ from torch import Tensor
 
 from ..ops import functional as ops
 from ..ops import fused
-from ..ops.glue import Term, embed_direct, lincomb, qkv_post, xsa_gate
+from ..ops.glue import Term, embed_direct, grad_sink, lincomb, qkv_post, xsa_gate
 
 
 def fused_supported(model, x: Tensor) -> bool:
@@ -91,17 +91,41 @@ def forward_fused(m, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, big
     cos_t, sin_t = _rope_tables(m.yarn, 2 * T, x.device)
     cos_p, sin_p = _rope_tables(m.yarn_paired_head, 2 * T, x.device)
 
+    # Tensors that many lincombs consume get one shared gradient buffer each (x0, the bigram embedding, cached layer
+    # outputs, the gate matrices): their consumers add into it instead of autograd summing full-size gradients.
+    # The `*_s` aliases go to lincomb terms only; every other consumer keeps the plain tensor.
+    sinks: dict = {}
+
+    def sunk(name, t):
+        if t is None:
+            return None
+        if name not in sinks:
+            sinks[name] = grad_sink(t)
+        return sinks[name][0]
+
+    def X(name, t, **kw):                                    # lincomb term over a shared-gradient tensor
+        ts = sunk(name, t)
+        return Term(ts, sink=sinks[name][1], **kw)
+
+    def G(name, gate):                                       # gate= / gate_sink= keywords for a shared-gradient gate
+        if gate is None:
+            return {}
+        if gate.dtype != torch.bfloat16:                     # shared gate gradients are bf16 buffers
+            return dict(gate=gate)
+        gs = sunk(name, gate)
+        return dict(gate=gs, gate_sink=sinks[name][1])
+
     pre = pg = None
     lay0 = lay1 = None
     if track1:
         pre = m._gate_mlp(x0, 0)
         lay0, lay1 = m.gate_layouts
-        x = lincomb([Term(x0), Term(x0_bigram, gate=pre, col=lay0["inject"][0] + 1)])
+        x = lincomb([X("x0", x0), X("x0b", x0_bigram, col=lay0["inject"][0] + 1, **G("pre", pre))])
     cache = {0: x}
     normed7 = None
 
     def gate_of(i):
-        return (pre, lay0) if i < m.post_gate_layer else (pg, lay1)
+        return (pre, lay0, "pre") if i < m.post_gate_layer else (pg, lay1, "pg")
 
     for pl in m.plan:
         i, mu = pl.index, None
@@ -110,7 +134,7 @@ def forward_fused(m, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, big
 
         if not pl.has_attn:
             sk = torch.sigmoid(skip_lambda).reshape(1)
-            x = lincomb([Term(x), Term(cache[3], scalar=sk, gate=pg, col=lay1["skip"])])
+            x = lincomb([Term(x), X("c3", cache[3], scalar=sk, col=lay1["skip"], **G("pg", pg))])
         else:
             sl = pl.attn_slot
             if track1 and 7 in cache:
@@ -118,13 +142,15 @@ def forward_fused(m, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, big
                     normed7 = fused.rms_norm(cache[7])
                 attn_in = normed7
             else:
-                attn_in = fused.rms_norm(x)
+                attn_in, x = fused.rms_norm_fork(x)          # x's two gradients meet inside the norm backward
             ve_t = vgate = vadd = None
             if track1 and pl.last:
                 cache[9] = x
                 mu = m._mudd_raw(x, 0, 14)                                    # [T, 14]
-                vadd = lincomb([Term(cache[0], gate=mu, col=0), Term(cache[7], gate=mu, col=1), Term(x, gate=mu, col=2)])
-                x = lincomb([Term(x, gate=mu, col=5, addc=1.0), Term(cache[0], gate=mu, col=3), Term(cache[7], gate=mu, col=4)])
+                vadd = lincomb([X("c0", cache[0], col=0, **G("mu", mu)), X("c7", cache[7], col=1, **G("mu", mu)),
+                                Term(x, col=2, **G("mu", mu))])
+                x = lincomb([Term(x, col=5, addc=1.0, **G("mu", mu)), X("c0", cache[0], col=3, **G("mu", mu)),
+                             X("c7", cache[7], col=4, **G("mu", mu))])
                 vgate = mu[:, 6:8].repeat_interleave(H // 2, dim=-1).contiguous()
                 ve_t = ve[pl.ve_slot]
             elif pl.ve_slot >= 0:
@@ -144,7 +170,7 @@ def forward_fused(m, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, big
                                   ds2).view(T, H, Dh)
             else:
                 y = ops.attention(q, k, v, seqlens, ws[pl.long_window], yarn.attn_scale, max_len, ds1)
-            gt, lay = gate_of(i) if track1 else (None, None)
+            gt, lay, gname = gate_of(i) if track1 else (None, None, None)
             if track1 and pl.dc and not pl.paired:
                 o = lay1["dc"]
                 w1 = F.rms_norm(pg[:, o:o + H].float(), (H,), eps=1e-6).to(x.dtype).contiguous()
@@ -159,24 +185,25 @@ def forward_fused(m, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, big
             else:
                 attn_out = F.linear(y.reshape(T, D), sa_lambdas[i, 1] * vo_all[sl][D:])
             if mu is not None:
-                x = lincomb([Term(x, gate=mu, col=8), Term(attn_out, gate=mu, col=9), Term(cache[0], gate=mu, col=10),
-                             Term(x0_bigram, gate=mu, col=11)])
+                x = lincomb([Term(x, col=8, **G("mu", mu)), Term(attn_out, col=9, **G("mu", mu)),
+                             X("c0", cache[0], col=10, **G("mu", mu)), X("x0b", x0_bigram, col=11, **G("mu", mu))])
             elif track1:
                 o = lay["inject"][i]
-                terms = [Term(x, scalar=resid[i, 0]), Term(attn_out, scalar=post[i, 0]), Term(x0, gate=gt, col=o)]
+                terms = [Term(x, scalar=resid[i, 0]), Term(attn_out, scalar=post[i, 0]), X("x0", x0, col=o, **G(gname, gt))]
                 if i != 0:
-                    terms.append(Term(x0_bigram, gate=gt, col=o + 1))
+                    terms.append(X("x0b", x0_bigram, col=o + 1, **G(gname, gt)))
                 x = lincomb(terms)
             else:
                 x = lincomb([Term(x, scalar=resid[i, 0]), Term(attn_out, scalar=post[i, 0])])
 
         if direct:
             st = m._fp8_state.layer(i) if (training_fp8 and m._fp8_state is not None) else None
-            h = fused.norm_relu2_mlp(x, m.mlp_bank[i, 0], m.mlp_bank[i, 1], st, (m.mlp_bank.grad[i, 0], m.mlp_bank.grad[i, 1]))
+            h, x = fused.norm_relu2_mlp(x, m.mlp_bank[i, 0], m.mlp_bank[i, 1], st, (m.mlp_bank.grad[i, 0], m.mlp_bank.grad[i, 1]),
+                                        fork=True)
         else:
             h = m._mlp(i, x, training_fp8)
         if mu is not None:
-            x = lincomb([Term(x, gate=mu, col=12), Term(h, gate=mu, col=13)])
+            x = lincomb([Term(x, col=12, **G("mu", mu)), Term(h, col=13, **G("mu", mu))])
         else:
             x = lincomb([Term(x, scalar=resid[i, 1]), Term(h, scalar=post[i, 1])])
         if pl.cache:
@@ -184,8 +211,9 @@ def forward_fused(m, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, big
 
     if track1:
         mu = m._mudd_raw(x, 1, 5)
-        x = lincomb([Term(x), Term(cache[0], gate=mu, col=0), Term(cache[7], gate=mu, col=1), Term(cache[9], gate=mu, col=2),
-                     Term(ve[0], gate=mu, col=3), Term(cache[3], gate=mu, col=4)])
+        x = lincomb([Term(x), X("c0", cache[0], col=0, **G("mu2", mu)), X("c7", cache[7], col=1, **G("mu2", mu)),
+                     Term(cache[9], col=2, **G("mu2", mu)), Term(ve[0], col=3, **G("mu2", mu)),
+                     X("c3", cache[3], col=4, **G("mu2", mu))])
     x = fused.rms_norm(x)
 
     if m.training:

@@ -91,6 +91,42 @@ def rms_norm(x: Tensor) -> Tensor:
     return _RmsNorm.apply(x)
 
 
+def _norm_bwd_plus(x: Tensor, dy: Tensor | None, rstd: Tensor, dres: Tensor | None) -> Tensor | None:
+    """Gradient of a tensor that feeds both a norm (gradient `dy` of the normalised output) and a residual path
+    (gradient `dres`), formed in the norm-backward pass itself."""
+    if dy is None:
+        return dres
+    dy = dy.contiguous().view(x.shape)
+    if dres is None:
+        return _C().rmsnorm_bwd(x, dy, rstd, None)
+    return _C().rmsnorm_bwd_add(x, dy, rstd, dres.contiguous().view(x.shape))
+
+
+class _RmsNormFork(torch.autograd.Function):
+    """(norm(x), x): the second output carries x on to the residual path, so that both gradients of x meet in this
+    node and are summed inside the norm-backward kernel instead of by a separate elementwise pass."""
+
+    @staticmethod
+    def forward(ctx, x):
+        xc = x.contiguous()
+        y, _, _, rstd = _C().rmsnorm_fwd(xc, True, False, True)
+        ctx.save_for_backward(xc, rstd)
+        ctx.set_materialize_grads(False)
+        return y.view(x.shape), x
+
+    @staticmethod
+    def backward(ctx, dy, dres):
+        x, rstd = ctx.saved_tensors
+        return _norm_bwd_plus(x, dy, rstd, dres)
+
+
+def rms_norm_fork(x: Tensor):
+    """Returns (norm(x), x'), where x' equals x and is what the residual path should consume."""
+    if x.shape[-1] % 256 != 0 or x.shape[-1] > 4096 or not x.is_cuda:
+        return rms_norm(x), x
+    return _RmsNormFork.apply(x)
+
+
 # --------------------------------------------------------------------------------------------------
 # ReLU^2 MLP
 
@@ -145,10 +181,12 @@ class _NormRelu2Mlp(torch.autograd.Function):
     """out = relu(norm(x) @ W1^T)^2 @ W2 with W1, W2 stored (hidden, dim)."""
 
     @staticmethod
-    def forward(ctx, x, w_fc, w_proj, fp8, g_fc=None, g_proj=None):
+    def forward(ctx, x, w_fc, w_proj, fp8, g_fc=None, g_proj=None, fork=False):
         C = _C()
         T, D = x.shape
         ctx.grad_views = (g_fc, g_proj)
+        ctx.fork = fork
+        ctx.set_materialize_grads(False)
         hid = w_fc.shape[0]
         xc = x.contiguous()
         post = torch.empty(T, hid, dtype=torch.bfloat16, device=x.device)
@@ -164,12 +202,14 @@ class _NormRelu2Mlp(torch.autograd.Function):
             gemm(y, w_fc, out=post, epilogue=EPI_RELU2)
             out = gemm(post, w_proj, b_mn=True)
         ctx.save_for_backward(xc, rstd, y, post, w_fc, w_proj)
-        return out
+        return (out, x) if fork else out
 
     @staticmethod
-    def backward(ctx, g):
+    def backward(ctx, g, dres=None):
         C = _C()
         x, rstd, y, post, w_fc, w_proj = ctx.saved_tensors
+        if g is None:                                     # only the carried-on x was used
+            return dres, None, None, None, None, None, None
         g = g.contiguous()
         g_fc, g_proj = ctx.grad_views
         # weight gradients: either returned to autograd, or accumulated by the GEMM epilogue (beta = 1)
@@ -179,18 +219,19 @@ class _NormRelu2Mlp(torch.autograd.Function):
         dpre = gemm(g, w_proj, epilogue=EPI_DPRE, cin=post)                  # 2 (g W2^T) sqrt(post)
         d_fc = gemm(dpre, y, a_mn=True, b_mn=True, out=g_fc, cin=g_fc, **acc)            # dpre^T y      (hid, dim)
         dy = gemm(dpre, w_fc, b_mn=True)                                     # dpre W1          (T, dim)
-        dx = C.rmsnorm_bwd(x, dy, rstd, None)
+        dx = _norm_bwd_plus(x, dy, rstd, dres)
         if g_fc is not None:
-            return dx, None, None, None, None, None
-        return dx, d_fc, d_proj, None, None, None
+            return dx, None, None, None, None, None, None
+        return dx, d_fc, d_proj, None, None, None, None
 
 
-def norm_relu2_mlp(x: Tensor, w_fc: Tensor, w_proj: Tensor, fp8_state=None, grad_views=None) -> Tensor:
+def norm_relu2_mlp(x: Tensor, w_fc: Tensor, w_proj: Tensor, fp8_state=None, grad_views=None, fork: bool = False):
     """`grad_views = (g_fc, g_proj)`: slices of the bank gradient the weight gradients are accumulated
-    into by the backward GEMMs (the weights then receive no autograd gradient)."""
+    into by the backward GEMMs (the weights then receive no autograd gradient).
+    `fork`: also return x for the residual path; its gradient is then added inside the norm-backward kernel."""
     if grad_views is not None:
-        return _NormRelu2Mlp.apply(x, w_fc.detach(), w_proj.detach(), fp8_state, grad_views[0], grad_views[1])
-    return _NormRelu2Mlp.apply(x, w_fc, w_proj, fp8_state)
+        return _NormRelu2Mlp.apply(x, w_fc.detach(), w_proj.detach(), fp8_state, grad_views[0], grad_views[1], fork)
+    return _NormRelu2Mlp.apply(x, w_fc, w_proj, fp8_state, None, None, fork)
 
 
 class _BankLinear(torch.autograd.Function):

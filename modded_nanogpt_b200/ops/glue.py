@@ -15,18 +15,52 @@ from torch import Tensor
 from .native import lib
 
 
-class Term:
-    """One summand of `lincomb`: x * (addc + scalar * gate[:, col])."""
-    __slots__ = ("x", "scalar", "gate", "col", "addc")
+class GradSink:
+    """Gradient buffer shared by the fused ops that consume one tensor.  The first consumer to run in the backward pass
+    creates the buffer and hands it to autograd as its gradient; the later ones add into it (or, for gate columns,
+    write their own columns) and report no gradient, so autograd forms no sums of full-size tensors."""
+    __slots__ = ("buf",)
 
-    def __init__(self, x: Tensor, scalar: Tensor | None = None, gate: Tensor | None = None, col: int = 0, addc: float = 0.0):
+    def __init__(self):
+        self.buf = None
+
+
+class _SinkSource(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, t, sink):
+        ctx.sink = sink
+        return t
+
+    @staticmethod
+    def backward(ctx, g):
+        ctx.sink.buf = None                     # every consumer has run: the next backward starts a new buffer
+        return g, None
+
+
+def grad_sink(t: Tensor):
+    """Returns (t', sink): t' equals t and must be consumed ONLY through `Term(..., sink=sink)` (as x) or
+    `Term(..., gate_sink=sink)` (as gate) -- a consumer that returned its own gradient tensor for t' would have it
+    summed with a buffer that is still being added to.  (t, None) when no gradient is needed."""
+    if not (torch.is_grad_enabled() and t.requires_grad and t.is_cuda):
+        return t, None
+    sink = GradSink()
+    return _SinkSource.apply(t, sink), sink
+
+
+class Term:
+    """One summand of `lincomb`: x * (addc + scalar * gate[:, col]).  `sink` / `gate_sink`: the `GradSink` of x / gate."""
+    __slots__ = ("x", "scalar", "gate", "col", "addc", "sink", "gate_sink")
+
+    def __init__(self, x: Tensor, scalar: Tensor | None = None, gate: Tensor | None = None, col: int = 0, addc: float = 0.0,
+                 sink: GradSink | None = None, gate_sink: GradSink | None = None):
         self.x, self.scalar, self.gate, self.col, self.addc = x, scalar, gate, col, addc
+        self.sink, self.gate_sink = sink, gate_sink
 
 
 class _LinComb(torch.autograd.Function):
     @staticmethod
     def forward(ctx, meta, *tensors):
-        k, sidx, gidx, cols, addc = meta
+        k, sidx, gidx, cols, addc = meta[:5]
         xs = [t.contiguous() for t in tensors[:k]]
         scalars = [tensors[i] if i >= 0 else None for i in sidx]
         gates = [tensors[i] if i >= 0 else None for i in gidx]
@@ -37,7 +71,7 @@ class _LinComb(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, gout):
-        k, sidx, gidx, cols, addc = ctx.meta
+        k, sidx, gidx, cols, addc, xsinks, gsinks = ctx.meta
         tensors = ctx.saved_tensors
         xs = list(tensors[:k])
         scalars = [tensors[i] if i >= 0 else None for i in sidx]
@@ -46,11 +80,28 @@ class _LinComb(torch.autograd.Function):
         grads: list = [None] * len(tensors)
         dgate_bufs, dscal_bufs = {}, {}
         dgates, dscalars = [], []
+        dx_into, dx_acc, silent_gates = [None] * k, [False] * k, set()
         for j in range(k):
             gi, si = gidx[j], sidx[j]
+            sk = xsinks[j]
+            if sk is not None and need[j]:
+                if sk.buf is None:
+                    sk.buf = torch.empty_like(xs[j])
+                    grads[j] = sk.buf                  # the one gradient autograd sees for this tensor
+                else:
+                    dx_acc[j] = True
+                dx_into[j] = sk.buf
             if gi >= 0 and need[gi]:
                 if gi not in dgate_bufs:
-                    dgate_bufs[gi] = torch.zeros_like(tensors[gi], dtype=torch.bfloat16)
+                    gs = gsinks[j]
+                    if gs is not None:
+                        if gs.buf is None:
+                            gs.buf = torch.zeros_like(tensors[gi])
+                        else:
+                            silent_gates.add(gi)       # an earlier consumer already handed the buffer to autograd
+                        dgate_bufs[gi] = gs.buf
+                    else:
+                        dgate_bufs[gi] = torch.zeros_like(tensors[gi], dtype=torch.bfloat16)
                 dgates.append(dgate_bufs[gi])
             else:
                 dgates.append(None)
@@ -60,10 +111,14 @@ class _LinComb(torch.autograd.Function):
                 dscalars.append(dscal_bufs[si])
             else:
                 dscalars.append(None)
-        dxs = lib().lincomb_bwd(xs, scalars, gates, cols, addc, gout.contiguous(), [bool(n) for n in need[:k]], dgates, dscalars)
+        dxs = lib().lincomb_bwd(xs, scalars, gates, cols, addc, gout.contiguous(), [bool(n) for n in need[:k]], dgates, dscalars,
+                                dx_into, dx_acc)
         for j in range(k):
-            grads[j] = dxs[j]
+            if dx_into[j] is None:
+                grads[j] = dxs[j]
         for gi, buf in dgate_bufs.items():
+            if gi in silent_gates:
+                continue
             grads[gi] = buf if tensors[gi].dtype == torch.bfloat16 else buf.to(tensors[gi].dtype)
         for si, buf in dscal_bufs.items():
             grads[si] = buf.view(tensors[si].shape)
@@ -85,7 +140,10 @@ def lincomb(terms: list[Term]) -> Tensor:
 
     sidx = [slot(t.scalar) for t in terms]
     gidx = [slot(t.gate) for t in terms]
-    meta = (k, sidx, gidx, [int(t.col) for t in terms], [float(t.addc) for t in terms])
+    for t in terms:
+        assert t.gate_sink is None or t.gate.dtype == torch.bfloat16, "gate sinks hold bf16 gradients"
+    meta = (k, sidx, gidx, [int(t.col) for t in terms], [float(t.addc) for t in terms], [t.sink for t in terms],
+            [t.gate_sink for t in terms])
     return _LinComb.apply(meta, *[t.x for t in terms], *extra)
 
 

@@ -38,6 +38,44 @@ def test_lincomb_fwd_bwd():
         assert _rel(a, b) < 1e-2, (a.shape, _rel(a, b))
 
 
+def test_lincomb_grad_sinks_and_norm_fork():
+    """Shared gradient buffers (x and gate sinks) and the forked norm give the gradients autograd's own sums give."""
+    from modded_nanogpt_b200.ops import fused
+    from modded_nanogpt_b200.ops.glue import Term, grad_sink, lincomb
+    torch.manual_seed(1)
+    T, D = 515, 768
+    base = torch.randn(T, D, device="cuda").to(BF).requires_grad_(True)         # consumed by three lincombs
+    gate = (torch.randn(T, 8, device="cuda") * 0.5).to(BF).requires_grad_(True)
+    x_in = torch.randn(T, D, device="cuda").to(BF).requires_grad_(True)
+
+    def run(shared: bool):
+        for t in (base, gate, x_in):
+            t.grad = None
+        if shared:
+            b, bs = grad_sink(base)
+            g, gs = grad_sink(gate)
+            bt = lambda **kw: Term(b, sink=bs, **kw)
+            gk = lambda: dict(gate=g, gate_sink=gs)
+            fork = fused.rms_norm_fork
+        else:
+            bt = lambda **kw: Term(base, **kw)
+            gk = lambda: dict(gate=gate)
+            fork = lambda t: (fused.rms_norm(t), t)
+        x = x_in * 1.0
+        for layer in range(3):
+            y, x = fork(x)
+            x = lincomb([Term(x), Term(y, col=2 * layer, **gk()), bt(col=2 * layer + 1, **gk()), bt(addc=0.25)])
+        x = x + gate[:, 7:8] * 0.5                                               # a consumer outside the sink
+        (x.float() ** 2).mean().backward()
+        return x.detach(), base.grad.clone(), gate.grad.clone(), x_in.grad.clone()
+
+    want = run(False)
+    for _ in range(2):                                                           # twice: the sinks reset between backward passes
+        got = run(True)
+        for a, b in zip(got, want):
+            assert _rel(a, b) < 1e-2, (a.shape, _rel(a, b))
+
+
 @pytest.mark.parametrize("paired,key_offset,with_ve", [(False, False, False), (False, True, True), (True, False, True)])
 def test_qkv_post(paired, key_offset, with_ve):
     from modded_nanogpt_b200.models.gpt_fused import _rope_tables
