@@ -427,21 +427,39 @@ Tensor xsa_gate_fwd(const Tensor& y, const Tensor& v, const OptT& alpha, const O
   return out;
 }
 
-// Returns dy, dv (undefined without alpha), dalpha [T,H], dgate [T,H] (undefined when absent).
-std::vector<Tensor> xsa_gate_bwd(const Tensor& y, const Tensor& v, const OptT& alpha, const OptT& gate, const Tensor& dout) {
+// Returns dy, dv (undefined without alpha), dalpha [T,H], dgate [T,H] (undefined when absent).  da_into / dg_into
+// (optional): [T,H] views with unit column stride, e.g. columns of a wider shared gradient buffer, written instead.
+std::vector<Tensor> xsa_gate_bwd(const Tensor& y, const Tensor& v, const OptT& alpha, const OptT& gate, const Tensor& dout,
+                                 const OptT& da_into, const OptT& dg_into) {
   c10::cuda::CUDAGuard guard(y.device());
   TORCH_CHECK(dout.is_contiguous());
   const int64_t T = y.size(0), H = y.size(1);
   const bool ha = alpha.has_value() && alpha->defined(), hg = gate.has_value() && gate->defined();
   Tensor dy = torch::empty_like(y), dv, da, dg;
+  auto view_ok = [&](const Tensor& t) {
+    return t.dim() == 2 && t.size(0) == T && t.size(1) == H && t.stride(1) == 1 && t.scalar_type() == torch::kBFloat16;
+  };
   if (ha) {
     dv = torch::empty_like(v);
-    da = torch::empty({T, H}, y.options());
+    if (da_into.has_value() && da_into->defined()) {
+      TORCH_CHECK(view_ok(*da_into));
+      da = *da_into;
+    } else {
+      da = torch::empty({T, H}, y.options());
+    }
   }
-  if (hg) dg = torch::empty({T, H}, y.options());
+  if (hg) {
+    if (dg_into.has_value() && dg_into->defined()) {
+      TORCH_CHECK(view_ok(*dg_into));
+      dg = *dg_into;
+    } else {
+      dg = torch::empty({T, H}, y.options());
+    }
+  }
   auto st = [](const OptT& t) { return (t.has_value() && t->defined()) ? (int)t->stride(0) : 0; };
   check(mng_xsa_gate_bwd(y.data_ptr(), v.data_ptr(), optr(alpha), st(alpha), optr(gate), st(gate), dout.data_ptr(), dy.data_ptr(),
-                         ha ? dv.data_ptr() : nullptr, ha ? da.data_ptr() : nullptr, (int)H, hg ? dg.data_ptr() : nullptr, (int)H,
+                         ha ? dv.data_ptr() : nullptr, ha ? da.data_ptr() : nullptr, ha ? (int)da.stride(0) : 0,
+                         hg ? dg.data_ptr() : nullptr, hg ? (int)dg.stride(0) : 0,
                          T, (int)H, cur_stream()),
         "mng_xsa_gate_bwd");
   g_launches += 1;

@@ -10,7 +10,7 @@ from torch import Tensor
 
 from ..ops import functional as ops
 from ..ops import fused
-from ..ops.glue import Term, embed_direct, grad_sink, lincomb, qkv_post, xsa_gate
+from ..ops.glue import Term, cols_tap, embed_direct, grad_sink, lincomb, qkv_post, xsa_gate, xsa_gate_cols
 
 
 def fused_supported(model, x: Tensor) -> bool:
@@ -155,7 +155,12 @@ def forward_fused(m, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, big
                 ve_t = ve[pl.ve_slot]
             elif pl.ve_slot >= 0:
                 ve_t = ve[pl.ve_slot]
-                gate_in = torch.cat([attn_in[:, :6], ve_t[:, :6]], dim=-1)
+                if direct:                                   # the 6-column gradients join the main ones in place
+                    attn_in, a6 = cols_tap(attn_in, 6)
+                    ve_t, v6 = cols_tap(ve_t, 6)
+                    gate_in = torch.cat([a6, v6], dim=-1)
+                else:
+                    gate_in = torch.cat([attn_in[:, :6], ve_t[:, :6]], dim=-1)
                 vgate = (2 * torch.sigmoid(F.linear(gate_in, m.ve_gate_bank[pl.ve_slot]))).contiguous()
             if direct:
                 qkv = fused.bank_linear(attn_in, sa_lambdas[i, 0], [qk_all[sl], vo_all[sl][:D]], [qk_g[sl], vo_g[sl][:D]])
@@ -177,9 +182,13 @@ def forward_fused(m, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, big
                 w2 = pg[:, o + H:o + 2 * H].contiguous()
                 y = ops.dc_correction(y, q, k, v, w1, w2, seqlens, yarn.attn_scale, cfg.dc_window)
             if track1:
-                alpha = gt[:, lay["xsa"][i]:lay["xsa"][i] + H] if (pl.xsa and not pl.paired) else None
-                agate = gt[:, lay["attn"][i]:lay["attn"][i] + H] if pl.attn_gate else None
-                y = xsa_gate(y, v, alpha, agate)
+                ca = lay["xsa"][i] if (pl.xsa and not pl.paired) else None
+                cg = lay["attn"][i] if pl.attn_gate else None
+                gts = sunk(gname, gt) if gt.dtype == torch.bfloat16 else None
+                if gts is not None and sinks[gname][1] is not None:
+                    y = xsa_gate_cols(y, v, gts, sinks[gname][1], ca, cg)
+                else:
+                    y = xsa_gate(y, v, gt[:, ca:ca + H] if ca is not None else None, gt[:, cg:cg + H] if cg is not None else None)
             if direct:
                 attn_out = fused.bank_linear(y.reshape(T, D), sa_lambdas[i, 1], [vo_all[sl][D:]], [vo_g[sl][D:]])
             else:

@@ -47,6 +47,32 @@ def grad_sink(t: Tensor):
     return _SinkSource.apply(t, sink), sink
 
 
+class _ColsTap(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, t, n):
+        ctx.n = n
+        ctx.set_materialize_grads(False)
+        return t, t[:, :n].contiguous()
+
+    @staticmethod
+    def backward(ctx, g_main, g_cols):
+        if g_cols is None:
+            return g_main, None
+        if g_main is None:
+            raise RuntimeError("cols_tap: the carried-on tensor received no gradient")
+        g_main[:, :ctx.n] += g_cols             # a few columns, in place: no full-size zero fill and sum
+        return g_main, None
+
+
+def cols_tap(t: Tensor, n: int):
+    """Returns (t', t[:, :n]) where t' equals t and goes to t's main consumer.  The gradient of the n columns is added
+    in place into the gradient t' receives, which therefore must be a tensor its producer does not reuse (the fused
+    ops here return freshly allocated gradients)."""
+    if not (torch.is_grad_enabled() and t.requires_grad):
+        return t, t[:, :n]
+    return _ColsTap.apply(t, n)
+
+
 class Term:
     """One summand of `lincomb`: x * (addc + scalar * gate[:, col]).  `sink` / `gate_sink`: the `GradSink` of x / gate."""
     __slots__ = ("x", "scalar", "gate", "col", "addc", "sink", "gate_sink")
@@ -191,8 +217,43 @@ class _XsaGate(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dout):
         y, v, alpha, gate = ctx.saved_tensors
-        dy, dv, da, dg = lib().xsa_gate_bwd(y, v, alpha, gate, dout.contiguous())
+        dy, dv, da, dg = lib().xsa_gate_bwd(y, v, alpha, gate, dout.contiguous(), None, None)
         return dy, dv, da, dg
+
+
+class _XsaGateCols(torch.autograd.Function):
+    """`xsa_gate` with alpha / gate given as column offsets into one wide gate tensor that has a `GradSink`: the
+    backward writes its [T, H] column blocks straight into the shared gradient buffer."""
+
+    @staticmethod
+    def forward(ctx, y, v, gates, sink, col_alpha, col_gate):
+        y, v = y.contiguous(), v.contiguous()
+        H = y.shape[1]
+        alpha = gates[:, col_alpha:col_alpha + H] if col_alpha is not None else None
+        gate = gates[:, col_gate:col_gate + H] if col_gate is not None else None
+        out = lib().xsa_gate_fwd(y, v, alpha, gate)
+        ctx.save_for_backward(y, v, gates)
+        ctx.cfg = (sink, col_alpha, col_gate)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        y, v, gates = ctx.saved_tensors
+        sink, ca, cg = ctx.cfg
+        H = y.shape[1]
+        first = sink.buf is None
+        if first:
+            sink.buf = torch.zeros_like(gates)
+        sl = lambda t, c: t[:, c:c + H] if c is not None else None
+        dy, dv, _, _ = lib().xsa_gate_bwd(y, v, sl(gates, ca), sl(gates, cg), dout.contiguous(), sl(sink.buf, ca), sl(sink.buf, cg))
+        return dy, dv, (sink.buf if first else None), None, None, None
+
+
+def xsa_gate_cols(y: Tensor, v: Tensor, gates: Tensor, sink, col_alpha: int | None, col_gate: int | None) -> Tensor:
+    """`xsa_gate(y, v, gates[:, col_alpha:+H], gates[:, col_gate:+H])` for a gate tensor from `grad_sink`."""
+    if col_alpha is None and col_gate is None:
+        return y
+    return _XsaGateCols.apply(y, v, gates, sink, col_alpha, col_gate)
 
 
 def xsa_gate(y: Tensor, v: Tensor, alpha: Tensor | None, gate: Tensor | None) -> Tensor:
