@@ -144,12 +144,13 @@ lincomb_bwd_kernel(LinCombArgs a, LinCombGrads gr, const __nv_bfloat16* __restri
 constexpr int QP_WARPS = 8;
 constexpr float HEAD_EPS = 1.1920929e-07f;   // eps of the fp32 computation dtype, as F.rms_norm(eps=None)
 
+template <bool split>                         // rotary layout, compile-time so that each layout carries only its own shuffles
 __global__ void __launch_bounds__(QP_WARPS * 32)
 qkv_post_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                     const __nv_bfloat16* __restrict__ ve, const __nv_bfloat16* __restrict__ vgate, int vgate_stride,
                     const __nv_bfloat16* __restrict__ vadd, __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ k,
                     __nv_bfloat16* __restrict__ v, float* __restrict__ rstd_q, float* __restrict__ rstd_k, long long T, int H,
-                    int paired, int key_offset, int split) {
+                    int paired, int key_offset) {
   const int lane = threadIdx.x & 31;
   const long long idx = (long long)blockIdx.x * QP_WARPS + (threadIdx.x >> 5);     // (t, h)
   if (idx >= T * H) return;
@@ -184,8 +185,11 @@ qkv_post_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, const float* __restri
     float n2 = __bfloat162float(__float2bfloat16(b.x * r)), n3 = __bfloat162float(__float2bfloat16(b.y * r));
     float o0, o1, o2, o3;
     // split layout: the partner values live 16 lanes away (dims d and d + 64)
-    const float p0 = __shfl_xor_sync(0xffffffffu, n0, 16), p1 = __shfl_xor_sync(0xffffffffu, n1, 16);
-    const float p2 = __shfl_xor_sync(0xffffffffu, n2, 16), p3 = __shfl_xor_sync(0xffffffffu, n3, 16);
+    float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
+    if (split) {
+      p0 = __shfl_xor_sync(0xffffffffu, n0, 16); p1 = __shfl_xor_sync(0xffffffffu, n1, 16);
+      p2 = __shfl_xor_sync(0xffffffffu, n2, 16); p3 = __shfl_xor_sync(0xffffffffu, n3, 16);
+    }
     if (split && rot) {   // x1' = c x1 + s x2 (lanes 0-7), x2' = c x2 - s x1 (lanes 16-23)
       const float sg = lane < 16 ? 1.f : -1.f;
       o0 = c4[0] * n0 + sg * s4[0] * p0; o1 = c4[1] * n1 + sg * s4[1] * p1;
@@ -244,13 +248,14 @@ qkv_post_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, const float* __restri
 
 // Backward of the above.  dq, dk, dv: [T, H, 128].  Writes d_qkv [T, 3*H*128], and optionally
 // d_ve = vgate * dv, d_vgate[t,h] = <dv, ve> (bf16 column buffer), d_vadd = dv is the caller's alias.
+template <bool split>
 __global__ void __launch_bounds__(QP_WARPS * 32)
 qkv_post_bwd_kernel(const __nv_bfloat16* __restrict__ qkv, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                     const float* __restrict__ rstd_q, const float* __restrict__ rstd_k, const __nv_bfloat16* __restrict__ dq,
                     const __nv_bfloat16* __restrict__ dk, const __nv_bfloat16* __restrict__ dv, const __nv_bfloat16* __restrict__ ve,
                     const __nv_bfloat16* __restrict__ vgate, int vgate_stride, __nv_bfloat16* __restrict__ d_qkv,
                     __nv_bfloat16* __restrict__ d_ve, __nv_bfloat16* __restrict__ d_vgate, int d_vgate_stride, long long T, int H,
-                    int paired, int key_offset, int split) {
+                    int paired, int key_offset) {
   const int lane = threadIdx.x & 31;
   const long long idx = (long long)blockIdx.x * QP_WARPS + (threadIdx.x >> 5);
   if (idx >= T * H) return;
@@ -278,8 +283,11 @@ qkv_post_bwd_kernel(const __nv_bfloat16* __restrict__ qkv, const float* __restri
     const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&gu);
     float2 ga = __bfloat1622float2(gh[0]), gb = __bfloat1622float2(gh[1]);
     float d0, d1, d2, d3;                    // gradient w.r.t. the normalised (pre-rotary) values
-    const float q0 = __shfl_xor_sync(0xffffffffu, ga.x, 16), q1 = __shfl_xor_sync(0xffffffffu, ga.y, 16);
-    const float q2 = __shfl_xor_sync(0xffffffffu, gb.x, 16), q3 = __shfl_xor_sync(0xffffffffu, gb.y, 16);
+    float q0 = 0.f, q1 = 0.f, q2 = 0.f, q3 = 0.f;
+    if (split) {
+      q0 = __shfl_xor_sync(0xffffffffu, ga.x, 16); q1 = __shfl_xor_sync(0xffffffffu, ga.y, 16);
+      q2 = __shfl_xor_sync(0xffffffffu, gb.x, 16); q3 = __shfl_xor_sync(0xffffffffu, gb.y, 16);
+    }
     if (split && rot) {                      // transpose of [c s; -s c] over the (d, d + 64) pairs
       const float sg = lane < 16 ? -1.f : 1.f;
       d0 = c4[0] * ga.x + sg * s4[0] * q0; d1 = c4[1] * ga.y + sg * s4[1] * q1;
@@ -464,9 +472,10 @@ extern "C" int mng_qkv_post_fwd(const void* qkv, const float* cos_t, const float
                                 long long T, int H, int paired, int key_offset, int split, void* stream) {
   if (T == 0) return 0;
   const unsigned grid = (unsigned)((T * H + QP_WARPS - 1) / QP_WARPS);
-  qkv_post_fwd_kernel<<<grid, QP_WARPS * 32, 0, (cudaStream_t)stream>>>(
+  auto kern = split ? qkv_post_fwd_kernel<true> : qkv_post_fwd_kernel<false>;
+  kern<<<grid, QP_WARPS * 32, 0, (cudaStream_t)stream>>>(
       (const __nv_bfloat16*)qkv, cos_t, sin_t, (const __nv_bfloat16*)ve, (const __nv_bfloat16*)vgate, vgate_stride,
-      (const __nv_bfloat16*)vadd, (__nv_bfloat16*)q, (__nv_bfloat16*)k, (__nv_bfloat16*)v, rstd_q, rstd_k, T, H, paired, key_offset, split);
+      (const __nv_bfloat16*)vadd, (__nv_bfloat16*)q, (__nv_bfloat16*)k, (__nv_bfloat16*)v, rstd_q, rstd_k, T, H, paired, key_offset);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
@@ -476,10 +485,11 @@ extern "C" int mng_qkv_post_bwd(const void* qkv, const float* cos_t, const float
                                 int paired, int key_offset, int split, void* stream) {
   if (T == 0) return 0;
   const unsigned grid = (unsigned)((T * H + QP_WARPS - 1) / QP_WARPS);
-  qkv_post_bwd_kernel<<<grid, QP_WARPS * 32, 0, (cudaStream_t)stream>>>(
+  auto kern = split ? qkv_post_bwd_kernel<true> : qkv_post_bwd_kernel<false>;
+  kern<<<grid, QP_WARPS * 32, 0, (cudaStream_t)stream>>>(
       (const __nv_bfloat16*)qkv, cos_t, sin_t, rstd_q, rstd_k, (const __nv_bfloat16*)dq, (const __nv_bfloat16*)dk,
       (const __nv_bfloat16*)dv, (const __nv_bfloat16*)ve, (const __nv_bfloat16*)vgate, vgate_stride, (__nv_bfloat16*)d_qkv,
-      (__nv_bfloat16*)d_ve, (__nv_bfloat16*)d_vgate, d_vgate_stride, T, H, paired, key_offset, split);
+      (__nv_bfloat16*)d_ve, (__nv_bfloat16*)d_vgate, d_vgate_stride, T, H, paired, key_offset);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
