@@ -55,7 +55,12 @@ def main():
     ap.add_argument("--eager", action="store_true", help="profile the eager micro-step instead of the graph replay")
     ap.add_argument("--phases", type=int, default=0,
                     help="instead of the kernel table: CUDA-event time of the phases of N full steps (works under torchrun)")
+    ap.add_argument("--ops", type=int, default=0,
+                    help="instead of the kernel table: the N most expensive framework (aten) ops of one eager micro-step, "
+                         "grouped by input shapes -- what is left outside the native kernels")
     a = ap.parse_args()
+    if a.ops:
+        a.eager = True
     import torch
     from torch.autograd import DeviceType
     from torch.profiler import ProfilerActivity, profile
@@ -92,6 +97,17 @@ def main():
     torch.cuda.synchronize()
     if a.phases:
         return phases(tr, env, a.phases)
+    if a.ops:
+        with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA], record_shapes=True) as prof:
+            micro(851)
+            torch.cuda.synchronize()
+        evs = [e for e in prof.key_averages(group_by_input_shape=True) if e.key.startswith("aten::") and e.self_device_time_total > 0]
+        evs.sort(key=lambda e: -e.self_device_time_total)
+        print(f"aten ops of one eager micro-step: {sum(e.self_device_time_total for e in evs) / 1e3:.2f} ms of device time")
+        for e in evs[:a.ops]:
+            print(f"{e.self_device_time_total / 1e3:8.3f} ms {e.count:4d} x {e.self_device_time_total / e.count:8.1f} us  "
+                  f"{e.key:28s} {str(e.input_shapes)[:110]}")
+        return
     t = time.time()
     for _ in range(4):
         micro(850)
