@@ -198,6 +198,11 @@ class Trainer:
         self.model.quantize_mlp_fp8(bootstrap_down=True)
         self.log = logger or RunLogger(hp.run_id, env.master)
         self.train_loader = None
+        # The first micro-batch of the next step is prepared (host work + asynchronous copy) at the end of a step,
+        # while the device still runs that step's kernels; `_prefetch_state` is the loader cursor before it.
+        pf = os.environ.get("MNG_PREFETCH_BATCH")           # default: on with a GPU; "1" / "0" force it
+        self.prefetch_first_batch = pf == "1" or (pf is None and env.device.type == "cuda")
+        self._prefetched = self._prefetch_state = None
         self.step = 0
         self.training_time_ms = 0.0
         self.health = monitor_from_env(env)
@@ -247,17 +252,39 @@ class Trainer:
     def _train_step(self, step: int) -> torch.Tensor:
         if self.train_loader is None:
             self.train_loader = self.make_train_loader()
-        self.manager.advance_schedule(step)
+        m = self.manager
+        m.advance_schedule(step)
         total = None
         for _ in range(self.env.grad_accum_steps):
-            batch = self.train_loader.next_batch(self.manager.train_loader_send_args)
-            self.manager.train_loader_send_args = None
+            batch = self._take_batch()
             l = self.micro_step(batch, step)
             total = l if total is None else total + l
-        self.manager.step_optimizers(step)
+        m.step_optimizers(step)
         self.model.quantize_mlp_fp8(bootstrap_down=(step < 16))
         self.step = step + 1
+        if self.prefetch_first_batch and step + 1 < self.schedule.total_steps:
+            nxt, _ = self.schedule.lookup(step + 1)
+            if nxt.batch_size == m.batch_size and nxt.train_max_seq_len == m.train_max_seq_len:
+                self._prefetch_state = self.train_loader.state_dict()
+                self._prefetched = self.train_loader.next_batch()
         return total
+
+    def _take_batch(self):
+        m = self.manager
+        if self._prefetched is not None:
+            batch, self._prefetched, state = self._prefetched, None, self._prefetch_state
+            if m.train_loader_send_args is None:
+                return batch
+            self.train_loader.load_state_dict(state)     # the batch geometry changed after all: rewind and redo
+        batch = self.train_loader.next_batch(m.train_loader_send_args)
+        m.train_loader_send_args = None
+        return batch
+
+    def loader_state(self):
+        """Cursor of the training data for a checkpoint: the position before a prefetched, not yet used batch."""
+        if self.train_loader is None:
+            return None
+        return self._prefetch_state if self._prefetched is not None else self.train_loader.state_dict()
 
     @torch.no_grad()
     def validate(self, val_tokens: int | None = None) -> torch.Tensor:
@@ -298,6 +325,7 @@ class Trainer:
         (`train_gpt.py:2264-2301`)."""
         m = self.manager
         init = dict(model=copy.deepcopy(self.model.state_dict()), optimizer=m.get_state())
+        self._prefetched = self._prefetch_state = None
         self.train_loader = self.make_train_loader()
         val_loader = self.make_val_loader()
         trans = m.get_transition_steps()
@@ -330,6 +358,7 @@ class Trainer:
         m.reset(init["optimizer"])
         self.model.quantize_mlp_fp8(bootstrap_down=True)
         self.model.train()
+        self._prefetched = self._prefetch_state = None
         self.train_loader = None
         self.step = 0
 

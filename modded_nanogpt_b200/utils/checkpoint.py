@@ -62,7 +62,7 @@ def save_checkpoint(trainer, path: str | None = None, compiled_prefix: bool = Tr
     pending = {l: p.grad.detach().cpu().clone() for l, p in m.optimizer.params.items()
                if p.grad is not None and bool(p.grad.ne(0).any())}
     shard = dict(step=step, optimizer=m.optimizer.state_dict(), rank=env.rank, world_size=env.world_size,
-                 loader=trainer.train_loader.state_dict() if trainer.train_loader is not None else None,
+                 loader=trainer.loader_state(),
                  pending_grads=pending)
     torch.save(shard, os.path.join(d, f"optim_step{step:06d}_rank{env.rank}.pt"))
     main = os.path.join(d, f"state_step{step:06d}.pt")
@@ -107,6 +107,7 @@ def load_checkpoint(trainer, main_path: str) -> int:
         if shard.get("loader") is not None:
             if trainer.train_loader is None:
                 trainer.train_loader = trainer.make_train_loader()
+            trainer._prefetched = trainer._prefetch_state = None
             trainer.train_loader.load_state_dict(shard["loader"])
     elif env.world_size == 1 and "optimizer" in log and "state" in log["optimizer"]:
         m.optimizer.load_state_dict(log["optimizer"])

@@ -75,8 +75,11 @@ def _trainer(root, run_id, steps=6):
                    logger=RunLogger(run_id, True, log_dir=os.path.join(root, "logs"), quiet=True))
 
 
-def test_checkpoint_resume_is_bitwise(tiny_corpus, tmp_path, monkeypatch):
+@pytest.mark.parametrize("prefetch", ["0", "1"])
+def test_checkpoint_resume_is_bitwise(tiny_corpus, tmp_path, monkeypatch, prefetch):
+    """Also with the next step's first batch prefetched: the checkpoint stores the cursor before that batch."""
     monkeypatch.chdir(tmp_path)
+    monkeypatch.setenv("MNG_PREFETCH_BATCH", prefetch)
     a = _trainer(tiny_corpus, "full")
     for s in range(6):
         a.train_step(s)
