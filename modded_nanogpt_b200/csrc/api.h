@@ -134,6 +134,7 @@ int mng_xsa_gate_bwd(const void* y, const void* v, const void* alpha, int alpha_
 // ---- DC cross-head mixing (dc.cu) ---------------------------------------------------------------------
 int mng_dc_mix_fwd(const float* S, const void* w1, const int* doc_start, void* P, void* a, long long T, int H, int window,
                    void* stream);
+int mng_dc_fold(const void* part, void* out, long long T, int H, void* stream);
 int mng_dc_mix_bwd(const float* dM, const void* P, const void* a, const void* w1, const void* w2, void* dS, float* g_w1,
                    float* g_w2, long long T, int H, float scale, void* stream);
 

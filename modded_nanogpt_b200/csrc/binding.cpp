@@ -497,6 +497,18 @@ std::vector<Tensor> dc_mix_bwd(const Tensor& dM, const Tensor& P, const Tensor& 
   return {dS, g1, g2};
 }
 
+// part [H, T/128, 256, 128] bf16 (windowed gradients) -> [T, H, 128]: own rows of a block plus the next block's look-back rows
+Tensor dc_fold(const Tensor& part) {
+  TORCH_CHECK(part.dim() == 4 && part.is_contiguous() && part.scalar_type() == torch::kBFloat16 && part.size(2) == 256 &&
+              part.size(3) == 128);
+  const int64_t H = part.size(0), T = part.size(1) * 128;
+  c10::cuda::CUDAGuard guard(part.device());
+  Tensor out = torch::empty({T, H, 128}, part.options());
+  check(mng_dc_fold(part.data_ptr(), out.data_ptr(), T, (int)H, cur_stream()), "mng_dc_fold");
+  g_launches += 1;
+  return out;
+}
+
 // grad[sorted_ids[j], :] += g[perm[j], :]   (grad: bf16 [V, D] updated in place)
 void embed_bwd(const Tensor& g, const Tensor& sorted_ids, const Tensor& perm, Tensor& grad) {
   TORCH_CHECK(g.dim() == 2 && g.is_contiguous() && g.scalar_type() == torch::kBFloat16);
@@ -583,6 +595,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_bwd", &embed_bwd);
   m.def("dc_mix_fwd", &dc_mix_fwd);
   m.def("dc_mix_bwd", &dc_mix_bwd);
+  m.def("dc_fold", &dc_fold);
   m.def("attn_fwd", &attn_fwd);
   m.def("attn_bwd", &attn_bwd);
   m.def("status_tensor", &status_tensor);

@@ -119,6 +119,38 @@ extern "C" int mng_dc_mix_fwd(const float* S, const void* w1, const int* doc_sta
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
+// Fold of the windowed key/value gradients.  part [H, nblk, 256, 128] bf16: row j of block b's window is position
+// 128*b - 128 + j, so position t = 128*b + r gets part[h, b, 128 + r] + part[h, b + 1, r].  out [T, H, 128] bf16.
+// One thread per 8 elements.
+__global__ void __launch_bounds__(256)
+dc_fold_kernel(const __nv_bfloat16* __restrict__ part, __nv_bfloat16* __restrict__ out, long long T, int H) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;      // over T * H * 16
+  if (i >= T * H * 16) return;
+  const int seg = (int)(i & 15);
+  const long long th = i >> 4;
+  const long long t = th / H;
+  const int h = (int)(th - t * H);
+  const long long nblk = T >> 7, b = t >> 7;
+  const int r = (int)(t & 127);
+  const __nv_bfloat16* hi = part + (((long long)h * nblk + b) * 256 + 128 + r) * 128 + seg * 8;
+  uint4 u = *reinterpret_cast<const uint4*>(hi);
+  if (b + 1 < nblk) {
+    const uint4 v = *reinterpret_cast<const uint4*>(part + (((long long)h * nblk + b + 1) * 256 + r) * 128 + seg * 8);
+    __nv_bfloat162* a2 = reinterpret_cast<__nv_bfloat162*>(&u);
+    const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) a2[k] = __hadd2(a2[k], b2[k]);
+  }
+  *reinterpret_cast<uint4*>(out + th * 128 + seg * 8) = u;
+}
+
+extern "C" int mng_dc_fold(const void* part, void* out, long long T, int H, void* stream) {
+  if (T % 128) return -1;
+  const long long n = T * H * 16;
+  dc_fold_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>((const __nv_bfloat16*)part, (__nv_bfloat16*)out, T, H);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
 extern "C" int mng_dc_mix_bwd(const float* dM, const void* P, const void* a, const void* w1, const void* w2, void* dS,
                               float* g_w1, float* g_w2, long long T, int H, float scale, void* stream) {
   if (T % 128 || H > DC_MAXH) return -1;

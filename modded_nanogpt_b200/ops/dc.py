@@ -98,7 +98,7 @@ class _DC(torch.autograd.Function):
             fused.gemm(dS[h], _windows(kp, h, nblk, H, Dh), b_mn=True, out=_blocks(dq, h, nblk, H, Dh), bn=128)
             fused.gemm(dS[h], _blocks(q, h, nblk, H, Dh), a_mn=True, b_mn=True, out=dkp[h], bn=128)
             fused.gemm(a, _blocks(doutw, h, nblk, H, Dh), a_mn=True, b_mn=True, out=dvp[h], bn=128)
-        dk, dv = _fold(dkp, T, H, Dh), _fold(dvp, T, H, Dh)
+        dk, dv = C.dc_fold(dkp), C.dc_fold(dvp)             # one pass each (`_fold` is the same in torch ops)
         return dout, dq, dk, dv, g_w1.to(w1.dtype), g_w2.to(w2.dtype), None, None, None
 
 

@@ -140,6 +140,17 @@ def test_xsa_gate():
     assert _rel(only_gate, y.detach().float() * gates.detach().float()[:, 11:17].unsqueeze(-1)) < 5e-3
 
 
+def test_dc_fold_kernel_matches_torch_fold():
+    from modded_nanogpt_b200.ops import dc
+    from modded_nanogpt_b200.ops.native import lib
+    torch.manual_seed(3)
+    H, nblk = 6, 5
+    part = torch.randn(H, nblk, 256, 128, device="cuda").to(BF)
+    want = dc._fold(part, nblk * 128, H, 128)
+    got = lib().dc_fold(part)
+    assert got.shape == want.shape and torch.equal(got, want)
+
+
 def test_dc_gemm_path_matches_reference():
     from modded_nanogpt_b200.ops import dc, fused, reference as ref
     torch.manual_seed(3)
