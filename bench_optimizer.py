@@ -6,7 +6,8 @@ all-gather around the same update kernels).
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port 29533 \
         bench_optimizer.py --steps 20
 
-The bigram table's gradient is reduced densely here (the sparse row exchange needs the loader's row bookkeeping).
+Mode `fused_sparse` gives the bigram table a gradient with 98,304 random touched rows and lets the fused Adam kernel pull
+only those from the peers; the other modes reduce that table densely.
 Prints one JSON line per communication mode: device time (CUDA events, max over ranks) of odd steps
 (NorMuon + Adam) and even steps (NorMuon only)."""
 import argparse
@@ -33,7 +34,8 @@ def main():
     for mode in a.modes.split(","):
         if mode != "nccl" and env.world_size == 1:
             continue
-        os.environ["MNG_COMM"] = mode
+        os.environ["MNG_COMM"] = "fused" if mode == "fused_sparse" else mode
+        os.environ["MNG_SPARSE_PULL"] = "1" if mode == "fused_sparse" else "0"
         sched = TrainingSchedule(track1_stages(), 1270, 15, cooldown_frac=0.6)
         hp = Hyperparameters(val_loss_every=0, seed=0)
         tr = Trainer(track1_model(hp.val_batch_size // 8), sched, hp, env, use_cuda_graphs=False, sparse_min_world=1 << 30,
@@ -43,11 +45,20 @@ def main():
         g = torch.Generator(device="cuda").manual_seed(env.rank)
         params = list(tr.model.parameters())
 
+        bigram = tr.model.bigram_embed.weight
+
         def fill():
             for p in params:
                 if p.grad is None:
                     p.grad = torch.empty_like(p)
                 p.grad.copy_((torch.randn(p.shape, generator=g, device="cuda", dtype=torch.float32) * 1e-3).to(p.dtype))
+            if mode == "fused_sparse":
+                # the bigram gradient as training leaves it: rows of the 2 x 49,152 tokens since the last Adam step
+                rows = torch.randint(0, bigram.shape[0], (98304,), generator=g, device="cuda")
+                keep = torch.zeros(bigram.shape[0], dtype=torch.bool, device="cuda")
+                keep[rows] = True
+                bigram.grad.mul_(keep[:, None])
+                tr.manager.optimizer.coll.mark_rows("bigram_embed", rows)
 
         times = {0: [], 1: []}
         for step in range(849, 849 + a.steps + 4):

@@ -79,6 +79,12 @@ typedef struct {
   long long n;
   int p_is_f32;
   float beta1, beta2, eps, step_size, eff_wd, grad_mul;
+  // Row masks (optional, local memory): row_mask[r * mask_stride + row] != 0 iff rank r's gradient row `row` (rows of
+  // row_elems elements, counted from the parameter's start) may be non-zero.  Rows whose byte is 0 are not loaded from
+  // rank r at all: a sparse pull over NVLink for embedding-type gradients.  row_elems must be a multiple of 8.
+  const unsigned char* row_mask;
+  long long mask_stride;
+  int row_elems;
 } AdamDesc;
 int mng_adam(const AdamDesc* d, void* stream);
 

@@ -226,9 +226,17 @@ PeerPtrs peers_from(const std::vector<int64_t>& ptrs, int64_t self) {
 // gradient / parameter buffers on each rank (length 1 = local only).
 void adam(const std::vector<int64_t>& grad_ptrs, const std::vector<int64_t>& param_ptrs, int64_t self, int64_t off, Tensor& exp_avg,
           Tensor& exp_avg_sq, int64_t n, bool p_is_f32, double beta1, double beta2, double eps, double step_size, double eff_wd,
-          double grad_mul) {
+          double grad_mul, const c10::optional<Tensor>& row_mask, int64_t row_elems) {
   c10::cuda::CUDAGuard guard(exp_avg.device());
   AdamDesc d{};
+  if (row_mask.has_value() && row_mask->defined()) {        // [ranks, rows] uint8 in local memory
+    TORCH_CHECK(row_mask->dim() == 2 && row_mask->is_contiguous() && row_mask->scalar_type() == torch::kUInt8 &&
+                row_mask->size(0) == (int64_t)grad_ptrs.size() && row_mask->is_cuda());
+    TORCH_CHECK(row_elems > 0 && (off + n + row_elems - 1) / row_elems <= row_mask->size(1));
+    d.row_mask = row_mask->data_ptr<uint8_t>();
+    d.mask_stride = row_mask->size(1);
+    d.row_elems = (int)row_elems;
+  }
   d.grads = peers_from(grad_ptrs, grad_ptrs.size() == 1 ? 0 : self);
   d.params = peers_from(param_ptrs, param_ptrs.size() == 1 ? 0 : self);
   d.off = off;

@@ -32,7 +32,8 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
 template <bool F32>
 __global__ void __launch_bounds__(256)
 adam_kernel(PeerPtrs grads, PeerPtrs params, long long off, float* __restrict__ m, float* __restrict__ v, long long n,
-            float beta1, float beta2, float eps, float step_size, float eff_wd, float gmul) {
+            float beta1, float beta2, float eps, float step_size, float eff_wd, float gmul,
+            const unsigned char* __restrict__ row_mask, long long mask_stride, int row_elems) {
   constexpr int VEC = F32 ? 4 : 8;
   const long long nvec = n / VEC;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += (long long)gridDim.x * blockDim.x) {
@@ -42,9 +43,16 @@ adam_kernel(PeerPtrs grads, PeerPtrs params, long long off, float* __restrict__ 
     for (int t = 0; t < VEC; ++t) g[t] = 0.f;
     // all peers' loads are issued before the first is consumed: one NVLink round trip instead of grads.n
     uint4 raw[MNG_MAX_RANKS];
+    const long long row = row_mask ? e / row_elems : 0;     // a vector never straddles rows (row_elems % 8 == 0)
 #pragma unroll
-    for (int r = 0; r < MNG_MAX_RANKS; ++r)
-      if (r < grads.n) raw[r] = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(grads.p[r]) + e * (F32 ? 4 : 2));
+    for (int r = 0; r < MNG_MAX_RANKS; ++r) {
+      if (r < grads.n) {
+        if (row_mask && row_mask[r * mask_stride + row] == 0)
+          raw[r] = make_uint4(0u, 0u, 0u, 0u);               // rank r did not touch this row: nothing crosses NVLink
+        else
+          raw[r] = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(grads.p[r]) + e * (F32 ? 4 : 2));
+      }
+    }
 #pragma unroll
     for (int r = 0; r < MNG_MAX_RANKS; ++r) {
       if (r < grads.n) {
@@ -318,13 +326,16 @@ extern "C" int mng_adam(const AdamDesc* d, void* stream) {
   if (a.n == 0) return 0;
   const int vec = a.p_is_f32 ? 4 : 8;
   if (a.n % vec || a.off % vec) return -1;
+  if (a.row_mask && (a.row_elems <= 0 || a.row_elems % 8 || a.mask_stride <= 0)) return -3;
   const unsigned grid = grid_for(a.n / vec);
   if (a.p_is_f32)
     adam_kernel<true><<<grid, 256, 0, (cudaStream_t)stream>>>(a.grads, a.params, a.off, a.exp_avg, a.exp_avg_sq, a.n, a.beta1,
-                                                              a.beta2, a.eps, a.step_size, a.eff_wd, a.grad_mul);
+                                                              a.beta2, a.eps, a.step_size, a.eff_wd, a.grad_mul, a.row_mask,
+                                                              a.mask_stride, a.row_elems);
   else
     adam_kernel<false><<<grid, 256, 0, (cudaStream_t)stream>>>(a.grads, a.params, a.off, a.exp_avg, a.exp_avg_sq, a.n, a.beta1,
-                                                               a.beta2, a.eps, a.step_size, a.eff_wd, a.grad_mul);
+                                                               a.beta2, a.eps, a.step_size, a.eff_wd, a.grad_mul, a.row_mask,
+                                                               a.mask_stride, a.row_elems);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 

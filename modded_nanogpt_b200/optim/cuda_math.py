@@ -90,7 +90,8 @@ class CudaMath(TorchMath):
                         scratch, red_rows, float(cfg.beta2), float(eff_wd), lrs)
 
     def adam(self, p_slice: Tensor, grad: Tensor, state: dict, cfg: ParamConfig, step_size: float, eff_wd: float,
-             grad_ptrs=None, param_ptrs=None, off: int = 0, grad_mul: float = 1.0) -> None:
+             grad_ptrs=None, param_ptrs=None, off: int = 0, grad_mul: float = 1.0, row_mask=None, row_elems: int = 0) -> None:
+        """`row_mask` ([ranks, rows] uint8, local) with `row_elems`: gradient rows a rank did not touch are not loaded."""
         n = p_slice.numel()
         is_f32 = p_slice.dtype == torch.float32
         vec = 4 if is_f32 else 8
@@ -103,7 +104,7 @@ class CudaMath(TorchMath):
             grad_ptrs, param_ptrs, off = [grad.data_ptr()], [p_slice.data_ptr()], 0
         b1, b2 = cfg.adam_betas
         lib().adam(grad_ptrs, param_ptrs, self.rank, off, state["exp_avg"], state["exp_avg_sq"], n, is_f32, b1, b2, cfg.eps,
-                   step_size, eff_wd, grad_mul)
+                   step_size, eff_wd, grad_mul, row_mask, row_elems)
 
     def transpose_add(self, src: Tensor, dst: Tensor) -> None:
         if src.dtype == torch.bfloat16 and src.is_contiguous() and dst.is_contiguous():

@@ -9,6 +9,10 @@ communication themselves (`csrc/optim.cu`):
   loads, sums in fp32 and scales by 1/world - no separate reduction pass, no staging buffer;
 * parameter all-gather: the kernel that computes the new weights stores them into every rank's
   parameter tensor with peer stores;
+* sparse pull for embedding-type gradients (`enable_row_masks`): every rank keeps a byte per row of the table saying
+  whether its gradient row was touched since the last Adam step and copies that mask into every peer's memory before
+  the barrier; the Adam kernel then skips the peer loads of untouched rows (they are exactly zero), so only touched
+  rows cross NVLink - the device-side counterpart of the host-driven row exchange of `train_gpt.py:263-346`;
 * ordering: one `peer_barrier` kernel (release/acquire flags in the arena's signal pad, bounded
   spin that reports through the status word) after backward and one after the updates.
 
@@ -62,8 +66,38 @@ class NvlinkCollectives(TorchCollectives):
             p.grad = gv
             self.offsets[label] = (po, go)
         self.epoch = 0
+        self.row_masks = {}           # label -> dict(touched, masks, peers, cols): see enable_row_masks
         torch.cuda.synchronize()
         dist.barrier()
+
+    # -- sparse pull ---------------------------------------------------------------------------------
+    def enable_row_masks(self, label: str, param) -> bool:
+        """Collective.  From now on the gradient rows of `param` ([rows, cols]) that `mark_rows` was not told about since
+        the last Adam step are treated as zero and not read from this rank by anybody."""
+        import torch.distributed._symmetric_memory as symm
+        if label not in self.offsets or param.dim() != 2 or param.shape[1] % 8 or param.shape[0] % self.world_size:
+            return False
+        rows, W = param.shape[0], self.world_size
+        masks = symm.empty((W, rows), dtype=torch.uint8, device=self.device)
+        handle = symm.rendezvous(masks, dist.group.WORLD.group_name)
+        masks.fill_(1)                                        # until the first publication: read everything
+        peers = [handle.get_buffer(q, (W, rows), torch.uint8) for q in range(W)]
+        self.row_masks[label] = dict(touched=torch.zeros(rows, dtype=torch.uint8, device=self.device), masks=masks,
+                                     peers=peers, handle=handle, cols=param.shape[1])
+        torch.cuda.synchronize()
+        dist.barrier()
+        return True
+
+    def mark_rows(self, label: str, rows: torch.Tensor):
+        st = self.row_masks.get(label)
+        if st is not None:
+            st["touched"].index_fill_(0, rows.reshape(-1).long(), 1)
+
+    def _publish_masks(self):
+        # plain device-to-device copies into the peers' mask tables; ordered before the barrier on this stream
+        for st in self.row_masks.values():
+            for q in range(self.world_size):
+                st["peers"][q][self.rank].copy_(st["touched"], non_blocking=True)
 
     # ------------------------------------------------------------------------------------------
     def _ptrs(self, label: str, which: int):
@@ -103,6 +137,7 @@ class NvlinkCollectives(TorchCollectives):
         return (None, None)           # nothing to launch: the update kernel reads the peers directly
 
     def reduce_barrier(self):
+        self._publish_masks()
         self.peer_barrier()           # every rank's backward (and tied-embedding transpose-add) is complete
 
     def gather_barrier(self):
@@ -121,8 +156,11 @@ class NvlinkCollectives(TorchCollectives):
         if cfg.comms.startswith("sharded"):
             n = p.numel() // W
             shard = p.data.view(-1)[r * n:(r + 1) * n]
+            rm = self.row_masks.get(label)
             self.math.adam(shard, None, state, cfg, step_size, eff_wd, grad_ptrs=gptrs, param_ptrs=pptrs, off=r * n,
-                           grad_mul=1.0 / W)
+                           grad_mul=1.0 / W, row_mask=rm["masks"] if rm else None, row_elems=rm["cols"] if rm else 0)
+            if rm:
+                rm["touched"].zero_()                         # the gradients are cleared after this step as well
         else:       # replicated: all ranks read all gradients and apply the same update to their own copy
             self.math.adam(p.data.view(-1), None, state, cfg, step_size, eff_wd, grad_ptrs=gptrs,
                            param_ptrs=[pptrs[r]], off=0, grad_mul=1.0 / W)

@@ -87,6 +87,15 @@ class TrainingManager:
             rank=env.rank, world_size=env.world_size)
         if hasattr(self.optimizer.coll, "prepare"):
             self.optimizer.coll.prepare(self.optimizer)
+        # fused NVLink path: the Adam kernel pulls only the bigram-gradient rows that a rank touched (`mark_rows` in
+        # `Trainer.micro_step`); MNG_SPARSE_PULL=0 keeps the dense pull
+        self.row_mask_labels = []
+        coll = self.optimizer.coll
+        if (getattr(coll, "fused", False) and hasattr(model, "bigram_embed") and env.world_size > 1
+                and os.environ.get("MNG_SPARSE_PULL", "1") != "0"
+                and self.param_table.get("bigram_embed", {}).get("comms") == "sharded_sparse"):
+            if coll.enable_row_masks("bigram_embed", model.bigram_embed.weight):
+                self.row_mask_labels.append("bigram_embed")
         self.split_step = schedule.split_step
         self.device = dev
         self.reset()
@@ -230,6 +239,8 @@ class Trainer:
     def micro_step(self, batch, step: int) -> torch.Tensor:
         m = self.manager
         m.sparse_index_update(step, batch.bigram_cpu)
+        if m.row_mask_labels and self.model.training:
+            m.optimizer.coll.mark_rows("bigram_embed", batch.bigram_inputs)
         if self.graphs is not None and self.model.training:
             m.sparse_index_share(step)
             return self.graphs.run(batch, m.get_forward_args())

@@ -99,6 +99,8 @@ def load_checkpoint(trainer, main_path: str) -> int:
         shard = torch.load(shard_path, map_location="cpu", weights_only=False)
         m.optimizer.load_state_dict(shard["optimizer"])
         for l, g in shard.get("pending_grads", {}).items():
+            if l in getattr(m, "row_mask_labels", ()):           # restored rows count as touched: mark all of them
+                m.optimizer.coll.row_masks[l]["touched"].fill_(1)
             p = m.optimizer.params[l]
             if p.grad is None:
                 p.grad = g.to(p.device, p.dtype)

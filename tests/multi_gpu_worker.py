@@ -37,6 +37,7 @@ def main():
         tr = build(env, comm)
         opt = tr.manager.optimizer
         assert getattr(opt.coll, "fused", False) == (comm != "nccl")
+        assert bool(tr.manager.row_mask_labels) == (comm != "nccl" and env.world_size > 1)
         with torch.no_grad():      # away from the zero inits
             g = torch.Generator(device="cuda").manual_seed(1)
             for p in tr.model.parameters():
@@ -46,6 +47,15 @@ def main():
             g = torch.Generator(device="cuda").manual_seed(100 * step + env.rank)
             for p in tr.model.parameters():
                 grad = (torch.randn(p.shape, generator=g, device="cuda", dtype=torch.float32) * 1e-3).to(p.dtype)
+                if p is tr.model.bigram_embed.weight:
+                    # an embedding gradient: only the rows of the tokens seen are non-zero, and the fused path is
+                    # told which (it pulls just those rows from the peers)
+                    rows = torch.randint(0, p.shape[0], (p.shape[0] // 3,), generator=g, device="cuda")
+                    keep = torch.zeros(p.shape[0], dtype=torch.bool, device="cuda")
+                    keep[rows] = True
+                    grad = grad * keep[:, None]
+                    if tr.manager.row_mask_labels:
+                        opt.coll.mark_rows("bigram_embed", rows)
                 if p.grad is None:
                     p.grad = grad
                 else:

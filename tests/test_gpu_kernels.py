@@ -261,10 +261,36 @@ def test_adam_kernel(fused):
         g = (torch.randn(n, device="cuda") * 0.01).to(dt)
         m, v = torch.rand(n, device="cuda") * 0.01, torch.rand(n, device="cuda") * 1e-4
         pr, mr, vr = p.clone(), m.clone(), v.clone()
-        C.adam([g.data_ptr()], [p.data_ptr()], 0, 0, m, v, n, dt == torch.float32, 0.9, 0.99, 1e-10, 3e-3, 2e-4, 1.0)
+        C.adam([g.data_ptr()], [p.data_ptr()], 0, 0, m, v, n, dt == torch.float32, 0.9, 0.99, 1e-10, 3e-3, 2e-4, 1.0, None, 0)
         ref.adam_update_(pr, g, mr, vr, 0.9, 0.99, 1e-10, 3e-3, 2e-4)
         assert torch.allclose(m, mr, rtol=1e-5, atol=1e-8) and torch.allclose(v, vr, rtol=1e-5, atol=1e-10)
         assert (p.float() - pr.float()).abs().max() < (2e-3 if dt == BF else 1e-6)
+
+
+def test_adam_kernel_row_mask(fused):
+    """Rows whose mask byte is 0 are not read: the update equals Adam on the gradient with those rows zeroed, even
+    when the skipped rows hold garbage.  Two "ranks" are two gradient buffers of this GPU."""
+    from modded_nanogpt_b200.ops import native
+    C = native.lib()
+    torch.manual_seed(12)
+    rows, cols = 96, 768
+    n = rows * cols
+    p = (torch.randn(n, device="cuda") * 0.1).to(BF)
+    gs = [(torch.randn(rows, cols, device="cuda") * 0.01).to(BF) for _ in range(2)]
+    mask = (torch.rand(2, rows, device="cuda") < 0.4).to(torch.uint8)
+    clean = [g * mask[i][:, None].to(BF) for i, g in enumerate(gs)]                 # what the ranks "really" hold
+    dirty = [torch.where(mask[i][:, None].bool(), g, torch.full_like(g, 7.0)) for i, g in enumerate(gs)]
+    off, cnt = 16 * cols, 64 * cols                                                  # update rows 16..79 only
+    outs = []
+    for grads, mk in ((clean, None), (dirty, mask)):
+        pp = p.clone()
+        m, v = torch.zeros(cnt, device="cuda"), torch.zeros(cnt, device="cuda")
+        C.adam([g.data_ptr() for g in grads], [pp.data_ptr(), pp.data_ptr()], 0, off, m, v, cnt, False, 0.9, 0.99, 1e-10,
+               3e-3, 2e-4, 0.5, mk, cols if mk is not None else 0)
+        outs.append((pp, m, v))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+    assert not torch.equal(outs[0][0], p)
 
 
 def test_normuon_kernels(fused):
