@@ -225,7 +225,7 @@ class GPTMedium(nn.Module):
         `ops.fused`) and, in training, weight and embedding gradients accumulated straight into the
         parameters' `.grad` buffers (no full-bank temporaries from slicing the parameter banks)."""
         from ..ops import fused
-        from ..ops.glue import Term, embed_direct, lincomb, qkv_post, xsa_gate
+        from ..ops.glue import Term, cols_tap, embed_direct, grad_sink, lincomb, qkv_post, xsa_gate
         L, H, Dh, D, V = self.num_layers, self.num_heads, self.head_dim, self.model_dim, self.vocab_size
         T = input_seq.size(0)
         max_len = sc.train_max_seq_len if self.training else self.eval_seq_len
@@ -256,6 +256,9 @@ class GPTMedium(nn.Module):
         cos_t, sin_t = cos[:, :32].contiguous(), sin[:, :32].contiguous()
         bounds = fused.doc_bounds(seqlens, T) if fused.ATTN_KERNEL else None
         skips, x_backout, skip_idx = [], None, 0
+        # x0 / x02 feed every layer's mix: one shared gradient buffer each instead of a sum per layer
+        x0_s, x0_sink = grad_sink(x0)
+        x02_s, x02_sink = grad_sink(x02)
         for i in range(L):
             terms = []
             if i in SKIP_OUT:
@@ -264,12 +267,16 @@ class GPTMedium(nn.Module):
                 skip_idx += 1
                 terms.append(Term(skips.pop(), scalar=resid[i].reshape(1), gate=sg, col=0))
             if i == 0:
-                terms += [Term(x, scalar=(resid[0] + x0l[0, 0]).reshape(1)), Term(x02, scalar=x0l[0, 1].reshape(1))]
+                terms += [Term(x, scalar=(resid[0] + x0l[0, 0]).reshape(1)),
+                          Term(x02_s, scalar=x0l[0, 1].reshape(1), sink=x02_sink)]
             else:
-                terms += [Term(x, scalar=resid[i].reshape(1)), Term(x0, scalar=x0l[i, 0].reshape(1)),
-                          Term(x02, scalar=x0l[i, 1].reshape(1))]
+                terms += [Term(x, scalar=resid[i].reshape(1)), Term(x0_s, scalar=x0l[i, 0].reshape(1), sink=x0_sink),
+                          Term(x02_s, scalar=x0l[i, 1].reshape(1), sink=x02_sink)]
             x = lincomb(terms)
-            xin = fused.rms_norm(x)
+            xin, x = fused.rms_norm_fork(x)                  # x's gradients meet inside the norm backward
+            x16 = xin[:, :16]
+            if direct:
+                xin, x16 = cols_tap(xin, 16)                 # gate inputs: their gradient joins the main one in place
             is_long = i in LONG_LAYERS
             if direct:
                 qkv = fused.bank_linear(xin, sa[i, 0], [w_all[i][:3 * D]], [g_all[i][:3 * D]])
@@ -278,11 +285,11 @@ class GPTMedium(nn.Module):
             ve_t = vgate = None
             if i in VE_LAYERS:
                 ve_t = ve[VE_LAYERS[i]]
-                vgate = (2 * torch.sigmoid(F.linear(xin[:, :16], self.value_embed_gate_bank[self._ve_slot[i]]))).contiguous()
+                vgate = (2 * torch.sigmoid(F.linear(x16, self.value_embed_gate_bank[self._ve_slot[i]]))).contiguous()
             q, k, v = qkv_post(qkv, cos_t, sin_t, ve_t, vgate, None, H, False, is_long, split=True)
             window = sc.ws_long if is_long else sc.ws_short
             y = ops.attention(q, k, v, seqlens, window, self.yarn.attn_scale, max_len, bounds)
-            agate = torch.sigmoid(F.linear(xin[:, :16], self.attn_gate_bank[i])).contiguous()
+            agate = torch.sigmoid(F.linear(x16, self.attn_gate_bank[i])).contiguous()
             y = xsa_gate(y, v, None, agate)
             if direct:
                 attn_out = fused.bank_linear(y.reshape(T, D), sa[i, 1], [w_all[i][3 * D:]], [g_all[i][3 * D:]])
@@ -291,7 +298,8 @@ class GPTMedium(nn.Module):
             x = lincomb([Term(x), Term(attn_out)])
             st = self._fp8_state.layer(i) if (self.training and self.use_fp8 and self._fp8_state is not None) else None
             if direct:
-                h = fused.norm_relu2_mlp(x, self.mlp_bank[i, 0], self.mlp_bank[i, 1], st, (self.mlp_bank.grad[i, 0], self.mlp_bank.grad[i, 1]))
+                h, x = fused.norm_relu2_mlp(x, self.mlp_bank[i, 0], self.mlp_bank[i, 1], st,
+                                            (self.mlp_bank.grad[i, 0], self.mlp_bank.grad[i, 1]), fork=True)
             else:
                 h = ops.norm_relu2_mlp(x, self.mlp_bank[i, 0], self.mlp_bank[i, 1], st)
             x = lincomb([Term(x), Term(h)])
