@@ -266,10 +266,33 @@ class GPT(nn.Module):
         if not (self.use_fp8 and self.mlp_bank.is_cuda):
             return
         from ..ops import fused
-        with torch.no_grad():
-            self._fp8_state = fused.quantize_mlp_weights(self.mlp_bank, self._fp8_state,
-                                                         self._mlp_down_proj_scales, self._mlp_down_proj_next_scales,
-                                                         bootstrap_down)
+
+        def refresh(bootstrap):
+            with torch.no_grad():
+                self._fp8_state = fused.quantize_mlp_weights(self.mlp_bank, self._fp8_state,
+                                                             self._mlp_down_proj_scales, self._mlp_down_proj_next_scales,
+                                                             bootstrap)
+
+        # The steady-state refresh is ~70 tiny launches (a few microseconds of work each): once the state exists and
+        # the call has run eagerly twice it is replayed as one CUDA graph.  Every tensor it touches is persistent (the
+        # bank, the state, the scale buffers); a changed bank address or state object drops the graph.
+        import os
+        if bootstrap_down or self._fp8_state is None or os.environ.get("MNG_FP8_GRAPH", "1") == "0":
+            return refresh(bootstrap_down)
+        key = (self.mlp_bank.data_ptr(), id(self._fp8_state), self._mlp_down_proj_scales.data_ptr())
+        ent = getattr(self, "_fp8_graph", None)
+        if ent is None or ent["key"] != key:
+            ent = self._fp8_graph = dict(key=key, runs=0, graph=None)
+        if ent["graph"] is None:
+            if ent["runs"] < 2:
+                ent["runs"] += 1
+                return refresh(False)
+            g = torch.cuda.CUDAGraph()
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g):
+                refresh(False)
+            ent["graph"] = g
+        ent["graph"].replay()
 
     # ----------------------------------------------------------------------------------
     def _gate_mlp(self, x: Tensor, gid: int) -> Tensor:

@@ -39,3 +39,24 @@ def test_graph_replay_matches_eager(tmp_path):
     assert torch.isfinite(b).all()
     assert ((a - b).abs() / a.abs()).max() < 2e-2, (losses[False], losses[True])
     assert b[-1] < b[0]
+
+
+def test_fp8_refresh_graph_matches_eager(tmp_path):
+    """The graph-replayed FP8 weight refresh leaves the same e4m3 copies and scales as a fresh eager quantisation."""
+    from modded_nanogpt_b200.ops import fused
+    tr = _trainer(tmp_path, False, "fp8g")
+    model = tr.model
+    for it in range(5):
+        with torch.no_grad():
+            model.mlp_bank.mul_(1.0 + 0.05 * (it + 1)).add_(torch.randn_like(model.mlp_bank) * 1e-3)
+        model.quantize_mlp_fp8(bootstrap_down=False)
+        st = model._fp8_state
+        ref = fused.quantize_mlp_weights(model.mlp_bank, None, model._mlp_down_proj_scales.clone(),
+                                         model._mlp_down_proj_next_scales.clone(), False)
+        for name in ("fc8", "fc_scale", "projT8", "projT_scale"):
+            a, b = getattr(st, name), getattr(ref, name)
+            assert torch.equal(a.view(torch.uint8) if a.dtype != torch.float32 else a,
+                               b.view(torch.uint8) if b.dtype != torch.float32 else b), (it, name)
+    assert model._fp8_graph["graph"] is not None
+    torch.cuda.synchronize()
+    fused.check_status()
