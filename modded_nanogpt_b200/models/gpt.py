@@ -273,11 +273,11 @@ class GPT(nn.Module):
                                                              self._mlp_down_proj_scales, self._mlp_down_proj_next_scales,
                                                              bootstrap)
 
-        # The steady-state refresh is ~70 tiny launches (a few microseconds of work each): once the state exists and
-        # the call has run eagerly twice it is replayed as one CUDA graph.  Every tensor it touches is persistent (the
-        # bank, the state, the scale buffers); a changed bank address or state object drops the graph.
+        # The steady-state refresh is ~70 tiny launches.  With MNG_FP8_GRAPH=1 it is replayed as one CUDA graph once the
+        # state exists and the call has run eagerly twice (every tensor it touches is persistent; a changed bank
+        # address or state object drops the graph).  Measured gain: 0.47 -> 0.40 ms per step, so it is off by default.
         import os
-        if bootstrap_down or self._fp8_state is None or os.environ.get("MNG_FP8_GRAPH", "1") == "0":
+        if bootstrap_down or self._fp8_state is None or os.environ.get("MNG_FP8_GRAPH", "0") != "1":
             return refresh(bootstrap_down)
         key = (self.mlp_bank.data_ptr(), id(self._fp8_state), self._mlp_down_proj_scales.data_ptr())
         ent = getattr(self, "_fp8_graph", None)

@@ -41,9 +41,10 @@ def test_graph_replay_matches_eager(tmp_path):
     assert b[-1] < b[0]
 
 
-def test_fp8_refresh_graph_matches_eager(tmp_path):
+def test_fp8_refresh_graph_matches_eager(tmp_path, monkeypatch):
     """The graph-replayed FP8 weight refresh leaves the same e4m3 copies and scales as a fresh eager quantisation."""
     from modded_nanogpt_b200.ops import fused
+    monkeypatch.setenv("MNG_FP8_GRAPH", "1")
     tr = _trainer(tmp_path, False, "fp8g")
     model = tr.model
     for it in range(5):
