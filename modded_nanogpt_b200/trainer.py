@@ -276,8 +276,12 @@ class Trainer:
         if self.prefetch_first_batch and step + 1 < self.schedule.total_steps:
             nxt, _ = self.schedule.lookup(step + 1)
             if nxt.batch_size == m.batch_size and nxt.train_max_seq_len == m.train_max_seq_len:
-                self._prefetch_state = self.train_loader.state_dict()
-                self._prefetched = self.train_loader.next_batch()
+                state = self.train_loader.state_dict()
+                try:
+                    self._prefetched, self._prefetch_state = self.train_loader.next_batch(), state
+                except StopIteration:                        # out of data: the step that needs the batch reports it
+                    self.train_loader.load_state_dict(state)
+                    self._prefetched = self._prefetch_state = None
         return total
 
     def _take_batch(self):
