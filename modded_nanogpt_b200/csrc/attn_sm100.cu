@@ -780,14 +780,28 @@ extern "C" int mng_attn_bwd(const void* q, const void* k, const void* v, const v
   // MNG_ATTN_BWD=static keeps the persistent grid but strides the items instead of claiming them from the counter
   static const std::string mode = [] { const char* e = getenv("MNG_ATTN_BWD"); return std::string(e ? e : ""); }();
   static const bool per_item = mode == "tile";
-  static int* work = nullptr;
-  if (!work && cudaGetSymbolAddress(reinterpret_cast<void**>(&work), g_atb_work) != cudaSuccess) return -6;
-  int* const w0 = mode == "static" ? nullptr : work;
-  static int sms = 0;
-  if (sms == 0) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -6;
+  // the work counters are a __device__ symbol: its address and the SM count belong to the current device
+  constexpr int kMaxDevices = 64;
+  static int* work_of[kMaxDevices] = {};
+  static int sms_of[kMaxDevices] = {};
+  static std::mutex mu;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -6;
+  int* work = nullptr;
+  int sms = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!work_of[dev]) {
+      if (cudaGetSymbolAddress(reinterpret_cast<void**>(&work_of[dev]), g_atb_work) != cudaSuccess ||
+          cudaDeviceGetAttribute(&sms_of[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+        work_of[dev] = nullptr;
+        return -6;
+      }
+    }
+    work = work_of[dev];
+    sms = sms_of[dev];
   }
+  int* const w0 = mode == "static" ? nullptr : work;
   const int items = ((T + 127) / 128) * H;
   dim3 grid(per_item ? items : (items < sms ? items : sms));
   AttnBwdParams pa{doc_start, doc_end, lse2, delta, reinterpret_cast<__nv_bfloat16*>(dk), reinterpret_cast<__nv_bfloat16*>(dv),

@@ -12,8 +12,10 @@
 // the library holds from load until the process exits.
 //
 // Rules for callers:
-//   * `cols` must not exceed MNG_STATIC_SCRATCH_COLS; larger inputs are refused with
-//     MNG_ERR_TOO_LARGE and nothing is launched.  Inputs and outputs are still the caller's.
+//   * `cols` must not exceed MNG_STATIC_SCRATCH_COLS and `rows` must not exceed MNG_STATIC_MAX_ROWS
+//     (the kernels tile rows in blocks of 64 along a grid dimension that holds 65,535 blocks); larger
+//     inputs are refused with MNG_ERR_TOO_LARGE and nothing is launched.  Inputs and outputs are
+//     still the caller's.
 //   * The first call on each device resolves the device address of the scratch array
 //     (cudaGetSymbolAddress, with that device current).  Make that first call outside of any
 //     stream capture; later calls only enqueue a memset and two kernels on `stream`.
@@ -29,10 +31,11 @@ extern "C" {
 #endif
 
 #define MNG_STATIC_SCRATCH_COLS 65536
+#define MNG_STATIC_MAX_ROWS (65535LL * 64)
 
 enum {
   MNG_OK = 0,
-  MNG_ERR_TOO_LARGE = -22,     // cols > MNG_STATIC_SCRATCH_COLS
+  MNG_ERR_TOO_LARGE = -22,     // cols > MNG_STATIC_SCRATCH_COLS or rows > MNG_STATIC_MAX_ROWS
   MNG_ERR_SYMBOL = -23,        // the scratch array's device address could not be resolved
   MNG_ERR_BAD_SHAPE = -24,     // rows <= 0 or cols <= 0
   MNG_ERR_LAUNCH = -25,        // memset or kernel launch failed

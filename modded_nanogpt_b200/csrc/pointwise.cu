@@ -357,7 +357,7 @@ int static_scratch_ptr(unsigned int** out) {
 extern "C" int mng_quant_transpose_e4m3_static(const void* src, void* q, float* scale, long long rows, long long cols,
                                                void* stream) {
   if (rows <= 0 || cols <= 0) return MNG_ERR_BAD_SHAPE;
-  if (cols > MNG_STATIC_SCRATCH_COLS) return MNG_ERR_TOO_LARGE;
+  if (cols > MNG_STATIC_SCRATCH_COLS || rows > MNG_STATIC_MAX_ROWS) return MNG_ERR_TOO_LARGE;
   unsigned int* scratch = nullptr;
   const int rc = static_scratch_ptr(&scratch);
   if (rc != MNG_OK) return rc;
@@ -374,7 +374,9 @@ extern "C" int mng_quant_transpose_e4m3_static(const void* src, void* q, float* 
 extern "C" const char* mng_static_strerror(int code) {
   switch (code) {
     case MNG_OK: return "ok";
-    case MNG_ERR_TOO_LARGE: return "cols exceeds MNG_STATIC_SCRATCH_COLS (65536): the built-in scratch array is too small";
+    case MNG_ERR_TOO_LARGE:
+      return "cols exceeds MNG_STATIC_SCRATCH_COLS (65536, the size of the built-in scratch array) or rows exceeds "
+             "MNG_STATIC_MAX_ROWS (4194240, the launch grid's limit)";
     case MNG_ERR_SYMBOL: return "could not resolve the device address of the built-in scratch array on the current device";
     case MNG_ERR_BAD_SHAPE: return "rows and cols must be positive";
     case MNG_ERR_LAUNCH: return "memset or kernel launch failed";

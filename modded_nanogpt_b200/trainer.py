@@ -8,6 +8,7 @@ with the reference's log lines), checkpoint save/resume and device-timed step st
 """
 from __future__ import annotations
 
+import contextlib
 import copy
 import os
 import sys
@@ -122,11 +123,11 @@ class TrainingManager:
         if new_long != self.ws_long and (cap is None or new_long <= cap):
             for y in {id(self.model.yarn): self.model.yarn, id(self.model.yarn_paired_head): self.model.yarn_paired_head}.values():
                 y.apply(self.ws_long * self.block_size, new_long * self.block_size)
+        # Idempotent: a pending re-parameterisation stays pending until the loader has consumed it (`Trainer._take_batch`
+        # clears it), so calling this twice for the same step - `run()` and then `train_step()` - changes nothing.
         if stage.batch_size != self.batch_size or stage.train_max_seq_len != self.train_max_seq_len:
             self.train_loader_send_args = (stage.batch_size, stage.train_max_seq_len, self.env.grad_accum_steps)
             self.batch_size, self.train_max_seq_len = stage.batch_size, stage.train_max_seq_len
-        else:
-            self.train_loader_send_args = None
         self.ws_long = new_long
         self.mtp_weights = torch.tensor(self.schedule.mtp_weights[step], dtype=torch.float32, device=self.device)
         self.prefix_weight = torch.tensor([self.schedule.prefix_weights[step]], dtype=torch.float32, device=self.device)
@@ -214,6 +215,7 @@ class Trainer:
         self._prefetched = self._prefetch_state = None
         self.step = 0
         self.training_time_ms = 0.0
+        self._status_host = self._status_event = None
         self.health = monitor_from_env(env)
         if use_cuda_graphs is None:
             use_cuda_graphs = env.device.type == "cuda" and os.environ.get("MNG_CUDA_GRAPHS", "1") != "0"
@@ -257,8 +259,48 @@ class Trainer:
             # peers that failed or stalled are noticed here, on the host, before any kernel that waits on them
             self.health.pre_step(step)
             with self.health.guard():
-                return self._train_step(step)
-        return self._train_step(step)
+                self.check_device_status(sync=False)
+                out = self._train_step(step)
+                self._probe_status()
+                return out
+        self.check_device_status(sync=False)
+        out = self._train_step(step)
+        self._probe_status()
+        return out
+
+    # -- device status word ------------------------------------------------------------------
+    # Every bounded device-side wait (peer barriers, mbarrier waits of the GEMM / attention kernels) records a code
+    # in one status word when it gives up.  The word is read wherever the host synchronises anyway (validation,
+    # checkpoint, end of run) and, without any synchronisation, one step late through an asynchronous copy into
+    # pinned memory: replicas that diverged after a timed-out barrier stop the run instead of training on.
+    def _probe_status(self):
+        if self.env.device.type != "cuda":
+            return
+        from .ops import native
+        if self._status_host is None:
+            self._status_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+            self._status_event = torch.cuda.Event()
+        elif not self._status_event.query():
+            return                                            # the previous probe has not landed yet: keep it
+        self._status_host.copy_(native.lib().status_tensor(torch.empty(0, device=self.env.device)).view(torch.int32),
+                                non_blocking=True)
+        self._status_event.record()
+
+    def check_device_status(self, sync: bool = True):
+        """Raises `DeviceWaitTimeout` if a kernel's bounded wait has expired.  `sync=False` only looks at the last
+        asynchronous probe that has completed (no host-device synchronisation)."""
+        if self.env.device.type != "cuda":
+            return
+        from .runtime.health import DeviceWaitTimeout, check_device
+        if sync:
+            ctx = self.health.guard() if self.health is not None else contextlib.nullcontext()
+            with ctx:
+                check_device(self.env.device)
+            return
+        if self._status_host is not None and self._status_event.query() and int(self._status_host[0]) != 0:
+            code = int(self._status_host[0])
+            self._status_host.zero_()
+            raise DeviceWaitTimeout(f"device status word {code}: a bounded wait on a peer flag or barrier expired")
 
     def _train_step(self, step: int) -> torch.Tensor:
         if self.train_loader is None:
@@ -307,6 +349,7 @@ class Trainer:
         val_tokens = val_tokens or hp.val_tokens
         assert val_tokens % hp.val_batch_size == 0
         steps = env.grad_accum_steps * val_tokens // hp.val_batch_size
+        self.check_device_status()                            # the caller has synchronised: the clock is stopped
         loader = self.make_val_loader()
         self.model.eval()
         tot = 0
@@ -323,11 +366,12 @@ class Trainer:
     # -- checkpoint ------------------------------------------------------------------------
     def save_checkpoint(self, path: str | None = None):
         from .utils.checkpoint import save_checkpoint
+        self.check_device_status()                            # never persist weights written after a timed-out wait
         return save_checkpoint(self, path)
 
-    def load_checkpoint(self, path: str):
+    def load_checkpoint(self, path: str, strict: bool = True):
         from .utils.checkpoint import load_checkpoint
-        return load_checkpoint(self, path)
+        return load_checkpoint(self, path, strict)
 
     # -- the whole run -----------------------------------------------------------------------
     def _sync(self):
@@ -410,6 +454,7 @@ class Trainer:
             self.train_step(step)
             approx = self.training_time_ms + 1000 * (time.perf_counter() - t0)
             log.print0(f"step:{step + 1}/{total} train_time:{approx:.0f}ms step_avg:{approx / (step + 1):.2f}ms", console=True)
+        self.check_device_status()
         if env.device.type == "cuda":
             log.print0(f"peak memory allocated: {torch.cuda.max_memory_allocated() // 1024 // 1024} MiB "
                        f"reserved: {torch.cuda.max_memory_reserved() // 1024 // 1024} MiB", console=True)

@@ -83,9 +83,13 @@ def save_checkpoint(trainer, path: str | None = None, compiled_prefix: bool = Tr
     return main
 
 
-def load_checkpoint(trainer, main_path: str) -> int:
+def load_checkpoint(trainer, main_path: str, strict: bool = True) -> int:
     """Restores model, optimizer shard of this rank, loader cursor, rotary and schedule state.
-    Returns the step to continue from."""
+    Returns the step to continue from.
+
+    The optimizer shards are per rank, so they only fit a job of the same world size.  When this rank's shard is
+    missing or was written by a different world size, `strict=True` (default) raises instead of resuming with
+    zeroed moments and a rewound data cursor; `strict=False` loads the model only and says so loudly."""
     log = torch.load(main_path, map_location="cpu", weights_only=False)
     if not isinstance(log, dict) or "model" not in log or "step" not in log:
         raise ValueError(f"{main_path}: not a checkpoint of this framework or of the reference")
@@ -111,8 +115,19 @@ def load_checkpoint(trainer, main_path: str) -> int:
                 trainer.train_loader = trainer.make_train_loader()
             trainer._prefetched = trainer._prefetch_state = None
             trainer.train_loader.load_state_dict(shard["loader"])
-    elif env.world_size == 1 and "optimizer" in log and "state" in log["optimizer"]:
+    elif (env.world_size == 1 and log.get("world_size", 1) == 1 and "optimizer" in log
+          and "state" in log["optimizer"]):
         m.optimizer.load_state_dict(log["optimizer"])
+        print(f"[checkpoint] {main_path}: no per-rank shard, optimizer state taken from the main file; "
+              "the data cursor restarts at the first shard", flush=True)
+    else:
+        why = (f"written by world_size {log.get('world_size')}, this job has {env.world_size}"
+               if log.get("world_size", env.world_size) != env.world_size else f"{shard_path} is missing")
+        msg = (f"{main_path}: optimizer state, pending Adam gradients and the loader cursor cannot be restored ({why})")
+        if strict:
+            raise RuntimeError(msg + "; pass strict=False to resume from the model weights alone")
+        print(f"[checkpoint] WARNING: {msg}; continuing from step {step} with fresh optimizer state and data from "
+              "the first shard", flush=True)
     if "yarn" in log:
         trainer.model.yarn.load_state_dict(log["yarn"])
         trainer.model.yarn_paired_head.load_state_dict(log["yarn_paired"])

@@ -135,3 +135,71 @@ def test_full_run_log_lines(tiny_corpus, tmp_path, monkeypatch):
     for line in text.splitlines():
         if line.startswith("step:"):
             assert VAL_LINE.fullmatch(line) or TRAIN_LINE.fullmatch(line), line
+
+
+def _staged_trainer(root, run_id, steps=6):
+    """Three scheduled stages with different batch sizes and document caps (as tracks 1 and 2 have)."""
+    from modded_nanogpt_b200.config import Hyperparameters, TrainingSchedule, TrainingStage, tiny_model
+    from modded_nanogpt_b200.runtime.dist import DistEnv
+    from modded_nanogpt_b200.trainer import Trainer
+    from modded_nanogpt_b200.utils.logging import RunLogger
+    env = DistEnv(0, 1, 0, torch.device("cpu"), 1, 1.0, True)
+    hp = Hyperparameters(data_path=root, num_scheduled_iterations=steps, num_extension_iterations=0, val_batch_size=2048,
+                         val_tokens=2048, val_loss_every=0, run_id=run_id)
+    stages = [TrainingStage(duration=1 / 3, train_max_seq_len=s, batch_size=b, window_sizes=(1, 2), lr_mul=1.0,
+                            mtp_weights_start=[1.0], mtp_weights_end=[1.0])
+              for b, s in ((1024, 128), (2048, 256), (3072, 256))]
+    stages.append(TrainingStage(train_max_seq_len=256, batch_size=3072, window_sizes=(1, 2), lr_mul=1.0,
+                                mtp_weights_start=[1.0], mtp_weights_end=[1.0]))
+    return Trainer(tiny_model(2048), TrainingSchedule(stages, steps, 0), hp, env, param_dtype=torch.float32,
+                   logger=RunLogger(run_id, True, log_dir=os.path.join(root, "logs"), quiet=True))
+
+
+@pytest.mark.parametrize("prefetch", ["0", "1"])
+@pytest.mark.parametrize("drive", ["run", "train_step"])
+def test_stage_transitions_reparameterise_the_loader(tiny_corpus, tmp_path, monkeypatch, prefetch, drive):
+    """Every step trains on its stage's batch size and document cap, whether the schedule is advanced once
+    (bare `train_step`) or twice per step (`run()` advances it before validation, `train_step` again)."""
+    monkeypatch.chdir(tmp_path)
+    monkeypatch.setenv("MNG_PREFETCH_BATCH", prefetch)
+    t = _staged_trainer(tiny_corpus, f"stages_{drive}_{prefetch}")
+    seen = []
+    orig = t.micro_step
+
+    def spy(batch, step):
+        doc_lens = torch.diff(batch.cum_seqlens.long())
+        seen.append((step, batch.inputs.numel(), int(doc_lens.max())))
+        return orig(batch, step)
+
+    t.micro_step = spy
+    if drive == "run":
+        t.run(do_warmup=False)
+    else:
+        for s in range(6):
+            t.train_step(s)
+    assert [(s, n) for s, n, _ in seen] == [(0, 1024), (1, 1024), (2, 2048), (3, 2048), (4, 3072), (5, 3072)]
+    assert all(d <= 128 for s, _, d in seen if s < 2) and all(d <= 256 for _, _, d in seen)
+    assert t.manager.batch_size == 3072
+
+
+def test_checkpoint_from_another_world_size_is_refused(tiny_corpus, tmp_path, monkeypatch):
+    monkeypatch.chdir(tmp_path)
+    a = _trainer(tiny_corpus, "ws_a")
+    for s in range(2):
+        a.train_step(s)
+    path = a.save_checkpoint()
+    blob = torch.load(path, weights_only=False)
+    blob["world_size"] = 8                                      # as if an 8-rank job had written it
+    torch.save(blob, path)
+    b = _trainer(tiny_corpus, "ws_b")
+    with pytest.raises(RuntimeError, match="world_size 8"):
+        b.load_checkpoint(path)
+    assert b.load_checkpoint(path, strict=False) == 2           # model only, announced on stdout
+    for (n, pa), (_, pb) in zip(a.model.state_dict().items(), b.model.state_dict().items()):
+        assert torch.equal(pa, pb), n
+    os.remove(os.path.join(os.path.dirname(path), "optim_step000002_rank0.pt"))
+    blob["world_size"] = 1
+    blob.pop("optimizer")
+    torch.save(blob, path)
+    with pytest.raises(RuntimeError, match="is missing"):
+        _trainer(tiny_corpus, "ws_c").load_checkpoint(path)

@@ -54,3 +54,5 @@ def test_static_scratch_entry_point_rejects_oversize():
     rc = fn(x.data_ptr(), x.data_ptr(), x.data_ptr(), 8, 65537, torch.cuda.current_stream().cuda_stream)
     assert rc == -22 and b"65536" in lib.mng_static_strerror(rc)
     assert fn(x.data_ptr(), x.data_ptr(), x.data_ptr(), 0, 8, None) == -24
+    # more rows than the kernels' launch grid covers: refused up front, not reported as a failed launch
+    assert fn(x.data_ptr(), x.data_ptr(), x.data_ptr(), 65535 * 64 + 1, 8, torch.cuda.current_stream().cuda_stream) == -22
