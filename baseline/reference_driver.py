@@ -65,14 +65,15 @@ def drive(args, ref_dir: str) -> dict:
     if world != args.gpus:
         return {"impl": "reference", "unavailable": f"--gpus {args.gpus} but WORLD_SIZE={world}"}
     K, W = args.steps, args.warmup
-    batch = 24 * 2048 * 8
-    root = f"/tmp/mng_bench_ref_{K}_{W}"
+    stage_idx = int(getattr(args, "stage", 2))
+    batch = (8, 16, 24)[stage_idx] * 2048 * 8
+    root = f"/tmp/mng_bench_ref_{stage_idx}_{K}_{W}"
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     from modded_nanogpt_b200.data.shards import write_synthetic_corpus   # data generation only
     if rank == 0:
-        need = int(batch * (K * 2 + W + 3) * 1.02) + 1_000_000
+        need = int(batch * (K * 2 + W + 12) * 1.02) + 1_000_000
         # the reference loader preloads a second shard at start-up, so there must be at least two
-        write_synthetic_corpus(root, train_tokens=need, val_tokens=3_000_000, seed=0, max_doc_len=2048,
+        write_synthetic_corpus(root, train_tokens=need, val_tokens=3_000_000, seed=0, max_doc_len=(896, 2048, 2048)[stage_idx],
                                shard_tokens=max(2_000_000, need // 3 + 1))
     os.environ["DATA_PATH"] = root
     # The reference's FP8 MLP Triton kernel (linear_relu_square_kernel, TMA-descriptor persistent GEMM
@@ -121,11 +122,10 @@ def drive(args, ref_dir: str) -> dict:
     ns["training_manager"] = tm
     model.prefix_table.copy_(ns["build_prefix_table"](model.vocab_size))
 
-    stage_idx = 2
     for b0, _ in sched.boundaries[:stage_idx + 1]:
         tm.advance_schedule(b0)
     first = sched.boundaries[stage_idx][0] + 1
-    tm.optimizer.split_embed = True
+    tm.optimizer.split_embed = first > tm.split_step
     stage = ns["TRAINING_STAGES"][stage_idx]
     loader = ns["distributed_data_generator"](rargs.train_files, stage.batch_size, stage.train_max_seq_len,
                                               grad_accum_steps=ga)
@@ -135,24 +135,40 @@ def drive(args, ref_dir: str) -> dict:
 
     def one_step(step, read_loss):
         tm.advance_schedule(step)
-        total = 0.0
+        total = None
         for _ in range(ga):
             inputs, targets, cum_seqlens, bigram_inputs, bigram_cpu = loader.send(tm.train_loader_send_args)
             tm.sparse_index_update(step, bigram_cpu)
             loss = model(inputs, targets, cum_seqlens, bigram_inputs, tm.get_forward_args()).sum() * grad_scale
             tm.sparse_index_share(step)
             loss.backward()
-            if read_loss:
-                total += float(loss)
+            # the step loss is summed on the device and read once per step, as the other arm does
+            total = loss.detach() if total is None else total + loss.detach()
             del loss
         tm.step_optimizers(step)
         model.quantize_mlp_fp8(bootstrap_down=(step < 16))
-        return total
+        return float(total) if read_loss else 0.0
 
+    from torch._dynamo.utils import counters
+
+    def compiled_frames():
+        return int(counters["frames"]["ok"]) + int(counters["stats"]["unique_graphs"])
+
+    # Warm-up: W steps, then (untimed, to the reference's benefit) more until an odd and an even step in a row
+    # compiled nothing new: the sparse-comms path that only exists at 8 ranks compiles late.
     step = first
-    for _ in range(max(W, 2)):
+    extra = 0
+    quiet = 0
+    for i in range(max(W, 2) + 8):
+        before = compiled_frames()
         one_step(step, False)
         step += 1
+        quiet = quiet + 1 if compiled_frames() == before else 0
+        if i + 1 >= max(W, 2):
+            if quiet >= 2:
+                break
+            extra += 1
+    frames_before_timing = compiled_frames()
 
     def timed(read_loss):
         nonlocal step
@@ -175,11 +191,13 @@ def drive(args, ref_dir: str) -> dict:
 
     dev_ms, _, _ = timed(False)
     e2e_ms, e2e_wall, last = timed(True)
+    recompiles_in_timed = compiled_frames() - frames_before_timing
     tokens = stage.batch_size * K
     T = stage.batch_size // 8
-    h2d = ga * (T * 4 + T * 8 + 128 * 4 + T * 4)
+    max_docs = {16384: 64, 32768: 96, 49152: 128}[T]
+    h2d = ga * (T * 4 + T * 8 + max_docs * 4 + T * 4)
     out = {
-        "impl": "reference", "metric": "train tokens/s, track-1 GPT, stage-2 batch (393216 tok/step)",
+        "impl": "reference", "metric": f"train tokens/s, track-1 GPT, stage-{stage_idx} batch ({stage.batch_size} tok/step)",
         "value": tokens / (dev_ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": dev_ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": ("bf16 (fp8 lm_head; bf16 MLP: reference run with its own DISABLE_FP8=1)" if os.environ.get("DISABLE_FP8")
@@ -189,7 +207,8 @@ def drive(args, ref_dir: str) -> dict:
                    "attention": "FlashAttention-2 (FA3 is a Hopper-only binary)", "first_step": first,
                    "reference_env": {"DISABLE_FP8": os.environ.get("DISABLE_FP8", "")}},
         "e2e": {"value": tokens / (max(e2e_ms, e2e_wall) / 1e3), "unit": "tokens/s", "ms_per_step": max(e2e_ms, e2e_wall) / K,
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4 * ga, "last_loss": last},
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "last_loss": last},
+        "extra_warmup_steps": extra, "recompiles_in_timed_regions": recompiles_in_timed,
         "gpu_launches": None,
     }
     dist.barrier()

@@ -9,11 +9,17 @@ streams, random-init weights.  Every step is a full training step: forward, back
         --master-port 29511 bench.py --gpus 8 --steps 10 --warmup 3
 
 Two timed regions of K steps each, both bracketed by barrier + synchronize and timed with CUDA
-events, max over ranks:
-  * `value`  - inputs already resident on the device;
-  * `e2e`    - through `Trainer.train_step`: every step copies its inputs from pinned host memory
-               and reads the step loss back to the host.
+events, max over ranks; both go through `Trainer.train_step`, which packs every micro-batch on the
+host and copies it from pinned memory inside the timed region (the reference arm does the same):
+  * `value`  - the step loss stays on the device;
+  * `e2e`    - additionally reads the step loss back to the host after every step.
 Inputs (K*393,216 tokens of ids/targets/hashes per region) are far larger than L2.
+
+`--mlp bf16` runs the MLP forward in bf16 (the lm_head + loss path stays FP8): the precision the
+reference arm runs at on this GPU, for a like-for-like pair next to the FP8 headline.
+`--stage 0|1|2` times another stage of the schedule (131,072 / 262,144 / 393,216 tokens per step).
+At N > 1 the line carries `params_identical`: a bitwise checksum of every parameter compared
+across ranks after the warm-up and after the timed steps.
 """
 from __future__ import annotations
 
@@ -38,7 +44,8 @@ def parse():
     ap.add_argument("--stage", type=int, default=2, help="schedule stage whose batch/window settings are timed")
     ap.add_argument("--tokens-per-gpu", type=int, default=0, help="override the micro-batch size (smoke runs only)")
     ap.add_argument("--track", type=int, default=1, choices=[1, 2],
-                    help="2 = track-2 model at its 524,288-token plateau batch (own arm only; not the headline)")
+                    help="2 = track-2 model at its 524,288-token plateau batch (not the headline)")
+    ap.add_argument("--mlp", default="fp8", choices=["fp8", "bf16"], help="precision of the MLP forward (own arm)")
     return ap.parse_args()
 
 
@@ -46,7 +53,7 @@ def reference_arm(args):
     from baseline.run_reference import run_reference
     try:
         out = run_reference(args)
-    except Exception as e:  # noqa: BLE001 - the reference arm must never take the driver down
+    except Exception as e:  # noqa: BLE001 - a failed reference run is reported as a line, not as a crash
         import traceback
         traceback.print_exc()
         out = {"impl": "reference", "unavailable": f"reference run failed: {type(e).__name__}: {str(e)[:300]}"}
@@ -59,9 +66,6 @@ def reference_arm(args):
 def main():
     args = parse()
     if args.impl == "reference":
-        if args.track != 1:
-            print(json.dumps({"impl": "reference", "unavailable": "the reference arm is wired for the track-1 headline only"}))
-            return
         return reference_arm(args)
     import torch
     import torch.distributed as dist
@@ -109,9 +113,12 @@ def main():
         model = GPTMedium(max_seq_len=eval_seq, world_size=env.world_size, grad_scale=env.grad_scale, use_fp8=True,
                           eval_seq_len=eval_seq)
     else:
-        hp = Hyperparameters(data_path=root, val_loss_every=0, seed=0)
+        hp = Hyperparameters(data_path=root, val_loss_every=0, seed=0, disable_fp8=(args.mlp == "bf16"))
+    if model is not None and args.mlp == "bf16":
+        model.use_fp8 = False
     tr = Trainer(None if model is not None else track1_model(hp.val_batch_size // 8), sched, hp, env, model=model,
                  logger=RunLogger(f"bench_{os.getpid()}", env.master, log_dir="/tmp/mng_logs", quiet=True))
+    tr.model.fp8_head = True                                  # as the reference: the loss path is FP8 in both MLP modes
     # enter the timed stage the way a run would: windows / YaRN state of the earlier stages applied
     for b0, _ in sched.boundaries[:args.stage + 1]:
         tr.manager.advance_schedule(b0)
@@ -146,23 +153,27 @@ def main():
         ms = max_over_ranks(e0.elapsed_time(e1))
         return ms, max_over_ranks(wall * 1e3), native.lib().launch_count() + replayed() - launches0, clocks, out
 
-    # ---- region 1: device-resident inputs ------------------------------------------------------
-    staged = [[tr.train_loader.next_batch() for _ in range(env.grad_accum_steps)] for _ in range(K)]
-    torch.cuda.synchronize()
+    def params_checksum_identical():
+        """Bitwise: every parameter's bytes summed as integers, compared across ranks."""
+        if env.world_size == 1:
+            return None
+        sums = torch.stack([p.detach().contiguous().view(torch.int16 if p.element_size() == 2 else torch.int32)
+                            .to(torch.int64).sum() for p in tr.model.parameters()])
+        lo, hi = sums.clone(), sums.clone()
+        dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+        dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+        return bool(torch.equal(lo, hi))
 
+    same_after_warmup = params_checksum_identical()
+
+    # ---- region 1: the loss stays on the device ---------------------------------------------------
     def region_device():
         nonlocal step
-        m = tr.manager
-        for batches in staged:
-            m.advance_schedule(step)
-            for b in batches:
-                tr.micro_step(b, step)
-            m.step_optimizers(step)
-            tr.model.quantize_mlp_fp8(bootstrap_down=False)
+        for _ in range(K):
+            tr.train_step(step)
             step += 1
 
     dev_ms, _, launches, clocks, _ = timed(region_device)
-    del staged
 
     # ---- region 2: end to end through the public API -------------------------------------------
     h2d = d2h = 0
@@ -181,17 +192,18 @@ def main():
     e2e_ms, e2e_wall_ms, _, clocks2, losses = timed(region_e2e)
     h2d = tr.train_loader.bytes_copied
     fused.check_status()
+    same_at_end = params_checksum_identical()
 
     tokens = stage.batch_size * K
     value = tokens / (dev_ms / 1e3)
     e2e_value = tokens / (max(e2e_ms, e2e_wall_ms) / 1e3)
     if env.master:
         out = {
-            "metric": ("train tokens/s, track-1 GPT, stage-2 batch (393216 tok/step)" if args.track == 1 else
+            "metric": (f"train tokens/s, track-1 GPT, stage-{args.stage} batch ({stage.batch_size} tok/step)" if args.track == 1 else
                        "train tokens/s, track-2 GPT, plateau batch (524288 tok/step)"), "value": value, "unit": "tokens/s",
             "n_gpus": env.world_size, "steps": K, "warmup": W, "ms_per_step": dev_ms / K, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": (value / BASELINE_TOKENS_PER_S) if BASELINE_TOKENS_PER_S else None,
-            "dtype": "bf16 (fp8 e4m3 MLP forward and lm_head)", "data": "synthetic Zipf(1.1) ids, EoS-delimited lognormal docs; random-init weights",
+            "dtype": ("bf16 (fp8 e4m3 MLP forward and lm_head)" if args.mlp == "fp8" else "bf16 (bf16 MLP; fp8 e4m3 lm_head)"), "data": "synthetic Zipf(1.1) ids, EoS-delimited lognormal docs; random-init weights",
             "impl": "ours",
             "config": {"model": ("track-1 GPT (11L, d768, 6x128 heads, vocab 50304)" if args.track == 1 else
                                  "track-2 GPT (16L, d1024, 8x128 heads, vocab 50304)"), "global_batch": stage.batch_size,
@@ -202,6 +214,7 @@ def main():
             "e2e": {"value": e2e_value, "unit": "tokens/s", "ms_per_step": max(e2e_ms, e2e_wall_ms) / K,
                     "h2d_bytes_per_step": h2d // K, "d2h_bytes_per_step": d2h // K, "last_loss": losses[-1]},
             "gpu_launches": launches,
+            "params_identical": (None if same_at_end is None else bool(same_after_warmup and same_at_end)),
             "clocks": clocks,
             "clocks_e2e": clocks2,
         }

@@ -1,12 +1,16 @@
 """Micro-benchmarks of the hand-written kernels, one case per invocation (CUDA-event timing after warm-up).
 
-    python bench_kernels.py --list
-    python bench_kernels.py --case gemm_bf16_o --rows 49152 --bn 256 --iters 10
+    python bench/bench_kernels.py --list
+    python bench/bench_kernels.py --case gemm_bf16_o --rows 49152 --bn 256 --iters 10
 
 Every case works on operands larger than the L2 cache at the default --rows.  The same command line
 (with a small --iters) is what the committed profiler summaries under profiles/ were captured from."""
 import argparse
 import json
+import os
+import sys
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 import torch
 

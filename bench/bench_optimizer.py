@@ -4,7 +4,7 @@ gradient shards and store the new weights to every peer) with the NCCL path (red
 all-gather around the same update kernels).
 
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port 29533 \
-        bench_optimizer.py --steps 20
+        bench/bench_optimizer.py --steps 20
 
 Mode `fused_sparse` gives the bigram table a gradient with 98,304 random touched rows and lets the fused Adam kernel pull
 only those from the peers; the other modes reduce that table densely.
@@ -15,7 +15,7 @@ import json
 import os
 import sys
 
-sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 
 def main():

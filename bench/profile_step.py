@@ -1,6 +1,6 @@
 """Per-kernel device-time table of the training step (torch.profiler, CUDA activities only).
 
-    python profile_step.py [--micro-steps 2] [--rows 60]
+    python bench/profile_step.py [--micro-steps 2] [--rows 60]
 
 Builds the track-1 trainer at its stage-2 configuration on synthetic data, warms up (including the CUDA-graph
 capture of the micro-step), then profiles `--micro-steps` micro-batches plus one optimizer step and prints the
@@ -10,7 +10,7 @@ import os
 import sys
 import time
 
-sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 
 def phases(tr, env, n_steps):

@@ -73,6 +73,9 @@ class GPT(nn.Module):
         self.world_size = world_size
         self.grad_scale = grad_scale
         self.use_fp8 = use_fp8
+        # The lm_head + loss path follows `use_fp8` unless set on its own: the reference's training loss quantises
+        # to FP8 even with DISABLE_FP8 (`train_gpt.py:1685-1687`), which `fp8_head = True` reproduces.
+        self.fp8_head = None
         self.eval_seq_len = eval_seq_len or cfg.max_seq_len
         L, H, Dh, D = cfg.num_layers, cfg.num_heads, cfg.head_dim, cfg.model_dim
         assert H * Dh == D, "num_heads * head_dim must equal model_dim"
@@ -258,6 +261,10 @@ class GPT(nn.Module):
 
     # ----------------------------------------------------------------------------------
     # FP8 MLP weight copies (row-scaled e4m3), refreshed after every optimizer step
+    @property
+    def head_fp8(self) -> bool:
+        return self.use_fp8 if self.fp8_head is None else bool(self.fp8_head)
+
     def quantize_mlp_fp8(self, bootstrap_down: bool = False):
         """Refresh the e4m3 copies of the MLP weights (`train_gpt.py:1403-1434`).  This build
         scales each weight row separately (one scale per 768- or 3072-element row, "1xK block
@@ -474,5 +481,5 @@ class GPT(nn.Module):
             prefix_targets = self.prefix_table[target_seq]
             return ops.softcap_ce(x, self.lm_head.weight, target_seq, schedule_cfg.mtp_weights, prefix_targets,
                                   schedule_cfg.prefix_weight, cfg.softcap_a, cfg.softcap_b, cfg.softcap_c,
-                                  grad_scale=self.grad_scale, fp8=self.use_fp8)
+                                  grad_scale=self.grad_scale, fp8=self.head_fp8)
         return ops.softcap_ce_eval(x, self.lm_head.weight, target_seq, cfg.softcap_a, cfg.softcap_b, cfg.softcap_c)

@@ -231,5 +231,5 @@ def forward_fused(m, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, big
     if m.training:
         prefix_targets = m.prefix_table[target_seq]
         return ops.softcap_ce(x, m.lm_head.weight, target_seq, sc.mtp_weights, prefix_targets, sc.prefix_weight,
-                              cfg.softcap_a, cfg.softcap_b, cfg.softcap_c, grad_scale=m.grad_scale, fp8=m.use_fp8)
+                              cfg.softcap_a, cfg.softcap_b, cfg.softcap_c, grad_scale=m.grad_scale, fp8=m.head_fp8)
     return ops.softcap_ce_eval(x, m.lm_head.weight, target_seq, cfg.softcap_a, cfg.softcap_b, cfg.softcap_c)
