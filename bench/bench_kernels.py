@@ -95,6 +95,48 @@ def build_case(name, T, bn, fused):
             x.grad = w.grad = None
             fused.softcap_ce(x, w, tg, mtp, pt, pw, 23.0, 5.0, 7.5, grad_scale=1.0, fp8=True).sum().backward()
         return run, 3 * 2 * T * D * V, T * V * 3
+    if name.startswith("proj_"):            # proj_{qkv|o}_{ours|lib}: bank-backed projection, forward + backward
+        _, which, impl = name.split("_")
+        N = 3 * D if which == "qkv" else D
+        x = r(T, D).to(BF).requires_grad_(True)
+        w = (r(N, D) * 0.03).to(BF)
+        lam = torch.tensor(0.5, device=dev, requires_grad=True)
+        gv = [torch.zeros(N, D, dtype=BF, device=dev)]
+        dy = r(T, N).to(BF)
+
+        def ours():
+            x.grad = lam.grad = None
+            fused.bank_linear(x, lam, w, gv).backward(dy)
+
+        def lib():                                                              # what ran before: library GEMMs + eager glue
+            x.grad = lam.grad = None
+            we = (lam.detach() * w)
+            y = x.detach() @ we.t()
+            dx = dy @ we
+            dw = dy.t() @ x.detach()
+            dlam = (dw.float() * w.float()).sum()
+            gv[0].addcmul_(dw, lam.detach())
+            return y, dx, dlam
+        return (ours if impl == "ours" else lib), 3 * 2 * T * D * N, T * (N + D) * 2
+    if name.startswith("gatemlp_"):         # gatemlp_{ours|lib}: (T,768) -> 64 -> 41 gate MLP, forward + backward
+        impl = name.split("_")[1]
+        import torch.nn.functional as F
+        x = r(T, D).to(BF).requires_grad_(True)
+        w1 = (r(64, D) * D ** -0.5).to(BF).requires_grad_(True)
+        w2 = (r(41, 64) * 0.1).to(BF).requires_grad_(True)
+        b2 = r(41).to(BF).requires_grad_(True)
+        sc = torch.tensor(0.1, device=dev, requires_grad=True)
+        dout = r(T, 41).to(BF)
+
+        def run():
+            for t in (x, w1, w2, b2, sc):
+                t.grad = None
+            if impl == "ours":
+                out = fused.gate_mlp(x, w1, w2, b2, sc)
+            else:
+                out = (F.linear(F.gelu(F.linear(x, w1)), w2) + b2) * sc.to(BF)
+            out.backward(dout)
+        return run, 3 * 2 * T * D * 64, T * D * 2
     if name.startswith("attn"):             # attn[bwd]_{ours|fa2}_{short|long|paired}: packed documents, sliding window
         op, impl, kind = name.split("_")
         Tq, Hh, window = (2 * T, 3, 2 * 640) if kind == "paired" else (T, 6, 640 if kind == "short" else 1408)
@@ -133,7 +175,7 @@ def build_case(name, T, bn, fused):
     raise SystemExit(f"unknown case {name}")
 
 
-CASES = ["gemm_bf16_up", "gemm_bf16_dpre", "gemm_bf16_down", "gemm_bf16_dw", "gemm_fp8_relu2", "gemm_fp8_down", "gemm_bf16_qkv",
+CASES = ["proj_qkv_ours", "proj_qkv_lib", "proj_o_ours", "proj_o_lib", "gatemlp_ours", "gatemlp_lib", "gemm_bf16_up", "gemm_bf16_dpre", "gemm_bf16_down", "gemm_bf16_dw", "gemm_fp8_relu2", "gemm_fp8_down", "gemm_bf16_qkv",
          "gemm_bf16_o", "gemm_bf16_o_null", "gemm_bf16_up_null", "gemm_fp8_logits", "gemm_fp8_logits_kk", "gemm_fp8_lmhead_dw_kmajor_a", "gemm_fp8_lmhead_dx", "gemm_fp8_lmhead_dw", "softcap_ce_e5m2", "softcap_ce_bf16", "lmhead_ce_fwdbwd",
          "attn_ours_short", "attn_fa2_short", "attn_ours_long", "attn_fa2_long", "attn_ours_paired", "attn_fa2_paired",
          "attnbwd_ours_short", "attnbwd_fa2_short", "attnbwd_ours_long", "attnbwd_fa2_long", "attnbwd_ours_paired", "attnbwd_fa2_paired"]

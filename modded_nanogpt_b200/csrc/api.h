@@ -59,6 +59,13 @@ int mng_transpose_u8(const void* src, void* dst, long long rows, long long cols,
 int mng_quant_transpose_e4m3(const void* src, void* q, float* scale, unsigned int* amax_scratch, long long rows,
                              long long cols, void* stream);
 
+// All FP8 copies of a [layers, 2, hid, dim] bf16 MLP bank in one call (five launches): fc8 [layers, hid, dim] with
+// fc_scale [layers, hid]; projT8 [layers, dim, hid] with projT_scale [layers, dim]; act_scale / amax_bits / used /
+// next: [layers].  amax_scratch: layers * dim words.
+int mng_mlp_weight_refresh(const void* bank, int layers, int hid, int dim, void* fc8, float* fc_scale, void* projT8,
+                           float* projT_scale, unsigned int* amax_scratch, float* act_scale, unsigned int* amax_bits,
+                           float* used_scales, float* next_scales, int bootstrap, void* stream);
+
 // ---- softcapped cross entropy (ce.cu) -------------------------------------------------------------
 // One CTA per token row: z = A*sigmoid((logit+B)/C), loss = sum_k w_k (lse - z[t_{i+k}]) + w_p (lse - z[p_i]),
 // dlogits (e5m2 or bf16) = grad_mul * d loss / d logit.
@@ -136,6 +143,24 @@ int mng_xsa_gate_fwd(const void* y, const void* v, const void* alpha, int alpha_
 int mng_xsa_gate_bwd(const void* y, const void* v, const void* alpha, int alpha_stride, const void* gate, int gate_stride,
                      const void* dout, void* dy, void* dv, void* dalpha, int dalpha_stride, void* dgate, int dgate_stride,
                      long long T, int H, void* stream);
+
+// ---- weight-side helpers (weights.cu) ------------------------------------------------------------------
+// dW = sum_s parts[s] (fp32 [S, n]); grad (bf16, slices g0 = elements [0, n0), g1 = the rest) += lam * dW;
+// *dlam = <dW, W>.  partials: MNG_BANK_GRAD_BLOCKS floats of scratch; counter: one word, zero before and after.
+#define MNG_BANK_GRAD_BLOCKS 592
+int mng_bank_grad_acc(const float* parts, int S, long long n, const void* W, const float* lam, void* g0, long long n0,
+                      void* g1, float* partials, unsigned int* counter, float* dlam, void* stream);
+
+// ---- gate / MUDD MLP tail (gatemlp.cu): out = (gelu(pre) W2^T + b2) * scale, pre [rows, 64], n <= 48 outputs --------
+// scale = *scale_ptr (rounded to bf16) when scale_ptr is given, else scale_const.
+#define MNG_GATE_TAIL_BLOCKS 296
+int mng_gate_tail_fwd(const void* pre, const void* W2, long long w2_ld, const void* b2, const float* scale_ptr,
+                      float scale_const, void* out, long long rows, int n, void* stream);
+// dpre [rows, 64] bf16; dW2 [n, 64] and db2 [n] bf16; *dscale fp32 (may be null).
+// partials: MNG_GATE_TAIL_BLOCKS * (n*64 + n + 1) floats of scratch.
+int mng_gate_tail_bwd(const void* pre, const void* W2, long long w2_ld, const void* b2, const float* scale_ptr,
+                      float scale_const, const void* dout, long long dout_ld, void* dpre, float* partials, void* dW2,
+                      long long dw2_ld, void* db2, float* dscale, long long rows, int n, void* stream);
 
 // ---- DC cross-head mixing (dc.cu) ---------------------------------------------------------------------
 int mng_dc_mix_fwd(const float* S, const void* w1, const int* doc_start, void* P, void* a, long long T, int H, int window,

@@ -188,6 +188,27 @@ void quant_transpose(const Tensor& src, Tensor& q, Tensor& scale, Tensor& scratc
   g_launches += 2;
 }
 
+void mlp_weight_refresh(const Tensor& bank, Tensor& fc8, Tensor& fc_scale, Tensor& projT8, Tensor& projT_scale, Tensor& scratch,
+                        Tensor& act_scale, Tensor& amax_bits, Tensor& used, Tensor& next, bool bootstrap) {
+  TORCH_CHECK(bank.is_cuda() && bank.dim() == 4 && bank.size(1) == 2 && bank.is_contiguous() && bank.scalar_type() == torch::kBFloat16);
+  const int64_t L = bank.size(0), hid = bank.size(2), dim = bank.size(3);
+  TORCH_CHECK(fc8.is_contiguous() && fc8.numel() == L * hid * dim && fc8.element_size() == 1);
+  TORCH_CHECK(projT8.is_contiguous() && projT8.numel() == L * hid * dim && projT8.element_size() == 1);
+  TORCH_CHECK(fc_scale.is_contiguous() && fc_scale.numel() == L * hid && fc_scale.scalar_type() == torch::kFloat32);
+  TORCH_CHECK(projT_scale.is_contiguous() && projT_scale.numel() == L * dim && projT_scale.scalar_type() == torch::kFloat32);
+  TORCH_CHECK(scratch.is_contiguous() && scratch.numel() >= L * dim && scratch.element_size() == 4);
+  TORCH_CHECK(act_scale.numel() == L && amax_bits.numel() == L && used.numel() >= L && next.numel() >= L);
+  TORCH_CHECK(act_scale.is_contiguous() && amax_bits.is_contiguous() && used.is_contiguous() && next.is_contiguous());
+  TORCH_CHECK(used.scalar_type() == torch::kFloat32 && next.scalar_type() == torch::kFloat32 && act_scale.scalar_type() == torch::kFloat32);
+  c10::cuda::CUDAGuard guard(bank.device());
+  check(mng_mlp_weight_refresh(bank.data_ptr(), (int)L, (int)hid, (int)dim, fc8.data_ptr(), fc_scale.data_ptr<float>(), projT8.data_ptr(),
+                               projT_scale.data_ptr<float>(), reinterpret_cast<unsigned int*>(scratch.data_ptr()),
+                               act_scale.data_ptr<float>(), reinterpret_cast<unsigned int*>(amax_bits.data_ptr()),
+                               used.data_ptr<float>(), next.data_ptr<float>(), bootstrap ? 1 : 0, cur_stream()),
+        "mng_mlp_weight_refresh");
+  g_launches += 4;
+}
+
 std::vector<Tensor> softcap_ce(const Tensor& logits, const Tensor& targets, const Tensor& mtp_weights,
                                const c10::optional<Tensor>& prefix_targets, const c10::optional<Tensor>& prefix_weight,
                                bool dlogits_e5m2, double A, double B, double C, double grad_mul) {
@@ -572,6 +593,72 @@ std::vector<Tensor> attn_bwd(const Tensor& dout, const Tensor& q, const Tensor& 
   return {dq, dk, dv};
 }
 
+// Folds the split-K partial products of a bank-backed linear layer's weight gradient: grad slices += lam * dW,
+// returns dlam = <dW, W> as a 0-dim fp32 tensor.
+Tensor g_bank_counter;   // one zero word per device, left at zero by every launch
+Tensor bank_grad_acc(const Tensor& parts, const Tensor& W, const Tensor& lam, Tensor& g0, const c10::optional<Tensor>& g1) {
+  TORCH_CHECK(parts.is_cuda() && parts.scalar_type() == torch::kFloat32 && parts.is_contiguous() && parts.dim() == 3);
+  TORCH_CHECK(W.scalar_type() == torch::kBFloat16 && W.is_contiguous() && W.numel() == parts.size(1) * parts.size(2));
+  TORCH_CHECK(lam.scalar_type() == torch::kFloat32 && lam.numel() == 1 && lam.is_cuda());
+  TORCH_CHECK(g0.scalar_type() == torch::kBFloat16 && g0.is_contiguous());
+  c10::cuda::CUDAGuard guard(parts.device());
+  const int64_t n = W.numel(), n0 = g0.numel();
+  void* p1 = nullptr;
+  if (g1.has_value() && g1->defined()) {
+    TORCH_CHECK(g1->scalar_type() == torch::kBFloat16 && g1->is_contiguous() && n0 + g1->numel() == n);
+    p1 = g1->data_ptr();
+  } else {
+    TORCH_CHECK(n0 == n, "gradient slices do not cover the weight");
+  }
+  if (!g_bank_counter.defined() || g_bank_counter.device() != parts.device())
+    g_bank_counter = torch::zeros({1}, torch::dtype(torch::kInt32).device(parts.device()));
+  Tensor partials = torch::empty({MNG_BANK_GRAD_BLOCKS}, parts.options());
+  Tensor dlam = torch::empty({}, parts.options());
+  check(mng_bank_grad_acc(parts.data_ptr<float>(), (int)parts.size(0), n, W.data_ptr(), lam.data_ptr<float>(), g0.data_ptr(), n0,
+                          p1, partials.data_ptr<float>(), reinterpret_cast<unsigned int*>(g_bank_counter.data_ptr<int32_t>()),
+                          dlam.data_ptr<float>(), cur_stream()),
+        "mng_bank_grad_acc");
+  g_launches += 1;
+  return dlam;
+}
+
+// Tail of the gate / MUDD MLPs (gatemlp.cu): out = (gelu(pre) W2^T + b2) * scale.
+Tensor gate_tail_fwd(const Tensor& pre, const Tensor& W2, const Tensor& b2, const c10::optional<Tensor>& scale_t, double scale_c) {
+  TORCH_CHECK(pre.is_cuda() && pre.scalar_type() == torch::kBFloat16 && pre.is_contiguous() && pre.dim() == 2 && pre.size(1) == 64);
+  TORCH_CHECK(W2.scalar_type() == torch::kBFloat16 && W2.dim() == 2 && W2.size(1) == 64 && W2.stride(1) == 1 && W2.size(0) <= 48);
+  TORCH_CHECK(b2.scalar_type() == torch::kBFloat16 && b2.is_contiguous() && b2.numel() == W2.size(0));
+  c10::cuda::CUDAGuard guard(pre.device());
+  const int n = (int)W2.size(0);
+  Tensor out = torch::empty({pre.size(0), n}, pre.options());
+  check(mng_gate_tail_fwd(pre.data_ptr(), W2.data_ptr(), W2.stride(0), b2.data_ptr(), fptr(scale_t), (float)scale_c, out.data_ptr(),
+                          pre.size(0), n, cur_stream()),
+        "mng_gate_tail_fwd");
+  g_launches += 1;
+  return out;
+}
+
+std::vector<Tensor> gate_tail_bwd(const Tensor& pre, const Tensor& W2, const Tensor& b2, const c10::optional<Tensor>& scale_t,
+                                  double scale_c, const Tensor& dout) {
+  TORCH_CHECK(pre.is_cuda() && pre.scalar_type() == torch::kBFloat16 && pre.is_contiguous() && pre.dim() == 2 && pre.size(1) == 64);
+  TORCH_CHECK(W2.scalar_type() == torch::kBFloat16 && W2.dim() == 2 && W2.size(1) == 64 && W2.stride(1) == 1 && W2.size(0) <= 48);
+  TORCH_CHECK(b2.scalar_type() == torch::kBFloat16 && b2.is_contiguous() && b2.numel() == W2.size(0));
+  const int n = (int)W2.size(0);
+  TORCH_CHECK(dout.scalar_type() == torch::kBFloat16 && dout.dim() == 2 && dout.size(0) == pre.size(0) && dout.size(1) == n &&
+              dout.stride(1) == 1);
+  c10::cuda::CUDAGuard guard(pre.device());
+  Tensor dpre = torch::empty_like(pre);
+  Tensor dW2 = torch::empty({n, 64}, pre.options());
+  Tensor db2 = torch::empty({n}, pre.options());
+  Tensor dscale = torch::empty({}, pre.options().dtype(torch::kFloat32));
+  Tensor partials = torch::empty({(int64_t)MNG_GATE_TAIL_BLOCKS * (n * 64 + n + 1)}, pre.options().dtype(torch::kFloat32));
+  check(mng_gate_tail_bwd(pre.data_ptr(), W2.data_ptr(), W2.stride(0), b2.data_ptr(), fptr(scale_t), (float)scale_c, dout.data_ptr(),
+                          dout.stride(0), dpre.data_ptr(), partials.data_ptr<float>(), dW2.data_ptr(), 64, db2.data_ptr(),
+                          dscale.data_ptr<float>(), pre.size(0), n, cur_stream()),
+        "mng_gate_tail_bwd");
+  g_launches += 2;
+  return {dpre, dW2, db2, dscale};
+}
+
 Tensor status_tensor(const Tensor& like) {
   status_ptr(like);
   return g_status;
@@ -606,6 +693,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dc_fold", &dc_fold);
   m.def("attn_fwd", &attn_fwd);
   m.def("attn_bwd", &attn_bwd);
+  m.def("mlp_weight_refresh", &mlp_weight_refresh);
+  m.def("bank_grad_acc", &bank_grad_acc);
+  m.def("gate_tail_fwd", &gate_tail_fwd);
+  m.def("gate_tail_bwd", &gate_tail_bwd);
   m.def("status_tensor", &status_tensor);
   m.def("launch_count", &launch_count);
 }

@@ -124,10 +124,14 @@ rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __r
 
 template <int MAXV>
 __global__ void __launch_bounds__(ROW_WARPS * 32)
-quant_rows_kernel(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ q, float* __restrict__ scale, long long rows, int cols) {
+quant_rows_kernel(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ q, float* __restrict__ scale, long long rows, int cols,
+                  long long group_rows, long long group_stride) {
+  // source row r lives at x + (r / group_rows) * group_stride + (r % group_rows) * cols: lets one launch walk the
+  // [hid, dim] matrices of a [layers, 2, hid, dim] parameter bank; outputs are dense
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
   if (row >= rows) return;
+  x += (row / group_rows) * group_stride + (row % group_rows) * cols - row * cols;
   const int nv = cols >> 8;
   float v[MAXV][8];
   float amax = 0.f;
@@ -182,7 +186,10 @@ transpose_bf16_kernel(const __nv_bfloat16* __restrict__ src, __nv_bfloat16* __re
 
 // Column amax of a [rows, cols] bf16 matrix (atomic max on float bits), then quantise the transpose.
 __global__ void __launch_bounds__(256)
-col_amax_kernel(const __nv_bfloat16* __restrict__ src, unsigned int* __restrict__ amax_bits, long long rows, long long cols) {
+col_amax_kernel(const __nv_bfloat16* __restrict__ src, unsigned int* __restrict__ amax_bits, long long rows, long long cols,
+                long long src_bstride = 0) {
+  src += blockIdx.z * src_bstride;                     // gridDim.z matrices, one amax row of `cols` words each
+  amax_bits += blockIdx.z * cols;
   // Block = 256 columns x 64 rows; a warp reads one row segment of 256 columns with 16-byte loads, the eight
   // warps' maxima are combined in shared memory, one atomic per column and block.  Ragged column edges (cols
   // not a multiple of 8) take the scalar path.
@@ -220,7 +227,11 @@ col_amax_kernel(const __nv_bfloat16* __restrict__ src, unsigned int* __restrict_
 
 __global__ void __launch_bounds__(256)
 quant_transpose_kernel(const __nv_bfloat16* __restrict__ src, uint8_t* __restrict__ q, const unsigned int* __restrict__ amax_bits,
-                       float* __restrict__ scale, long long rows, long long cols) {
+                       float* __restrict__ scale, long long rows, long long cols, long long src_bstride = 0) {
+  src += blockIdx.z * src_bstride;
+  q += blockIdx.z * rows * cols;
+  amax_bits += blockIdx.z * cols;
+  scale += blockIdx.z * cols;
   __shared__ float tile[64][65];
   const long long r0 = (long long)blockIdx.y * 64, c0 = (long long)blockIdx.x * 64;
   const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;
@@ -281,7 +292,7 @@ extern "C" int mng_rmsnorm_bwd_add(const void* x, const void* dy, const float* r
 
 extern "C" int mng_quant_rows_e4m3(const void* x, void* q, float* scale, long long rows, int cols, void* stream) {
   if (rows == 0) return 0;
-  DISPATCH_COLS(quant_rows_kernel, (const __nv_bfloat16*)x, (uint8_t*)q, scale, rows, cols);
+  DISPATCH_COLS(quant_rows_kernel, (const __nv_bfloat16*)x, (uint8_t*)q, scale, rows, cols, rows, 0LL);
 }
 
 // dst[c, r] = src[r, c] for 1-byte elements; rows and cols multiples of 64.  64 x 64 tiles through shared memory,
@@ -321,6 +332,61 @@ extern "C" int mng_quant_transpose_e4m3(const void* src, void* q, float* scale, 
   col_amax_kernel<<<g1, 256, 0, s>>>((const __nv_bfloat16*)src, amax_scratch, rows, cols);
   dim3 g2((unsigned)((cols + 63) / 64), (unsigned)((rows + 63) / 64));
   quant_transpose_kernel<<<g2, 256, 0, s>>>((const __nv_bfloat16*)src, (uint8_t*)q, amax_scratch, scale, rows, cols);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+// Refresh of the FP8 copies of a [layers, 2, hid, dim] MLP parameter bank in five launches for all layers:
+// row-scaled e4m3 of the up projections, column-amax + transposing quantiser of the down projections, and the
+// per-layer scale bookkeeping (delayed activation scales from the amax seen since the last refresh,
+// `train_gpt.py:1670-1675`; per-layer maxima of the down-projection scales for the state_dict buffers).
+namespace mng {
+__global__ void mlp_scales_kernel(const float* __restrict__ projT_scale, float* __restrict__ act_scale, unsigned int* __restrict__ amax_bits,
+                                  float* __restrict__ used, float* __restrict__ next, int dim, int bootstrap) {
+  const int l = blockIdx.x;
+  float m = 0.f;
+  for (int c = threadIdx.x; c < dim; c += blockDim.x) m = fmaxf(m, projT_scale[(long long)l * dim + c]);
+  __shared__ float red[8];
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, red[w]);
+    used[l] = bootstrap ? m : next[l];
+    next[l] = m * 1.12f;
+    const float seen = __uint_as_float(amax_bits[l]);
+    if (seen > 0.f) act_scale[l] = fmaxf(seen, 1e-12f) * (1.80f / 448.0f);
+    amax_bits[l] = 0u;
+  }
+}
+}  // namespace mng
+
+extern "C" int mng_mlp_weight_refresh(const void* bank, int layers, int hid, int dim, void* fc8, float* fc_scale, void* projT8,
+                                      float* projT_scale, unsigned int* amax_scratch, float* act_scale, unsigned int* amax_bits,
+                                      float* used_scales, float* next_scales, int bootstrap, void* stream) {
+  if (layers <= 0 || hid <= 0 || dim <= 0 || layers > 65535) return -1;
+  cudaStream_t s = (cudaStream_t)stream;
+  const __nv_bfloat16* w = (const __nv_bfloat16*)bank;
+  const long long lstride = 2LL * hid * dim;
+  {
+    const long long rows = (long long)layers * hid;
+    const int cols = dim;
+    if (cols % 256 != 0 || cols > 4096) return -1;
+    const unsigned grid = (unsigned)((rows + ROW_WARPS - 1) / ROW_WARPS);
+    const __nv_bfloat16* x = w;
+    uint8_t* q = (uint8_t*)fc8;
+    if (cols <= 256) quant_rows_kernel<1><<<grid, ROW_WARPS * 32, 0, s>>>(x, q, fc_scale, rows, cols, (long long)hid, lstride);
+    else if (cols <= 768) quant_rows_kernel<3><<<grid, ROW_WARPS * 32, 0, s>>>(x, q, fc_scale, rows, cols, (long long)hid, lstride);
+    else if (cols <= 1024) quant_rows_kernel<4><<<grid, ROW_WARPS * 32, 0, s>>>(x, q, fc_scale, rows, cols, (long long)hid, lstride);
+    else if (cols <= 3072) quant_rows_kernel<12><<<grid, ROW_WARPS * 32, 0, s>>>(x, q, fc_scale, rows, cols, (long long)hid, lstride);
+    else quant_rows_kernel<16><<<grid, ROW_WARPS * 32, 0, s>>>(x, q, fc_scale, rows, cols, (long long)hid, lstride);
+  }
+  if (cudaMemsetAsync(amax_scratch, 0, sizeof(unsigned int) * (size_t)layers * dim, s) != cudaSuccess) return -3;
+  const __nv_bfloat16* proj = w + (long long)hid * dim;                 // [l, 1] = down projection [hid, dim]
+  dim3 g1((unsigned)((dim + 255) / 256), (unsigned)((hid + 63) / 64), (unsigned)layers);
+  col_amax_kernel<<<g1, 256, 0, s>>>(proj, amax_scratch, hid, dim, lstride);
+  dim3 g2((unsigned)((dim + 63) / 64), (unsigned)((hid + 63) / 64), (unsigned)layers);
+  quant_transpose_kernel<<<g2, 256, 0, s>>>(proj, (uint8_t*)projT8, amax_scratch, projT_scale, hid, dim, lstride);
+  mlp_scales_kernel<<<layers, 256, 0, s>>>(projT_scale, act_scale, amax_bits, used_scales, next_scales, dim, bootstrap);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 

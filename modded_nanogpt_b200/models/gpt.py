@@ -259,6 +259,20 @@ class GPT(nn.Module):
         vo = self.vo_bank[:A * 2].view(A, 2 * D, D)
         return qk, vo
 
+    def qkv_weights(self) -> Tensor:
+        """[A, 3*D, D]: the QKV projection weight of every attention layer as one contiguous matrix, copied out of
+        `qk_bank` and `vo_bank` into a persistent buffer (two strided copies per call, 35 MB at track-1 size), so
+        that the projection and its input gradient are one GEMM each."""
+        A, D = self._num_attn_layers, self.model_dim
+        qk, vo = self.attn_layer_weights()
+        buf = getattr(self, "_qkv_cat", None)
+        if buf is None or buf.device != qk.device or buf.dtype != qk.dtype:
+            buf = self._qkv_cat = torch.empty(A, 3 * D, D, dtype=qk.dtype, device=qk.device)
+        with torch.no_grad():
+            buf[:, :2 * D].copy_(qk)
+            buf[:, 2 * D:].copy_(vo[:, :D])
+        return buf
+
     # ----------------------------------------------------------------------------------
     # FP8 MLP weight copies (row-scaled e4m3), refreshed after every optimizer step
     @property
@@ -304,13 +318,23 @@ class GPT(nn.Module):
     # ----------------------------------------------------------------------------------
     def _gate_mlp(self, x: Tensor, gid: int) -> Tensor:
         n = self.gate_layouts[gid]["n"]
-        h = F.gelu(F.linear(x, self.mudd_gate_w1[gid].type_as(x)))
-        out = F.linear(h, self.mudd_gate_w2[gid, :n].type_as(x)) + self.mudd_gate_b2[gid, :n].type_as(x)
+        w1, w2, b2 = self.mudd_gate_w1[gid], self.mudd_gate_w2[gid, :n], self.mudd_gate_b2[gid, :n]
+        if ops.use_kernel("gate_mlp", x):
+            from ..ops import fused
+            if fused.gate_mlp_supported(x, w1, w2):
+                return fused.gate_mlp(x, w1, w2, b2, self._mudd_gate_scale)
+        h = F.gelu(F.linear(x, w1.type_as(x)))
+        out = F.linear(h, w2.type_as(x)) + b2.type_as(x)
         return out * self._mudd_gate_scale.type_as(x)
 
     def _mudd_raw(self, x: Tensor, mid: int, n: int) -> Tensor:
-        h = F.gelu(F.linear(x, self.mudd_w1[mid].type_as(x)))
-        return (F.linear(h, self.mudd_w2[mid, :n].type_as(x)) + self.mudd_b2[mid, :n].type_as(x)) * self._mudd_scale
+        w1, w2, b2 = self.mudd_w1[mid], self.mudd_w2[mid, :n], self.mudd_b2[mid, :n]
+        if ops.use_kernel("gate_mlp", x):
+            from ..ops import fused
+            if fused.gate_mlp_supported(x, w1, w2):
+                return fused.gate_mlp(x, w1, w2, b2, self._mudd_scale)
+        h = F.gelu(F.linear(x, w1.type_as(x)))
+        return (F.linear(h, w2.type_as(x)) + b2.type_as(x)) * self._mudd_scale
 
     def _mudd(self, x: Tensor, mid: int, n: int):
         return self._mudd_raw(x, mid, n).split(1, dim=-1)

@@ -58,6 +58,9 @@ def forward_fused(m, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, big
         qk_g = m.qk_bank.grad[:m._num_qk_groups].view(A, 2 * D, D)
         vo_g = m.vo_bank.grad[:2 * A].view(A, 2 * D, D)
 
+    # [Wq; Wk; Wv] of every attention layer as one contiguous matrix (Q, K live in qk_bank, V in vo_bank)
+    qkv_w = m.qkv_weights() if (direct or not torch.is_grad_enabled()) else None
+
     ids = input_seq.long()
     gather = (lambda i, w: embed_direct(i, w, w.grad)) if direct else F.embedding
     x = gather(ids, m.embed.weight)
@@ -163,7 +166,9 @@ def forward_fused(m, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, big
                     gate_in = torch.cat([attn_in[:, :6], ve_t[:, :6]], dim=-1)
                 vgate = (2 * torch.sigmoid(F.linear(gate_in, m.ve_gate_bank[pl.ve_slot]))).contiguous()
             if direct:
-                qkv = fused.bank_linear(attn_in, sa_lambdas[i, 0], [qk_all[sl], vo_all[sl][:D]], [qk_g[sl], vo_g[sl][:D]])
+                qkv = fused.bank_linear(attn_in, sa_lambdas[i, 0], qkv_w[sl], [qk_g[sl], vo_g[sl][:D]])
+            elif not torch.is_grad_enabled():
+                qkv = fused.linear_scaled(attn_in, qkv_w[sl], sa_lambdas[i, 0])
             else:
                 qkv = F.linear(attn_in, sa_lambdas[i, 0] * torch.cat([qk_all[sl], vo_all[sl][:D]], dim=0))
             yarn = m.yarn_paired_head if pl.paired else m.yarn
@@ -193,7 +198,9 @@ def forward_fused(m, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, big
                 else:
                     y = xsa_gate(y, v, gt[:, ca:ca + H] if ca is not None else None, gt[:, cg:cg + H] if cg is not None else None)
             if direct:
-                attn_out = fused.bank_linear(y.reshape(T, D), sa_lambdas[i, 1], [vo_all[sl][D:]], [vo_g[sl][D:]])
+                attn_out = fused.bank_linear(y.reshape(T, D), sa_lambdas[i, 1], vo_all[sl][D:], [vo_g[sl][D:]])
+            elif not torch.is_grad_enabled():
+                attn_out = fused.linear_scaled(y.reshape(T, D), vo_all[sl][D:], sa_lambdas[i, 1])
             else:
                 attn_out = F.linear(y.reshape(T, D), sa_lambdas[i, 1] * vo_all[sl][D:])
             if mu is not None:

@@ -279,7 +279,9 @@ class GPTMedium(nn.Module):
                 xin, x16 = cols_tap(xin, 16)                 # gate inputs: their gradient joins the main one in place
             is_long = i in LONG_LAYERS
             if direct:
-                qkv = fused.bank_linear(xin, sa[i, 0], [w_all[i][:3 * D]], [g_all[i][:3 * D]])
+                qkv = fused.bank_linear(xin, sa[i, 0], w_all[i][:3 * D], [g_all[i][:3 * D]])
+            elif not torch.is_grad_enabled():
+                qkv = fused.linear_scaled(xin, w_all[i][:3 * D], sa[i, 0])
             else:
                 qkv = F.linear(xin, sa[i, 0] * w_all[i][:3 * D])
             ve_t = vgate = None
@@ -292,7 +294,9 @@ class GPTMedium(nn.Module):
             agate = torch.sigmoid(F.linear(x16, self.attn_gate_bank[i])).contiguous()
             y = xsa_gate(y, v, None, agate)
             if direct:
-                attn_out = fused.bank_linear(y.reshape(T, D), sa[i, 1], [w_all[i][3 * D:]], [g_all[i][3 * D:]])
+                attn_out = fused.bank_linear(y.reshape(T, D), sa[i, 1], w_all[i][3 * D:], [g_all[i][3 * D:]])
+            elif not torch.is_grad_enabled():
+                attn_out = fused.linear_scaled(y.reshape(T, D), w_all[i][3 * D:], sa[i, 1])
             else:
                 attn_out = F.linear(y.reshape(T, D), sa[i, 1] * w_all[i][3 * D:])
             x = lincomb([Term(x), Term(attn_out)])

@@ -144,7 +144,7 @@ class MlpFp8State:
         self.projT_scale = torch.empty(Lp, dim, dtype=torch.float32, device=dev)
         self.act_scale = torch.ones(Lp, dtype=torch.float32, device=dev)
         self.amax_bits = torch.zeros(Lp, dtype=torch.int32, device=dev)
-        self._scratch = torch.empty(max(hid, dim), dtype=torch.int32, device=dev)
+        self._scratch = torch.empty(Lp * max(hid, dim), dtype=torch.int32, device=dev)
 
     def layer(self, i: int):
         return (self.fc8[i], self.fc_scale[i], self.projT8[i], self.projT_scale[i], self.act_scale[i:i + 1],
@@ -154,26 +154,13 @@ class MlpFp8State:
 @torch.no_grad()
 def quantize_mlp_weights(bank: Tensor, state: MlpFp8State | None, used_scales: Tensor, next_scales: Tensor,
                          bootstrap: bool) -> MlpFp8State:
-    C = _C()
     if state is None:
         state = MlpFp8State(bank)
-    Lp, _, hid, dim = bank.shape
-    for l in range(Lp):
-        q, s = C.quant_rows(bank[l, 0])
-        state.fc8[l].copy_(q)
-        state.fc_scale[l].copy_(s)
-        C.quant_transpose(bank[l, 1], state.projT8[l], state.projT_scale[l], state._scratch)
-    # delayed activation scales: amax seen since the last refresh, with headroom (`train_gpt.py:1670-1675`)
-    amax = state.amax_bits.view(torch.float32)
-    seen = amax > 0
-    new = amax.clamp_min(1e-12) * (1.80 / 448.0)
-    state.act_scale.copy_(torch.where(seen, new, state.act_scale))
-    state.amax_bits.zero_()
-    # per-layer maxima of the down-projection scales keep the reference's state_dict buffers meaningful
-    used_scales.copy_(next_scales)
-    next_scales.copy_(state.projT_scale.amax(dim=1) * 1.12)
-    if bootstrap:
-        used_scales.copy_(state.projT_scale.amax(dim=1))
+    # one call for all layers: row-scaled e4m3 of the up projections, column-scaled transposed e4m3 of the down
+    # projections, delayed activation scales from the amax seen since the last refresh (`train_gpt.py:1670-1675`)
+    # and the per-layer maxima of the down-projection scales that keep the reference's state_dict buffers meaningful
+    _C().mlp_weight_refresh(bank, state.fc8, state.fc_scale, state.projT8, state.projT_scale, state._scratch,
+                            state.act_scale, state.amax_bits, used_scales, next_scales, bool(bootstrap))
     return state
 
 
@@ -234,35 +221,111 @@ def norm_relu2_mlp(x: Tensor, w_fc: Tensor, w_proj: Tensor, fp8_state=None, grad
     return _NormRelu2Mlp.apply(x, w_fc, w_proj, fp8_state, None, None, fork)
 
 
+def _split_k(rows: int, tiles: int) -> int:
+    """Number of token-dimension splits (1, 2, 4 or 8) for a weight-gradient GEMM with `tiles` 128 x 128 output
+    tiles: the fewest splits whose cost - waves over the SMs, each 1/s long - is within 5 % of the best."""
+    cost = {s: -(-tiles * s // NUM_SMS) / s for s in (1, 2, 4, 8) if rows % (s * 64) == 0}
+    if not cost:
+        return 1
+    best = min(cost.values())
+    return min(s for s, c in cost.items() if c <= 1.05 * best)
+
+
 class _BankLinear(torch.autograd.Function):
-    """y = x @ (lam * W)^T for a weight W assembled from parameter-bank slices.  The backward adds
-    lam * dy^T x into the given slices of the bank gradients and returns d lam = <dy^T x, W>."""
+    """y = x @ (lam * W)^T on the tcgen05 GEMM, for a weight W [N, K] whose rows belong to one or two slices of
+    parameter banks (`train_gpt.py:1103`, `:1161`: the QKV and O projections).  lam is a device scalar applied in the
+    GEMM epilogue, so no scaled copy of W is made.  Backward: dx = lam * dy W; the weight-gradient product dy^T x
+    runs split along the tokens (a batched GEMM with fp32 outputs) and `bank_grad_acc` folds the splits, adds
+    lam * dy^T x into the bank-gradient slices and returns d lam = <dy^T x, W>."""
 
     @staticmethod
     def forward(ctx, x, lam, w, *grad_views):
-        w_eff = (lam * w).contiguous()
-        ctx.save_for_backward(x, lam, w, w_eff)
+        x2 = x.reshape(-1, x.shape[-1])
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        lam32 = lam.detach().reshape(()).float() if lam.dtype != torch.float32 else lam.detach().reshape(())
+        ctx.save_for_backward(x2, lam32, w)
         ctx.grad_views = grad_views
-        return x @ w_eff.t()
+        ctx.lam_meta = (lam.dtype, lam.shape)
+        y = gemm(x2, w, alpha_t=lam32)
+        return y.view(*x.shape[:-1], w.shape[0])
 
     @staticmethod
     def backward(ctx, dy):
-        x, lam, w, w_eff = ctx.saved_tensors
-        dy = dy.reshape(-1, dy.shape[-1])
-        dx = dy @ w_eff
-        dw = dy.t() @ x.reshape(-1, x.shape[-1])                              # unscaled: (N, K)
-        dlam = (dw.float() * w.float()).sum().to(lam.dtype).reshape(lam.shape)
-        r = 0
-        for gv in ctx.grad_views:
-            n = gv.shape[0]
-            gv.addcmul_(dw[r:r + n], lam)
-            r += n
-        return (dx.view(x.shape), dlam, None) + (None,) * len(ctx.grad_views)
+        x2, lam32, w = ctx.saved_tensors
+        N, K = w.shape
+        dy2 = dy.reshape(-1, N)
+        if not dy2.is_contiguous():
+            dy2 = dy2.contiguous()
+        T = dy2.shape[0]
+        dx = gemm(dy2, w, b_mn=True, alpha_t=lam32)                           # [T, N] x [N, K]
+        S = _split_k(T, -(-N // 128) * -(-K // 128))
+        parts = torch.empty(S, N, K, dtype=torch.float32, device=dy.device)
+        gemm(dy2.view(S, T // S, N), x2.view(S, T // S, K), a_mn=True, b_mn=True, out=parts, bn=128)
+        gv = ctx.grad_views
+        dlam = _C().bank_grad_acc(parts, w, lam32, gv[0], gv[1] if len(gv) > 1 else None)
+        dtype, shape = ctx.lam_meta
+        return (dx.view(*dy.shape[:-1], K), dlam.to(dtype).reshape(shape), None) + (None,) * len(gv)
 
 
-def bank_linear(x: Tensor, lam: Tensor, w_parts: list, grad_views: list) -> Tensor:
-    w = torch.cat([p.detach() for p in w_parts], dim=0) if len(w_parts) > 1 else w_parts[0].detach()
-    return _BankLinear.apply(x, lam, w, *grad_views)
+def bank_linear(x: Tensor, lam: Tensor, w: Tensor, grad_views: list) -> Tensor:
+    """`w`: contiguous [N, K] bf16 weight (no autograd); `grad_views`: one or two contiguous bf16 gradient slices
+    that together cover w's rows in order."""
+    assert len(grad_views) in (1, 2) and w.is_contiguous()
+    return _BankLinear.apply(x, lam, w.detach(), *grad_views)
+
+
+def linear_scaled(x: Tensor, w: Tensor, lam: Tensor | None = None) -> Tensor:
+    """Inference-side x @ (lam * w)^T on the same GEMM (no autograd)."""
+    x2 = x.reshape(-1, x.shape[-1]).contiguous()
+    y = gemm(x2, w.contiguous(), alpha_t=None if lam is None else lam.detach().reshape(()).float())
+    return y.view(*x.shape[:-1], w.shape[0])
+
+
+class _GateMlp(torch.autograd.Function):
+    """out = (gelu(x W1^T) W2^T + b2) * scale for the 64-wide gate / MUDD MLPs (`train_gpt.py:1465-1467`,
+    `:1601-1610`, `:1677-1680`).  x W1^T and the two products of its backward run on the tcgen05 GEMM (the weight
+    gradient split along the tokens); the 64 -> n tail is one kernel per direction (csrc/gatemlp.cu)."""
+
+    @staticmethod
+    def forward(ctx, x, w1, w2, b2, scale_t, scale_c):
+        x2 = x.reshape(-1, x.shape[-1]).contiguous()
+        w1c, w2c, b2c = w1.contiguous(), w2.contiguous(), b2.contiguous()
+        st = None if scale_t is None else scale_t.detach().reshape(()).float()
+        pre = gemm(x2, w1c, bn=128)                                              # [T, 64]
+        out = _C().gate_tail_fwd(pre, w2c, b2c, st, scale_c)
+        ctx.save_for_backward(x2, pre, w1c, w2c, b2c, st)
+        ctx.cfg = (scale_c, x.shape, None if scale_t is None else (scale_t.dtype, scale_t.shape))
+        return out.view(*x.shape[:-1], w2.shape[0])
+
+    @staticmethod
+    def backward(ctx, dout):
+        x2, pre, w1, w2, b2, st = ctx.saved_tensors
+        scale_c, xshape, smeta = ctx.cfg
+        T, K = x2.shape
+        d2 = dout.reshape(T, -1)
+        if d2.stride(1) != 1:
+            d2 = d2.contiguous()
+        dpre, dw2, db2, dscale = _C().gate_tail_bwd(pre, w2, b2, st, scale_c, d2)
+        dx = gemm(dpre, w1, b_mn=True) if ctx.needs_input_grad[0] else None          # [T, 64] x [64, K]
+        S = max(s for s in (1, 2, 4, 8, 16, 32) if T % (s * 64) == 0)
+        parts = torch.empty(S, 64, K, dtype=torch.float32, device=x2.device)
+        gemm(dpre.view(S, T // S, 64), x2.view(S, T // S, K), a_mn=True, b_mn=True, out=parts, bn=128)
+        dw1 = parts.sum(0).to(w1.dtype)
+        ds = None if smeta is None else dscale.to(smeta[0]).reshape(smeta[1])
+        return (None if dx is None else dx.view(xshape)), dw1, dw2, db2, ds, None
+
+
+def gate_mlp(x: Tensor, w1: Tensor, w2: Tensor, b2: Tensor, scale) -> Tensor:
+    """`scale`: a Python number or a one-element fp32 tensor (then it receives a gradient)."""
+    if isinstance(scale, Tensor):
+        return _GateMlp.apply(x, w1, w2, b2, scale, 1.0)
+    return _GateMlp.apply(x, w1, w2, b2, None, float(scale))
+
+
+def gate_mlp_supported(x: Tensor, w1: Tensor, w2: Tensor) -> bool:
+    return (x.is_cuda and x.dtype == torch.bfloat16 and w1.dtype == torch.bfloat16 and w1.shape[0] == 64
+            and w2.shape[0] <= 48 and x.shape[-1] % 64 == 0 and x.numel() // x.shape[-1] >= 128)
 
 
 def relu2_mlp(x_normed: Tensor, w_fc: Tensor, w_proj: Tensor, fp8_state=None) -> Tensor:

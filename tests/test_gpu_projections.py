@@ -1,0 +1,115 @@
+"""Bank-backed projections, gate / MUDD MLPs and the batched FP8 weight refresh against plain PyTorch fp32
+restatements of the same ops."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+BF = torch.bfloat16
+
+
+@pytest.fixture(scope="module")
+def fused():
+    from modded_nanogpt_b200.ops import fused, native
+    assert native.available(required=True)
+    return fused
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
+
+
+@pytest.mark.parametrize("T,N,K,two_views", [(4096, 2304, 768, True), (2048, 768, 768, False), (49152, 2304, 768, True),
+                                             (1000, 512, 256, False)])
+def test_bank_linear_forward_backward(fused, T, N, K, two_views):
+    """y = x (lam W)^T; dx = lam dy W; grad slices += lam dy^T x; dlam = <dy^T x, W>."""
+    torch.manual_seed(0)
+    x = torch.randn(T, K, device="cuda").to(BF).requires_grad_(True)
+    w = (torch.randn(N, K, device="cuda") * 0.05).to(BF)
+    lam = torch.tensor(0.7, device="cuda", requires_grad=True)
+    n0 = (2 * N // 3) if two_views else N
+    g_init = torch.randn(N, K, device="cuda").to(BF)
+    views = [g_init[:n0].clone(), g_init[n0:].clone()] if two_views else [g_init.clone()]
+    y = fused.bank_linear(x, lam, w, views)
+    dy = (torch.randn(T, N, device="cuda") * 0.1).to(BF)
+    y.backward(dy)
+    xf, wf, dyf = x.detach().float(), w.float(), dy.float()
+    assert _rel(y, 0.7 * xf @ wf.T) < 6e-3
+    assert _rel(x.grad, 0.7 * dyf @ wf) < 6e-3
+    dw = dyf.T @ xf
+    got = torch.cat([v.float() for v in views])
+    assert _rel(got - g_init.float(), 0.7 * dw) < 1e-2          # bf16 accumulation into a bf16 gradient
+    # a sum of N*K signed terms: compare on the scale of the terms' norm
+    assert abs(lam.grad.item() - (dw * wf).sum().item()) <= 1e-3 * (dw * wf).norm().item()
+    # deterministic: a second backward over the same data gives the same bits
+    views2 = [g_init[:n0].clone(), g_init[n0:].clone()] if two_views else [g_init.clone()]
+    x2 = x.detach().clone().requires_grad_(True)
+    lam2 = torch.tensor(0.7, device="cuda", requires_grad=True)
+    fused.bank_linear(x2, lam2, w, views2).backward(dy)
+    assert torch.equal(lam2.grad, lam.grad) and all(torch.equal(a, b) for a, b in zip(views, views2))
+    assert torch.equal(x2.grad, x.grad)
+    fused.check_status()
+
+
+@pytest.mark.parametrize("T,n,param_scale", [(4096, 41, True), (49152, 26, True), (2048, 14, False), (1024, 5, False)])
+def test_gate_mlp_forward_backward(fused, T, n, param_scale):
+    torch.manual_seed(1)
+    D = 768
+    x = torch.randn(T, D, device="cuda").to(BF)
+    w1 = (torch.randn(64, D, device="cuda") * D ** -0.5).to(BF)
+    w2 = (torch.randn(48, 64, device="cuda") * 0.2).to(BF)
+    b2 = torch.randn(48, device="cuda").to(BF)
+    dout = torch.randn(T, n, device="cuda").to(BF)
+
+    def run(impl, dtype):
+        xs = x.to(dtype).requires_grad_(True)
+        a, b, c = (t.to(dtype).requires_grad_(True) for t in (w1, w2, b2))
+        sc = torch.tensor(0.1, device="cuda", requires_grad=True) if param_scale else 0.1
+        out = impl(xs, a, b[:n], c[:n], sc)
+        out.backward(dout.to(out.dtype))
+        return out, xs.grad, a.grad, b.grad[:n], c.grad[:n], (sc.grad if param_scale else None)
+
+    def oracle(xs, a, b, c, sc):
+        h = F.gelu(F.linear(xs, a))
+        return (F.linear(h, b) + c) * sc
+
+    got = run(fused.gate_mlp, BF)
+    want = run(oracle, torch.float32)
+    tol = [1.2e-2, 2e-2, 2e-2, 2e-2, 2e-2]
+    for g, w, t, name in zip(got, want, tol, ("out", "dx", "dw1", "dw2", "db2")):
+        assert _rel(g, w) < t, (name, _rel(g, w))
+    if param_scale:
+        assert abs(got[5].item() - want[5].item()) < 2e-2 * abs(want[5].item()) + 1.0
+    got2 = run(fused.gate_mlp, BF)
+    assert all(torch.equal(a, b) for a, b in zip(got[:5], got2[:5]))          # no atomics anywhere
+    fused.check_status()
+
+
+def test_batched_mlp_weight_refresh_matches_per_layer_kernels(fused):
+    from modded_nanogpt_b200.ops import native
+    C = native.lib()
+    torch.manual_seed(2)
+    Lp, hid, dim = 4, 3072, 768
+    bank = (torch.randn(Lp, 2, hid, dim, device="cuda") * 0.03).to(BF)
+    used, nxt = torch.full((Lp,), 7.0, device="cuda"), torch.full((Lp,), 3.0, device="cuda")
+    st = fused.MlpFp8State(bank)
+    st.amax_bits.copy_(torch.tensor([0.0, 2.5, 0.0, 9.0], device="cuda").view(torch.int32))
+    st.act_scale.fill_(5.0)
+    fused.quantize_mlp_weights(bank, st, used, nxt, bootstrap=False)
+    for l in range(Lp):
+        q, s = C.quant_rows(bank[l, 0].contiguous())
+        assert torch.equal(q.view(torch.uint8), st.fc8[l].view(torch.uint8)) and torch.equal(s, st.fc_scale[l])
+        qt = torch.empty(dim, hid, dtype=torch.float8_e4m3fn, device="cuda")
+        sc = torch.empty(dim, device="cuda")
+        C.quant_transpose(bank[l, 1].contiguous(), qt, sc, torch.empty(dim, dtype=torch.int32, device="cuda"))
+        assert torch.equal(qt.view(torch.uint8), st.projT8[l].view(torch.uint8)) and torch.equal(sc, st.projT_scale[l])
+        # and against the plain statement of the op
+        assert torch.allclose(st.projT_scale[l], bank[l, 1].float().abs().amax(0) / 448, rtol=1e-6)
+    assert torch.allclose(used, torch.full((Lp,), 3.0, device="cuda"))
+    assert torch.allclose(nxt, st.projT_scale.amax(1) * 1.12)
+    want_act = torch.tensor([5.0, 2.5 * 1.8 / 448, 5.0, 9.0 * 1.8 / 448], device="cuda")
+    assert torch.allclose(st.act_scale, want_act) and int(st.amax_bits.abs().sum()) == 0
+    fused.quantize_mlp_weights(bank, st, used, nxt, bootstrap=True)
+    assert torch.allclose(used, st.projT_scale.amax(1))
+    fused.check_status()
