@@ -28,6 +28,9 @@ typedef struct {
   const void* cin;                    // STORE: addend (beta); DPRE: saved post activations
   float alpha, beta;
   const float* alpha_ptr;             // optional device scalar folded into alpha
+  const float* alpha2_ptr;            // a second one (STORE, DPRE)
+  const float* beta_ptr;              // optional device scalar folded into beta (STORE)
+  float* dot_out;                     // DPRE: *dot_out += sum(acc * post) over the whole product (fp32 atomics), or null
   const float* row_scale;
   const float* col_scale;
   void* out8;                         // RELU2: e4m3 copy of the output
@@ -48,6 +51,9 @@ int mng_rmsnorm_bwd(const void* x, const void* dy, const float* rstd, void* dx, 
                     void* stream);
 int mng_rmsnorm_bwd_add(const void* x, const void* dy, const float* rstd, const void* addend, void* dx, long long rows,
                         int cols, void* stream);
+// dx = norm backward + (*addend_scale) * addend; *dot_out += sum(addend * x)  (fp32 atomics, one per block).
+int mng_rmsnorm_bwd_add_scaled(const void* x, const void* dy, const float* rstd, const void* addend,
+                               const float* addend_scale, float* dot_out, void* dx, long long rows, int cols, void* stream);
 // Row-wise e4m3 quantisation: q = x / s, s[r] = amax(x[r,:])/448 (bf16 in).
 int mng_quant_rows_e4m3(const void* x, void* q, float* scale, long long rows, int cols, void* stream);
 // dst[c, r] = src[r, c] (optionally += ), bf16; 32x32 tiles through shared memory.

@@ -42,7 +42,8 @@ void check(int rc, const char* what) { TORCH_CHECK(rc == 0, what, " failed with 
 void gemm(const Tensor& a, const Tensor& b, Tensor& out, bool a_mn, bool b_mn, int64_t epilogue, int64_t bn, double alpha,
           double beta, const c10::optional<Tensor>& cin, const c10::optional<Tensor>& alpha_t,
           const c10::optional<Tensor>& row_scale, const c10::optional<Tensor>& col_scale, const c10::optional<Tensor>& out8,
-          const c10::optional<Tensor>& act_scale, const c10::optional<Tensor>& amax_bits, int64_t max_ctas) {
+          const c10::optional<Tensor>& act_scale, const c10::optional<Tensor>& amax_bits, int64_t max_ctas,
+          const c10::optional<Tensor>& alpha2_t, const c10::optional<Tensor>& beta_t, const c10::optional<Tensor>& dot_out) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda());
   TORCH_CHECK(a.dim() == b.dim() && (a.dim() == 2 || a.dim() == 3) && out.dim() == a.dim());
   TORCH_CHECK(a.stride(-1) == 1 && b.stride(-1) == 1 && out.stride(-1) == 1, "innermost dims must be contiguous");
@@ -83,6 +84,9 @@ void gemm(const Tensor& a, const Tensor& b, Tensor& out, bool a_mn, bool b_mn, i
   g.alpha = (float)alpha;
   g.beta = (float)beta;
   g.alpha_ptr = fptr(alpha_t);
+  g.alpha2_ptr = fptr(alpha2_t);
+  g.beta_ptr = fptr(beta_t);
+  g.dot_out = const_cast<float*>(fptr(dot_out));
   g.row_scale = fptr(row_scale);
   g.col_scale = fptr(col_scale);
   if (out8.has_value() && out8->defined()) {
@@ -129,6 +133,22 @@ Tensor rmsnorm_bwd(const Tensor& x, const Tensor& dy, const c10::optional<Tensor
   check(mng_rmsnorm_bwd(x.data_ptr(), dy.data_ptr(), fptr(rstd), dx.data_ptr(), rows, cols,
                         (accum_into.has_value() && accum_into->defined()) ? 1 : 0, cur_stream()),
         "mng_rmsnorm_bwd");
+  g_launches += 1;
+  return dx;
+}
+
+// dx = rmsnorm backward(x, dy) + scale * addend in one pass; dot (fp32, one element) += sum(addend * x)
+Tensor rmsnorm_bwd_add_scaled(const Tensor& x, const Tensor& dy, const c10::optional<Tensor>& rstd, const Tensor& addend,
+                              const Tensor& scale, Tensor& dot) {
+  TORCH_CHECK(x.is_contiguous() && dy.is_contiguous() && addend.is_contiguous() && x.scalar_type() == torch::kBFloat16 &&
+              dy.scalar_type() == torch::kBFloat16 && addend.scalar_type() == torch::kBFloat16 && addend.numel() == x.numel());
+  TORCH_CHECK(scale.scalar_type() == torch::kFloat32 && scale.numel() == 1 && dot.scalar_type() == torch::kFloat32 && dot.numel() >= 1);
+  c10::cuda::CUDAGuard guard(x.device());
+  const int cols = (int)x.size(-1);
+  Tensor dx = torch::empty_like(x);
+  check(mng_rmsnorm_bwd_add_scaled(x.data_ptr(), dy.data_ptr(), fptr(rstd), addend.data_ptr(), scale.data_ptr<float>(),
+                                   dot.data_ptr<float>(), dx.data_ptr(), x.numel() / cols, cols, cur_stream()),
+        "mng_rmsnorm_bwd_add_scaled");
   g_launches += 1;
   return dx;
 }
@@ -671,6 +691,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("rmsnorm_bwd_add", &rmsnorm_bwd_add);
+  m.def("rmsnorm_bwd_add_scaled", &rmsnorm_bwd_add_scaled);
   m.def("quant_rows", &quant_rows);
   m.def("transpose", &transpose);
   m.def("quant_transpose", &quant_transpose);

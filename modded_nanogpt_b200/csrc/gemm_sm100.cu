@@ -45,20 +45,25 @@ struct EpiStore {
     const void* cin;            // same dtype/layout as out; may alias out
     const float* row_scale;     // [batch*M] or null
     const float* col_scale;     // [batch*N] or null
-    const float* alpha_ptr;     // optional device scalar multiplied into alpha
+    const float* alpha_ptr;     // optional device scalars multiplied into alpha / beta
+    const float* alpha2_ptr;
+    const float* beta_ptr;
     long long ld, bstride;      // elements
     float alpha, beta;
   };
   struct State {};
   __device__ static void finish(const Params&, State&) {}
-  __device__ static void apply(const Params& p, State&, ChunkIO& io, const float (&acc)[32], int b, long long row0, int col0,
+  __device__ static void apply(const Params& pp, State&, ChunkIO& io, const float (&acc)[32], int b, long long row0, int col0,
                                int M, int N) {
     constexpr int ESZ = OUT_F32 ? 4 : 2;
     constexpr int B = 32 * ESZ;
     const long long row = row0 + io.lane;
     const bool live = row < M;
+    Params p = pp;
+    if (p.beta_ptr) p.beta *= *p.beta_ptr;
     float a = p.alpha;
     if (p.alpha_ptr) a *= *p.alpha_ptr;
+    if (p.alpha2_ptr) a *= *p.alpha2_ptr;
     if (p.row_scale && live) a *= p.row_scale[(long long)b * M + row];
     float v[32];
 #pragma unroll
@@ -179,17 +184,28 @@ struct EpiRelu2 {
 };
 
 // MLP backward: dpre = bf16( 2 * bf16(acc) * sqrt(post) ) with post = relu(pre)^2 saved by the forward.
+// With alpha_ptr the incoming gradient is scaled by that device scalar (the consumer of the MLP output multiplied it
+// by a learned coefficient); dot_out receives sum(acc * post) = <g, post W2> = the gradient of that coefficient.
 struct EpiDpre {
   struct Params {
     __nv_bfloat16* out;
     const __nv_bfloat16* post;
     long long ld;
+    const float* alpha_ptr;
+    float* dot_out;
   };
-  struct State {};
-  __device__ static void finish(const Params&, State&) {}
-  __device__ static void apply(const Params& p, State&, ChunkIO& io, const float (&acc)[32], int b, long long row0, int col0,
+  struct State { float dot = 0.f; };
+  __device__ static void finish(const Params& p, State& st) {
+    if (p.dot_out) {
+      const float d = warp_sum(st.dot);
+      if ((threadIdx.x & 31) == 0) atomicAdd(p.dot_out, d);
+    }
+  }
+  __device__ static void apply(const Params& p, State& st, ChunkIO& io, const float (&acc)[32], int b, long long row0, int col0,
                                int M, int N) {
     io.load_rows<64>(p.post, p.ld * 2, row0, (long long)col0 * 2, M);
+    const float al = p.alpha_ptr ? *p.alpha_ptr : 1.f;
+    const bool live = row0 + io.lane < M;
     float o[32];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -198,6 +214,9 @@ struct EpiDpre {
 #pragma unroll
       for (int t = 0; t < 8; t += 2) {
         float a0 = acc[8 * j + t], a1 = acc[8 * j + t + 1];
+        if (live) st.dot += a0 * f[t] + a1 * f[t + 1];
+        a0 *= al;
+        a1 *= al;
         round_bf16x2(a0, a1);
         o[8 * j + t] = 2.f * a0 * sqrtf(f[t]);
         o[8 * j + t + 1] = 2.f * a1 * sqrtf(f[t + 1]);
@@ -237,6 +256,8 @@ struct TEpiStore {
     const float* row_scale;
     const float* col_scale;
     const float* alpha_ptr;
+    const float* alpha2_ptr;
+    const float* beta_ptr;
     float alpha, beta;
   };
   struct State {};
@@ -245,6 +266,8 @@ struct TEpiStore {
                                uint4 (&)[2], int b, long long row, int col0, int M, int N) {
     float a = p.alpha;
     if (p.alpha_ptr) a *= *p.alpha_ptr;
+    if (p.alpha2_ptr) a *= *p.alpha2_ptr;
+    const float beta = p.beta_ptr ? p.beta * *p.beta_ptr : p.beta;
     if (p.row_scale && row < M) a *= p.row_scale[(long long)b * M + row];
     float v[32];
 #pragma unroll
@@ -260,7 +283,7 @@ struct TEpiStore {
         float f[8];
         unpack_bf16x8(cin[j], f);
 #pragma unroll
-        for (int t = 0; t < 8; ++t) v[8 * j + t] += p.beta * f[t];
+        for (int t = 0; t < 8; ++t) v[8 * j + t] += beta * f[t];
       }
     }
 #pragma unroll
@@ -322,11 +345,18 @@ struct TEpiRelu2 {
 
 struct TEpiDpre {
   static constexpr bool kCin = true, kOut8 = false;
-  struct Params { int unused; };
-  struct State {};
-  __device__ static void finish(const Params&, State&) {}
-  __device__ static void apply(const Params&, State&, const float (&acc)[32], const uint4 (&cin)[4], uint4 (&out)[4],
-                               uint4 (&)[2], int, long long, int, int, int) {
+  struct Params { const float* alpha_ptr; float* dot_out; };
+  struct State { float dot = 0.f; };
+  __device__ static void finish(const Params& p, State& st) {
+    if (p.dot_out) {
+      const float d = warp_sum(st.dot);
+      if ((threadIdx.x & 31) == 0) atomicAdd(p.dot_out, d);
+    }
+  }
+  __device__ static void apply(const Params& p, State& st, const float (&acc)[32], const uint4 (&cin)[4], uint4 (&out)[4],
+                               uint4 (&)[2], int, long long row, int, int M, int) {
+    const float al = p.alpha_ptr ? *p.alpha_ptr : 1.f;
+    const bool live = row < M;
     float o[32];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -335,6 +365,9 @@ struct TEpiDpre {
 #pragma unroll
       for (int t = 0; t < 8; t += 2) {
         float a0 = acc[8 * j + t], a1 = acc[8 * j + t + 1];
+        if (live) st.dot += a0 * f[t] + a1 * f[t + 1];
+        a0 *= al;
+        a1 *= al;
         round_bf16x2(a0, a1);
         o[8 * j + t] = 2.f * a0 * sqrtf(f[t]);
         o[8 * j + t + 1] = 2.f * a1 * sqrtf(f[t + 1]);
@@ -528,10 +561,10 @@ static int launch_pair(const GemmDesc& g, const typename Epi::Params& ep, int ma
 template <int ES, bool A_MN, bool B_MN, uint32_t AF, uint32_t BF>
 static int launch_store_pair(const GemmDesc& g) {
   if (g.beta != 0.f) {
-    typename TEpiStore<true>::Params p{g.row_scale, g.col_scale, g.alpha_ptr, g.alpha, g.beta};
+    typename TEpiStore<true>::Params p{g.row_scale, g.col_scale, g.alpha_ptr, g.alpha2_ptr, g.beta_ptr, g.alpha, g.beta};
     return launch_pair<ES, A_MN, B_MN, AF, BF, TEpiStore<true>>(g, p, g.max_ctas);
   }
-  typename TEpiStore<false>::Params p{g.row_scale, g.col_scale, g.alpha_ptr, g.alpha, g.beta};
+  typename TEpiStore<false>::Params p{g.row_scale, g.col_scale, g.alpha_ptr, g.alpha2_ptr, g.beta_ptr, g.alpha, g.beta};
   return launch_pair<ES, A_MN, B_MN, AF, BF, TEpiStore<false>>(g, p, g.max_ctas);
 }
 
@@ -539,11 +572,11 @@ template <int ES, bool A_MN, bool B_MN, uint32_t AF, uint32_t BF>
 static int launch_store(const GemmDesc& g) {
   if (g.bn == 512 && pair_ok(g)) return launch_store_pair<ES, A_MN, B_MN, AF, BF>(g);
   if (g.out_f32) {
-    EpiStore<true>::Params p{g.out, g.cin, g.row_scale, g.col_scale, g.alpha_ptr, g.ldc, g.c_bstride, g.alpha, g.beta};
+    EpiStore<true>::Params p{g.out, g.cin, g.row_scale, g.col_scale, g.alpha_ptr, g.alpha2_ptr, g.beta_ptr, g.ldc, g.c_bstride, g.alpha, g.beta};
     return g.bn >= 256 ? launch_one<256, ES, A_MN, B_MN, AF, BF, EpiStore<true>>(g, p, g.max_ctas)
                        : launch_one<128, ES, A_MN, B_MN, AF, BF, EpiStore<true>>(g, p, g.max_ctas);
   }
-  EpiStore<false>::Params p{g.out, g.cin, g.row_scale, g.col_scale, g.alpha_ptr, g.ldc, g.c_bstride, g.alpha, g.beta};
+  EpiStore<false>::Params p{g.out, g.cin, g.row_scale, g.col_scale, g.alpha_ptr, g.alpha2_ptr, g.beta_ptr, g.ldc, g.c_bstride, g.alpha, g.beta};
   return g.bn >= 256 ? launch_one<256, ES, A_MN, B_MN, AF, BF, EpiStore<false>>(g, p, g.max_ctas)
                      : launch_one<128, ES, A_MN, B_MN, AF, BF, EpiStore<false>>(g, p, g.max_ctas);
 }
@@ -594,9 +627,9 @@ extern "C" int mng_gemm(const GemmDesc* gp) {
   }
   if (g.epilogue == MNG_EPI_DPRE) {
     if (g.a_mn || g.b_mn || g.batch != 1 || es != 2 || (g.N % 32) || (g.ldc % 8)) return -16;
-    EpiDpre::Params p{reinterpret_cast<__nv_bfloat16*>(g.out), reinterpret_cast<const __nv_bfloat16*>(g.cin), g.ldc};
+    EpiDpre::Params p{reinterpret_cast<__nv_bfloat16*>(g.out), reinterpret_cast<const __nv_bfloat16*>(g.cin), g.ldc, g.alpha_ptr, g.dot_out};
     if (g.bn == 512 && pair_ok(g)) {
-      TEpiDpre::Params tp{0};
+      TEpiDpre::Params tp{g.alpha_ptr, g.dot_out};
       return launch_pair<2, false, false, 1, 1, TEpiDpre>(g, tp, g.max_ctas);
     }
     return launch_one<256, 2, false, false, 1, 1, EpiDpre>(g, p, g.max_ctas);

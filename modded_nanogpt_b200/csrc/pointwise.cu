@@ -68,14 +68,23 @@ rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restric
   }
 }
 
-// dx = rstd * (dy - xhat * mean(dy * xhat)) [+ addend],  xhat = x * rstd.   `addend` may be `dx` itself (accumulate).
+// dx = rstd * (dy - xhat * mean(dy * xhat)) [+ s * addend],  xhat = x * rstd.   `addend` may be `dx` itself (accumulate).
+// s = *addend_scale (1 when null).  With dot_out, *dot_out += sum(addend * x) over all rows: when the addend is the
+// gradient g of y = s * x + ..., that sum is the gradient of s.
 template <int MAXV>
 __global__ void __launch_bounds__(ROW_WARPS * 32)
 rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ dy, const float* __restrict__ rstd_in,
-                   const __nv_bfloat16* addend, __nv_bfloat16* dx, long long rows, int cols, float eps) {
+                   const __nv_bfloat16* addend, __nv_bfloat16* dx, long long rows, int cols, float eps,
+                   const float* __restrict__ addend_scale = nullptr, float* __restrict__ dot_out = nullptr) {
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
-  if (row >= rows) return;
+  __shared__ float blk_dot[ROW_WARPS];
+  if (dot_out) {                                        // block-uniform: every warp takes part in the block sum
+    if (lane == 0) blk_dot[threadIdx.x >> 5] = 0.f;
+  }
+  const float as = addend_scale ? *addend_scale : 1.f;
+  float adot = 0.f;
+  if (row < rows) {
   const int nv = cols >> 8;
   float xv[MAXV][8], gv[MAXV][8];
   float ss = 0.f, dot = 0.f;
@@ -112,12 +121,25 @@ rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __r
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
           float2 f = __bfloat1622float2(h[t]);
-          r[2 * t] += f.x; r[2 * t + 1] += f.y;
+          r[2 * t] += as * f.x; r[2 * t + 1] += as * f.y;
+          adot += f.x * xv[i][2 * t] + f.y * xv[i][2 * t + 1];
         }
       }
       uint4 w;
       w.x = pack_bf16x2(r[0], r[1]); w.y = pack_bf16x2(r[2], r[3]); w.z = pack_bf16x2(r[4], r[5]); w.w = pack_bf16x2(r[6], r[7]);
       *reinterpret_cast<uint4*>(o) = w;
+    }
+  }
+  }
+  if (dot_out) {
+    adot = warp_sum(adot);
+    if (lane == 0) blk_dot[threadIdx.x >> 5] = adot;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float s = 0.f;
+#pragma unroll
+      for (int w = 0; w < ROW_WARPS; ++w) s += blk_dot[w];
+      atomicAdd(dot_out, s);
     }
   }
 }
@@ -288,6 +310,15 @@ extern "C" int mng_rmsnorm_bwd_add(const void* x, const void* dy, const float* r
   if (rows == 0) return 0;
   DISPATCH_COLS(rmsnorm_bwd_kernel, (const __nv_bfloat16*)x, (const __nv_bfloat16*)dy, rstd, (const __nv_bfloat16*)addend,
                 (__nv_bfloat16*)dx, rows, cols, kRmsEps);
+}
+
+// The same with the addend scaled by a device scalar, and sum(addend * x) added to *dot_out (see the kernel).
+extern "C" int mng_rmsnorm_bwd_add_scaled(const void* x, const void* dy, const float* rstd, const void* addend,
+                                          const float* addend_scale, float* dot_out, void* dx, long long rows, int cols,
+                                          void* stream) {
+  if (rows == 0) return 0;
+  DISPATCH_COLS(rmsnorm_bwd_kernel, (const __nv_bfloat16*)x, (const __nv_bfloat16*)dy, rstd, (const __nv_bfloat16*)addend,
+                (__nv_bfloat16*)dx, rows, cols, kRmsEps, addend_scale, dot_out);
 }
 
 extern "C" int mng_quant_rows_e4m3(const void* x, void* q, float* scale, long long rows, int cols, void* stream) {

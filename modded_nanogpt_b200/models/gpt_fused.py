@@ -13,6 +13,11 @@ from ..ops import fused
 from ..ops.glue import Term, cols_tap, embed_direct, grad_sink, lincomb, qkv_post, xsa_gate, xsa_gate_cols
 
 
+import os
+
+MLP_MIX_FUSED = os.environ.get("MNG_MLP_MIX", "1") != "0"    # 0: separate `lincomb` after the down projection (A/B switch)
+
+
 def fused_supported(model, x: Tensor) -> bool:
     from .. import ops as ops_pkg
     return (x.is_cuda and ops_pkg.get_backend() != "reference" and model.head_dim == 128 and model.model_dim % 256 == 0
@@ -217,11 +222,18 @@ def forward_fused(m, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, big
 
         if direct:
             st = m._fp8_state.layer(i) if (training_fp8 and m._fp8_state is not None) else None
-            h, x = fused.norm_relu2_mlp(x, m.mlp_bank[i, 0], m.mlp_bank[i, 1], st, (m.mlp_bank.grad[i, 0], m.mlp_bank.grad[i, 1]),
-                                        fork=True)
+            gviews = (m.mlp_bank.grad[i, 0], m.mlp_bank.grad[i, 1])
+            if mu is None and MLP_MIX_FUSED:
+                # resid * x + post * MLP(norm(x)) inside the down projection's epilogue (`train_gpt.py:1665`)
+                x = fused.norm_relu2_mlp_mix(x, m.mlp_bank[i, 0], m.mlp_bank[i, 1], resid[i, 1], post[i, 1], st, gviews)
+                h = None
+            else:
+                h, x = fused.norm_relu2_mlp(x, m.mlp_bank[i, 0], m.mlp_bank[i, 1], st, gviews, fork=True)
         else:
             h = m._mlp(i, x, training_fp8)
-        if mu is not None:
+        if h is None:
+            pass
+        elif mu is not None:
             x = lincomb([Term(x, col=12, **G("mu", mu)), Term(h, col=13, **G("mu", mu))])
         else:
             x = lincomb([Term(x, scalar=resid[i, 1]), Term(h, scalar=post[i, 1])])

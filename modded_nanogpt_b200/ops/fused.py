@@ -44,9 +44,14 @@ def gemm(a: Tensor, b: Tensor, *, a_mn: bool = False, b_mn: bool = False, out: T
          out_dtype=torch.bfloat16, bn: int | None = None, alpha: float = 1.0, beta: float = 0.0, cin: Tensor | None = None,
          alpha_t: Tensor | None = None, row_scale: Tensor | None = None, col_scale: Tensor | None = None,
          epilogue: int = EPI_STORE, out8: Tensor | None = None, act_scale: Tensor | None = None,
-         amax_bits: Tensor | None = None, max_ctas: int = 0) -> Tensor:
+         amax_bits: Tensor | None = None, max_ctas: int = 0, alpha2_t: Tensor | None = None,
+         beta_t: Tensor | None = None, dot_out: Tensor | None = None) -> Tensor:
     """out = epilogue(A @ B^T) on the tcgen05 kernel.  A is [.., M, K] (or [.., K, M] with a_mn),
-    B is [.., N, K] (or [.., K, N] with b_mn); fp32 accumulation."""
+    B is [.., N, K] (or [.., K, N] with b_mn); fp32 accumulation.  `alpha_t`, `alpha2_t`, `beta_t`: one-element fp32
+    device tensors multiplied into alpha / beta (`beta_t` alone means beta = 1 * beta_t); `dot_out` (EPI_DPRE):
+    one-element fp32 accumulator that receives sum(acc * cin)."""
+    if beta_t is not None and beta == 0.0:
+        beta = 1.0
     M = a.shape[-1] if a_mn else a.shape[-2]
     N = b.shape[-1] if b_mn else b.shape[-2]
     if out is None:
@@ -62,7 +67,7 @@ def gemm(a: Tensor, b: Tensor, *, a_mn: bool = False, b_mn: bool = False, out: T
         if PAIR_GEMM and out.dtype == torch.bfloat16 and -(-M // 256) * -(-N // 256) * batch >= NUM_SMS // 2:
             bn = 512
     _C().gemm(a, b, out, a_mn, b_mn, epilogue, bn, alpha, beta, cin, alpha_t, row_scale, col_scale, out8, act_scale,
-              amax_bits, max_ctas)
+              amax_bits, max_ctas, alpha2_t, beta_t, dot_out)
     return out
 
 
@@ -165,10 +170,16 @@ def quantize_mlp_weights(bank: Tensor, state: MlpFp8State | None, used_scales: T
 
 
 class _NormRelu2Mlp(torch.autograd.Function):
-    """out = relu(norm(x) @ W1^T)^2 @ W2 with W1, W2 stored (hidden, dim)."""
+    """out = relu(norm(x) @ W1^T)^2 @ W2 with W1, W2 stored (hidden, dim).
+
+    With `mix = (a, b)` (one-element fp32 device tensors) the result is a * x + b * MLP(norm(x)): the residual mix
+    of `train_gpt.py:1665` runs in the down-projection's epilogue (x arrives as the addend tile), and in the backward
+    b scales the incoming gradient inside the two GEMMs that consume it, d b = <g, MLP> falls out of the
+    pre-activation-gradient epilogue (sum of acc * post), a * g joins the norm backward as a scaled addend and
+    d a = <g, x> is summed by that same kernel - no separate mix kernel and no stored MLP output in either direction."""
 
     @staticmethod
-    def forward(ctx, x, w_fc, w_proj, fp8, g_fc=None, g_proj=None, fork=False):
+    def forward(ctx, x, w_fc, w_proj, fp8, g_fc=None, g_proj=None, fork=False, a_t=None, b_t=None):
         C = _C()
         T, D = x.shape
         ctx.grad_views = (g_fc, g_proj)
@@ -176,6 +187,12 @@ class _NormRelu2Mlp(torch.autograd.Function):
         ctx.set_materialize_grads(False)
         hid = w_fc.shape[0]
         xc = x.contiguous()
+        mix = {}
+        ctx.mix_meta = None
+        if a_t is not None:
+            a32, b32 = a_t.detach().reshape(1).float(), b_t.detach().reshape(1).float()
+            mix = dict(alpha2_t=b32, beta_t=a32, cin=xc)
+            ctx.mix_meta = ((a_t.dtype, a_t.shape), (b_t.dtype, b_t.shape))
         post = torch.empty(T, hid, dtype=torch.bfloat16, device=x.device)
         if fp8 is not None:
             fc8, fc_scale, projT8, projT_scale, act_scale, amax_bits = fp8
@@ -183,33 +200,50 @@ class _NormRelu2Mlp(torch.autograd.Function):
             post8 = torch.empty(T, hid, dtype=torch.float8_e4m3fn, device=x.device)
             gemm(y8, fc8, out=post, epilogue=EPI_RELU2, row_scale=y_scale, col_scale=fc_scale, out8=post8,
                  act_scale=act_scale, amax_bits=amax_bits)
-            out = gemm(post8, projT8, col_scale=projT_scale, alpha_t=act_scale)
+            out = gemm(post8, projT8, col_scale=projT_scale, alpha_t=act_scale, **mix)
         else:
             y, _, _, rstd = C.rmsnorm_fwd(xc, True, False, True)
             gemm(y, w_fc, out=post, epilogue=EPI_RELU2)
-            out = gemm(post, w_proj, b_mn=True)
+            out = gemm(post, w_proj, b_mn=True, **mix)
+        if a_t is not None:
+            ctx.save_for_backward(xc, rstd, y, post, w_fc, w_proj, a32, b32)
+            return out
         ctx.save_for_backward(xc, rstd, y, post, w_fc, w_proj)
         return (out, x) if fork else out
 
     @staticmethod
     def backward(ctx, g, dres=None):
         C = _C()
-        x, rstd, y, post, w_fc, w_proj = ctx.saved_tensors
-        if g is None:                                     # only the carried-on x was used
-            return dres, None, None, None, None, None, None
+        nothing = (None,) * 8
+        if ctx.mix_meta is not None:
+            x, rstd, y, post, w_fc, w_proj, a32, b32 = ctx.saved_tensors
+            sc = dict(alpha_t=b32)
+            dab = torch.zeros(2, dtype=torch.float32, device=x.device)
+        else:
+            x, rstd, y, post, w_fc, w_proj = ctx.saved_tensors
+            sc, dab = {}, None
+            if g is None:                                     # only the carried-on x was used
+                return (dres,) + nothing
         g = g.contiguous()
         g_fc, g_proj = ctx.grad_views
         # weight gradients: either returned to autograd, or accumulated by the GEMM epilogue (beta = 1)
         # straight into the caller's slices of the parameter-bank gradient
         acc = dict(beta=1.0) if g_fc is not None else {}
-        d_proj = gemm(post, g, a_mn=True, b_mn=True, out=g_proj, cin=g_proj, **acc)      # post^T g      (hid, dim)
-        dpre = gemm(g, w_proj, epilogue=EPI_DPRE, cin=post)                  # 2 (g W2^T) sqrt(post)
-        d_fc = gemm(dpre, y, a_mn=True, b_mn=True, out=g_fc, cin=g_fc, **acc)            # dpre^T y      (hid, dim)
-        dy = gemm(dpre, w_fc, b_mn=True)                                     # dpre W1          (T, dim)
-        dx = _norm_bwd_plus(x, dy, rstd, dres)
+        d_proj = gemm(post, g, a_mn=True, b_mn=True, out=g_proj, cin=g_proj, **acc, **sc)    # post^T g      (hid, dim)
+        dpre = gemm(g, w_proj, epilogue=EPI_DPRE, cin=post, **sc,                            # 2 (g W2^T) sqrt(post)
+                    **(dict(dot_out=dab[1:2]) if dab is not None else {}))
+        d_fc = gemm(dpre, y, a_mn=True, b_mn=True, out=g_fc, cin=g_fc, **acc)                # dpre^T y      (hid, dim)
+        dy = gemm(dpre, w_fc, b_mn=True)                                                     # dpre W1       (T, dim)
+        if dab is not None:
+            dx = C.rmsnorm_bwd_add_scaled(x, dy, rstd, g, a32, dab[0:1])
+            (adt, ashp), (bdt, bshp) = ctx.mix_meta
+            dmix = (dab[0].to(adt).reshape(ashp), dab[1].to(bdt).reshape(bshp))
+        else:
+            dx = _norm_bwd_plus(x, dy, rstd, dres)
+            dmix = (None, None)
         if g_fc is not None:
-            return dx, None, None, None, None, None, None
-        return dx, d_fc, d_proj, None, None, None, None
+            return (dx, None, None, None, None, None, None) + dmix
+        return (dx, d_fc, d_proj, None, None, None, None) + dmix
 
 
 def norm_relu2_mlp(x: Tensor, w_fc: Tensor, w_proj: Tensor, fp8_state=None, grad_views=None, fork: bool = False):
@@ -326,6 +360,14 @@ def gate_mlp(x: Tensor, w1: Tensor, w2: Tensor, b2: Tensor, scale) -> Tensor:
 def gate_mlp_supported(x: Tensor, w1: Tensor, w2: Tensor) -> bool:
     return (x.is_cuda and x.dtype == torch.bfloat16 and w1.dtype == torch.bfloat16 and w1.shape[0] == 64
             and w2.shape[0] <= 48 and x.shape[-1] % 64 == 0 and x.numel() // x.shape[-1] >= 128)
+
+
+def norm_relu2_mlp_mix(x: Tensor, w_fc: Tensor, w_proj: Tensor, a: Tensor, b: Tensor, fp8_state=None, grad_views=None):
+    """a * x + b * relu(norm(x) W1^T)^2 W2 with the mix fused into the down projection (see `_NormRelu2Mlp`);
+    a, b: one-element fp32 tensors (parameters or views of parameters)."""
+    if grad_views is not None:
+        return _NormRelu2Mlp.apply(x, w_fc.detach(), w_proj.detach(), fp8_state, grad_views[0], grad_views[1], False, a, b)
+    return _NormRelu2Mlp.apply(x, w_fc, w_proj, fp8_state, None, None, False, a, b)
 
 
 def relu2_mlp(x_normed: Tensor, w_fc: Tensor, w_proj: Tensor, fp8_state=None) -> Tensor:

@@ -63,8 +63,8 @@ def test_gate_mlp_forward_backward(fused, T, n, param_scale):
     dout = torch.randn(T, n, device="cuda").to(BF)
 
     def run(impl, dtype):
-        xs = x.to(dtype).requires_grad_(True)
-        a, b, c = (t.to(dtype).requires_grad_(True) for t in (w1, w2, b2))
+        xs = x.detach().clone().to(dtype).requires_grad_(True)
+        a, b, c = (t.detach().clone().to(dtype).requires_grad_(True) for t in (w1, w2, b2))
         sc = torch.tensor(0.1, device="cuda", requires_grad=True) if param_scale else 0.1
         out = impl(xs, a, b[:n], c[:n], sc)
         out.backward(dout.to(out.dtype))
@@ -112,4 +112,62 @@ def test_batched_mlp_weight_refresh_matches_per_layer_kernels(fused):
     assert torch.allclose(st.act_scale, want_act) and int(st.amax_bits.abs().sum()) == 0
     fused.quantize_mlp_weights(bank, st, used, nxt, bootstrap=True)
     assert torch.allclose(used, st.projT_scale.amax(1))
+    fused.check_status()
+
+
+@pytest.mark.parametrize("T,use_fp8", [(4096, False), (4096, True), (49152, True)])
+def test_mlp_with_fused_residual_mix(fused, T, use_fp8):
+    """a * x + b * relu(norm(x) W1^T)^2 W2 in one autograd node against the fp32 statement; also against the unfused
+    pair (MLP node + lincomb) on the same kernels, which it must match closely in every gradient."""
+    from modded_nanogpt_b200.ops.glue import Term, lincomb
+    torch.manual_seed(3)
+    D, hid = 768, 3072
+    bank = torch.empty(1, 2, hid, D, device="cuda")
+    bank[0, 0].uniform_(-1, 1).mul_(3 ** 0.5 * 0.5 * D ** -0.5)
+    bank[0, 1].normal_(0, 0.02)
+    bank = bank.to(BF)
+    x = torch.randn(T, D, device="cuda").to(BF)
+    g = (torch.randn(T, D, device="cuda") * 0.05).to(BF)
+    st = None
+    if use_fp8:
+        st = fused.quantize_mlp_weights(bank, None, torch.ones(1, device="cuda"), torch.ones(1, device="cuda"), True)
+        st.act_scale.fill_(0.25)                                   # relu(.)^2 of unit-variance inputs stays well below 448 * 0.25
+        st = st.layer(0)
+
+    def run(mode):
+        xs = x.clone().requires_grad_(True)
+        a = torch.tensor(1.05, device="cuda", requires_grad=True)
+        b = torch.tensor(0.8, device="cuda", requires_grad=True)
+        gv = (torch.zeros(hid, D, dtype=BF, device="cuda"), torch.zeros(hid, D, dtype=BF, device="cuda"))
+        if mode == "fused":
+            y = fused.norm_relu2_mlp_mix(xs, bank[0, 0], bank[0, 1], a, b, st, gv)
+        elif mode == "unfused":
+            h, xr = fused.norm_relu2_mlp(xs, bank[0, 0], bank[0, 1], st, gv, fork=True)
+            y = lincomb([Term(xr, scalar=a), Term(h, scalar=b)])
+        else:
+            xf = xs.float()
+            w1, w2 = bank[0, 0].float().requires_grad_(True), bank[0, 1].float().requires_grad_(True)
+            h = torch.relu(F.rms_norm(xf, (D,)) @ w1.T).square() @ w2
+            y = a * xf + b * h
+            y.backward(g.float())
+            # scale of the signed sums behind da and db: the norm of their terms
+            run.term_norm = dict(da=(g.float() * xf).norm().item(), db=(g.float() * h).norm().item())
+            return y, xs.grad, a.grad, b.grad, w1.grad, w2.grad
+        y.backward(g)
+        return y, xs.grad, a.grad, b.grad, gv[0], gv[1]
+
+    got, unf, ref = run("fused"), run("unfused"), run("oracle")
+    tol = 4e-2 if use_fp8 else 1.5e-2
+    names = ("y", "dx", "da", "db", "dW1", "dW2")
+    for name, a, b in zip(names, got, ref):
+        if a.numel() == 1:
+            # a sum of T * D signed terms, each off by a relative error of the order of tol
+            assert abs(a.item() - b.item()) < tol * abs(b.item()) + 4 * tol * run.term_norm[name], (name, a.item(), b.item())
+        else:
+            assert _rel(a, b) < tol, (name, _rel(a, b))
+    for name, a, b in zip(names, got, unf):                       # same kernels, mix moved into the epilogues
+        if a.numel() == 1:
+            assert abs(a.item() - b.item()) < 5e-3 * abs(b.item()) + 1e-2, (name, a.item(), b.item())
+        else:
+            assert _rel(a, b) < 8e-3, (name, _rel(a, b))
     fused.check_status()
