@@ -12,5 +12,9 @@ REF = os.path.join(HERE, "_ref")
 def run_reference(args) -> dict:
     if not os.path.exists(os.path.join(REF, "train_gpt.py")):
         return {"impl": "reference", "unavailable": "baseline/_ref is not staged on this machine"}
-    from .reference_driver import drive
+    from .reference_driver import drive, drive_track2
+    if getattr(args, "track", 1) == 2:
+        if not os.path.exists(os.path.join(REF, "train_gpt_medium.py")):
+            return {"impl": "reference", "unavailable": "baseline/_ref/train_gpt_medium.py is not staged on this machine"}
+        return drive_track2(args, REF)
     return drive(args, REF)

@@ -193,6 +193,15 @@ def main():
     if a.list:
         print("\n".join(CASES))
         return
+    if a.case == "ref_lmhead_ce":          # the reference's fused lm_head + CE op at the same shape (separate process state)
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        ref = os.path.join(root, "baseline", "_ref")
+        if not os.path.exists(os.path.join(ref, "triton_kernels.py")):
+            print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not staged on this machine"}))
+            return
+        from baseline.reference_driver import reference_lmhead_ce_ms
+        print(json.dumps(reference_lmhead_ce_ms(ref, a.rows, a.iters, a.warmup)), flush=True)
+        return
     from modded_nanogpt_b200.ops import fused
     for name in (CASES if a.case == "all" else a.case.split(",")):
         torch.manual_seed(0)

@@ -8,6 +8,7 @@ all-gather around the same update kernels).
 
 Mode `fused_sparse` gives the bigram table a gradient with 98,304 random touched rows and lets the fused Adam kernel pull
 only those from the peers; the other modes reduce that table densely.
+`--impl reference` times the unmodified reference's `NorMuonAndAdam.step` on the same parameters instead.
 Prints one JSON line per communication mode: device time (CUDA events, max over ranks) of odd steps
 (NorMuon + Adam) and even steps (NorMuon only)."""
 import argparse
@@ -22,7 +23,20 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--modes", default="nccl,fused")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"],
+                    help="reference: the unmodified reference optimizer (NCCL + its compiled update math) on the same shapes")
     a = ap.parse_args()
+    if a.impl == "reference":
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        ref = os.path.join(root, "baseline", "_ref")
+        if not os.path.exists(os.path.join(ref, "train_gpt.py")):
+            print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not staged on this machine"}))
+            return
+        from baseline.reference_driver import reference_optimizer_step_ms
+        out = reference_optimizer_step_ms(ref, a.steps)
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps(out), flush=True)
+        return
     import torch
     from modded_nanogpt_b200.config import Hyperparameters, TrainingSchedule, track1_model, track1_stages
     from modded_nanogpt_b200.ops import fused
