@@ -157,7 +157,7 @@ def test_mlp_with_fused_residual_mix(fused, T, use_fp8):
         return y, xs.grad, a.grad, b.grad, gv[0], gv[1]
 
     got, unf, ref = run("fused"), run("unfused"), run("oracle")
-    tol = 4e-2 if use_fp8 else 1.5e-2
+    tol = 6e-2 if use_fp8 else 1.5e-2                          # e4m3 activations and weights in the forward
     names = ("y", "dx", "da", "db", "dW1", "dW2")
     for name, a, b in zip(names, got, ref):
         if a.numel() == 1:
