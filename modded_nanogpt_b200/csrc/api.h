@@ -72,6 +72,18 @@ int mng_mlp_weight_refresh(const void* bank, int layers, int hid, int dim, void*
                            float* projT_scale, unsigned int* amax_scratch, float* act_scale, unsigned int* amax_bits,
                            float* used_scales, float* next_scales, int bootstrap, void* stream);
 
+// Saturating static-scale e4m3 cast of a bf16 [rows, cols] matrix, as is (q) and / or transposed (qT); either may be
+// null.  rows, cols multiples of 64.
+int mng_quant_static_dual(const void* src, void* q, void* qT, long long rows, long long cols, float scale, void* stream);
+
+// lm_head GEMM fused with the soft-capped cross entropy: no [T, V] logits in memory.  x8 [T, K], wT8 [V, K] e4m3;
+// losses [T] fp32; dlogits [T, V] e5m2 (times grad_mul); scratch: slab_sum T * ceil(V/128), ztgt T * 4, rowc T floats.
+// n_predict <= 3.
+int mng_lmhead_ce_fused(const void* x8, const void* wT8, int T, int V, int K, float alpha, const long long* targets,
+                        const float* mtp_w, int n_predict, const long long* prefix_targets, const float* prefix_w, float A,
+                        float B, float C, float grad_mul, float* losses, void* dlogits_e5m2, float* slab_sum, float* ztgt,
+                        float* rowc, void* stream, uint32_t* status);
+
 // ---- softcapped cross entropy (ce.cu) -------------------------------------------------------------
 // One CTA per token row: z = A*sigmoid((logit+B)/C), loss = sum_k w_k (lse - z[t_{i+k}]) + w_p (lse - z[p_i]),
 // dlogits (e5m2 or bf16) = grad_mul * d loss / d logit.

@@ -254,6 +254,50 @@ std::vector<Tensor> softcap_ce(const Tensor& logits, const Tensor& targets, cons
   return {losses, dl};
 }
 
+// (q [rows, cols], qT [cols, rows]) saturating e4m3 of src / scale; either output on request
+std::vector<Tensor> quant_static_dual(const Tensor& src, double scale, bool want_plain, bool want_t) {
+  TORCH_CHECK(src.is_cuda() && src.dim() == 2 && src.is_contiguous() && src.scalar_type() == torch::kBFloat16);
+  c10::cuda::CUDAGuard guard(src.device());
+  Tensor q, qT;
+  if (want_plain) q = torch::empty(src.sizes(), src.options().dtype(torch::kFloat8_e4m3fn));
+  if (want_t) qT = torch::empty({src.size(1), src.size(0)}, src.options().dtype(torch::kFloat8_e4m3fn));
+  check(mng_quant_static_dual(src.data_ptr(), want_plain ? q.data_ptr() : nullptr, want_t ? qT.data_ptr() : nullptr, src.size(0),
+                              src.size(1), (float)scale, cur_stream()),
+        "mng_quant_static_dual");
+  g_launches += 1;
+  return {q, qT};
+}
+
+// losses [T] fp32, dlogits [T, V] e5m2 from x8 [T, K] and wT8 [V, K] (e4m3, logit = acc * alpha)
+std::vector<Tensor> lmhead_ce_fused(const Tensor& x8, const Tensor& wT8, double alpha, const Tensor& targets, const Tensor& mtp_weights,
+                                    const c10::optional<Tensor>& prefix_targets, const c10::optional<Tensor>& prefix_weight,
+                                    double A, double B, double C, double grad_mul) {
+  TORCH_CHECK(x8.is_cuda() && x8.dim() == 2 && x8.is_contiguous() && x8.scalar_type() == torch::kFloat8_e4m3fn);
+  TORCH_CHECK(wT8.dim() == 2 && wT8.is_contiguous() && wT8.scalar_type() == torch::kFloat8_e4m3fn && wT8.size(1) == x8.size(1));
+  TORCH_CHECK(targets.scalar_type() == torch::kInt64 && targets.is_contiguous() && targets.numel() == x8.size(0));
+  TORCH_CHECK(mtp_weights.scalar_type() == torch::kFloat32 && mtp_weights.is_contiguous());
+  c10::cuda::CUDAGuard guard(x8.device());
+  const int64_t T = x8.size(0), V = wT8.size(0), K = x8.size(1);
+  const long long* pt = nullptr;
+  if (prefix_targets.has_value() && prefix_targets->defined()) {
+    TORCH_CHECK(prefix_targets->scalar_type() == torch::kInt64 && prefix_targets->is_contiguous() && prefix_targets->numel() == T);
+    pt = reinterpret_cast<const long long*>(prefix_targets->data_ptr<int64_t>());
+  }
+  auto f32 = x8.options().dtype(torch::kFloat32);
+  Tensor losses = torch::empty({T}, f32);
+  Tensor dl = torch::empty({T, V}, x8.options().dtype(torch::kFloat8_e5m2));
+  const int64_t slabs = (V + 127) / 128;
+  Tensor slab = torch::empty({T * slabs}, f32), ztgt = torch::zeros({T * 4}, f32), rowc = torch::empty({T}, f32);
+  check(mng_lmhead_ce_fused(x8.data_ptr(), wT8.data_ptr(), (int)T, (int)V, (int)K, (float)alpha,
+                            reinterpret_cast<const long long*>(targets.data_ptr<int64_t>()), mtp_weights.data_ptr<float>(),
+                            (int)mtp_weights.numel(), pt, fptr(prefix_weight), (float)A, (float)B, (float)C, (float)grad_mul,
+                            losses.data_ptr<float>(), dl.data_ptr(), slab.data_ptr<float>(), ztgt.data_ptr<float>(),
+                            rowc.data_ptr<float>(), cur_stream(), status_ptr(x8)),
+        "mng_lmhead_ce_fused");
+  g_launches += 3;
+  return {losses, dl};
+}
+
 PeerPtrs peers_from(const std::vector<int64_t>& ptrs, int64_t self) {
   PeerPtrs p{};
   TORCH_CHECK(ptrs.size() >= 1 && ptrs.size() <= MNG_MAX_RANKS && self >= 0 && self < (int64_t)ptrs.size());
@@ -697,6 +741,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("quant_transpose", &quant_transpose);
   m.def("transpose_u8", &transpose_u8);
   m.def("softcap_ce", &softcap_ce);
+  m.def("quant_static_dual", &quant_static_dual);
+  m.def("lmhead_ce_fused", &lmhead_ce_fused);
   m.def("adam", &adam);
   m.def("nesterov", &nesterov);
   m.def("scale_by_norm", &scale_by_norm);

@@ -2,6 +2,7 @@
 #include "api.h"
 #include "gemm_sm100.cuh"
 #include "gemm_sm100_pair.cuh"
+#include "epi_ce.cuh"
 
 #include <cstdio>
 #include <cstring>
@@ -515,8 +516,10 @@ static int launch_pair(const GemmDesc& g, const typename Epi::Params& ep, int ma
   if (!B_MN) rc = cached_map(&maps.b, g.b, ES, g.K, g.N, g.batch, g.ldb, g.b_bstride, BK, 128);
   else rc = cached_map(&maps.b, g.b, ES, g.N, g.K, g.batch, g.ldb, g.b_bstride, 128 / ES, BK);
   if (rc) return rc - 1000;
-  rc = cached_map(&maps.out, g.out, 2, g.N, g.M, g.batch, g.ldc, g.c_bstride, 64, 32);
-  if (rc) return rc - 1100;
+  if (epi_store16<Epi>::value) {
+    rc = cached_map(&maps.out, g.out, 2, g.N, g.M, g.batch, g.ldc, g.c_bstride, 64, 32);
+    if (rc) return rc - 1100;
+  }
   if (Epi::kCin) {
     rc = cached_map(&maps.cin, g.cin, 2, g.N, g.M, g.batch, g.ldc, g.c_bstride, 64, 32);
     if (rc) return rc - 1200;
@@ -584,6 +587,33 @@ static int launch_store(const GemmDesc& g) {
 }  // namespace mng
 
 using namespace mng;
+
+// lm_head GEMM fused with the soft-capped cross entropy (epi_ce.cuh): x8 [T, K] e4m3, wT8 [V, K] e4m3 (both K-major),
+// logit = acc * alpha.  Writes losses [T] fp32 and dlogits [T, V] e5m2 (already multiplied by grad_mul).
+// Scratch owned by the caller: slab_sum [T * ceil(V / 128)], ztgt [T * 4], rowc [T] floats.
+extern "C" int mng_lmhead_ce_fused(const void* x8, const void* wT8, int T, int V, int K, float alpha, const long long* targets,
+                                   const float* mtp_w, int n_predict, const long long* prefix_targets, const float* prefix_w,
+                                   float A, float B, float C, float grad_mul, float* losses, void* dlogits_e5m2, float* slab_sum,
+                                   float* ztgt, float* rowc, void* stream, uint32_t* status) {
+  if (T <= 0 || V <= 0 || K <= 0 || (V % 32) || (K % 16) || n_predict < 1 || n_predict > CE_FUSED_TARGETS - 1) return -1;
+  GemmDesc g{};
+  g.a = x8; g.b = wT8; g.M = T; g.N = V; g.K = K; g.batch = 1;
+  g.dtype_a = g.dtype_b = MNG_E4M3;
+  g.lda = g.ldb = K;
+  g.ldc = V;
+  g.out8 = dlogits_e5m2;
+  g.stream = stream;
+  g.status = status;
+  CeEpiParams p{};
+  p.targets = targets; p.prefix_targets = prefix_targets; p.mtp_w = mtp_w; p.prefix_w = prefix_w; p.n_predict = n_predict;
+  p.alpha = alpha; p.A = A; p.half_inv_c = 0.5f / C; p.half_b_over_c = 0.5f * B / C; p.k2 = A * 1.4426950408889634f;
+  p.slab_sum = slab_sum; p.slabs = (V + 127) / 128; p.ztgt = ztgt; p.rowc = rowc; p.gscale = grad_mul * (A / C);
+  int rc = launch_pair<1, false, false, 0, 0, TEpiCeStats>(g, p, 0);
+  if (rc) return rc;
+  ce_finish_kernel<<<(unsigned)((T + 7) / 8), 256, 0, (cudaStream_t)stream>>>(p, losses, rowc, T, V);
+  if (cudaGetLastError() != cudaSuccess) return -4;
+  return launch_pair<1, false, false, 0, 0, TEpiCeGrad>(g, p, 0);
+}
 
 extern "C" int mng_gemm(const GemmDesc* gp) {
   const GemmDesc& g = *gp;

@@ -27,10 +27,21 @@
 //                                  uint4 (&out)[4], uint4 (&out8)[2], int batch, long long row, int col0, int M, int N);
 //     __device__ static void finish(const Params&, State&); }
 // acc[j] = element (row, col0 + j); cin / out hold the same 32 positions as bf16; out8 as e4m3.
+// Optional members (detected below): `static constexpr bool kStore16 = false` - no bf16 output at all (only the
+// 8-bit copy, or nothing); `static constexpr bool kTileHooks = true` - the epilogue keeps per-row state over the
+// 128 columns a warp owns in a tile: the kernel sets st.taddr to the TMEM address of the warp's 128-column slab and
+// calls tile_begin(ep, st, b, row, n0, M, N) before the four chunks (it may re-read single accumulator columns with
+// tmem_ld1 there), and tile_end(ep, st, b, row, n0, M, N) after them.  For these epilogues the chunk loop is
+// unrolled and the TMEM load of chunk c + 1 is in flight while chunk c is processed.
 #pragma once
 #include "gemm_sm100.cuh"
 
 namespace mng {
+
+template <class E, class = void> struct epi_store16 { static constexpr bool value = true; };
+template <class E> struct epi_store16<E, decltype((void)E::kStore16)> { static constexpr bool value = E::kStore16; };
+template <class E, class = void> struct epi_hooks { static constexpr bool value = false; };
+template <class E> struct epi_hooks<E, decltype((void)E::kTileHooks)> { static constexpr bool value = E::kTileHooks; };
 
 template <bool OUT8>
 struct GemmPairSmem {
@@ -63,6 +74,8 @@ gemm_tcgen05_pair_kernel(const __grid_constant__ PairMaps maps, GemmShape shape,
   constexpr int A_CHUNKS = GEMM_BM / CHUNK_ELEMS;
   constexpr int B_CHUNKS = BNH / CHUNK_ELEMS;
   constexpr uint32_t CHUNK_BYTES = BK * 128;
+  constexpr bool STORE16 = epi_store16<Epi>::value;
+  constexpr bool HOOKS = epi_hooks<Epi>::value;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -101,7 +114,7 @@ gemm_tcgen05_pair_kernel(const __grid_constant__ PairMaps maps, GemmShape shape,
     mbar_fence_init();
     tma_prefetch_desc(&maps.a);
     tma_prefetch_desc(&maps.b);
-    tma_prefetch_desc(&maps.out);
+    if constexpr (STORE16) tma_prefetch_desc(&maps.out);
     if constexpr (Epi::kCin) tma_prefetch_desc(&maps.cin);
     if constexpr (Epi::kOut8) tma_prefetch_desc(&maps.out8);
   }
@@ -235,23 +248,15 @@ gemm_tcgen05_pair_kernel(const __grid_constant__ PairMaps maps, GemmShape shape,
         cin_phase ^= 1;
       }
       tc_fence_after();
-      if constexpr (!Epi::kCin) {
+      if constexpr (!Epi::kCin && (STORE16 || Epi::kOut8)) {
         // the previous tile's bulk stores have had a whole tile of MMA time to read the staging boxes: waiting
         // here, not right after issuing them, keeps the warp from idling on the store engine
         if (lane == 0) tma_store_wait_read<0>();
         __syncwarp();
       }
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + half * 128;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(taddr + c * 32, v);
-        tmem_ld_wait();
-        if (c == 3) {                                          // everything this warp needs is in registers
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[acc]), 0));
-        }
+      // one chunk: registers -> epilogue functor -> staging boxes
+      auto do_chunk = [&](int c, const uint32_t (&v)[32]) {
         float f[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
@@ -263,20 +268,62 @@ gemm_tcgen05_pair_kernel(const __grid_constant__ PairMaps maps, GemmShape shape,
           for (int j = 0; j < 4; ++j) cin[j] = *reinterpret_cast<const uint4*>(rowp + (((cb + j) ^ sw) << 4));
         }
         Epi::apply(ep, est, f, cin, out, out8, b, (long long)m0 + lane, n0 + c * 32, shape.M, shape.N);
+        if constexpr (STORE16) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(rowp + (((cb + j) ^ sw) << 4)) = out[j];
+          for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(rowp + (((cb + j) ^ sw) << 4)) = out[j];
+        }
         if constexpr (Epi::kOut8) {
           uint8_t* rowp8 = stg + 2 * SM::BOX_BYTES + lane * 128;
 #pragma unroll
           for (int j = 0; j < 2; ++j) *reinterpret_cast<uint4*>(rowp8 + (((c * 2 + j) ^ sw) << 4)) = out8[j];
         }
+      };
+      auto release_acc = [&]() {                               // everything this warp needs is in registers
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[acc]), 0));
+      };
+      if constexpr (HOOKS) {
+        est.taddr = taddr;
+        Epi::tile_begin(ep, est, b, (long long)m0 + lane, n0, shape.M, shape.N);
+        uint32_t va[32], vb[32];
+        tmem_ld32(taddr, va);
+        tmem_ld_wait();
+        tmem_ld32(taddr + 32, vb);
+        do_chunk(0, va);
+        tmem_ld_wait();
+        tmem_ld32(taddr + 64, va);
+        do_chunk(1, vb);
+        tmem_ld_wait();
+        tmem_ld32(taddr + 96, vb);
+        do_chunk(2, va);
+        tmem_ld_wait();
+        release_acc();
+        do_chunk(3, vb);
+        Epi::tile_end(ep, est, b, (long long)m0 + lane, n0, shape.M, shape.N);
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tmem_ld32(taddr + c * 32, v);
+          tmem_ld_wait();
+          if (c == 3) release_acc();
+          do_chunk(c, v);
+        }
+      }
+      if constexpr (!(STORE16 || Epi::kOut8)) {                // nothing staged for the store engine: next tile
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+        continue;
       }
       fence_proxy_async_smem();                                // generic-proxy writes -> visible to the bulk stores
       __syncwarp();
       if (lane == 0) {
         if (m0 < shape.M) {
-          if (n0 < shape.N) tma_store_3d(&maps.out, stg, n0, m0, b);
-          if (n0 + 64 < shape.N) tma_store_3d(&maps.out, stg + SM::BOX_BYTES, n0 + 64, m0, b);
+          if constexpr (STORE16) {
+            if (n0 < shape.N) tma_store_3d(&maps.out, stg, n0, m0, b);
+            if (n0 + 64 < shape.N) tma_store_3d(&maps.out, stg + SM::BOX_BYTES, n0 + 64, m0, b);
+          }
           if constexpr (Epi::kOut8) {
             if (n0 < shape.N) tma_store_3d(&maps.out8, stg + 2 * SM::BOX_BYTES, n0, m0, b);
           }

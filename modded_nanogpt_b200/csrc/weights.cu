@@ -73,9 +73,49 @@ bank_grad_acc_kernel(const float* __restrict__ parts, int S, long long n, const 
   }
 }
 
+// Saturating e4m3 cast of src / scale (one static scale for the whole tensor, `train_gpt.py:78-79`) of a row-major
+// bf16 [rows, cols] matrix, written as is (q, may be null) and / or transposed (qT [cols, rows], may be null) in one
+// pass: 64 x 64 tiles through shared memory, 16-byte accesses on every side.  rows, cols multiples of 64.
+__global__ void __launch_bounds__(256)
+quant_static_dual_kernel(const __nv_bfloat16* __restrict__ src, uint8_t* __restrict__ q, uint8_t* __restrict__ qT, long long rows,
+                         long long cols, float inv_scale) {
+  __shared__ uint8_t tile[64][64 + 16];
+  const long long r0 = (long long)blockIdx.y * 64, c0 = (long long)blockIdx.x * 64;
+  const int a = threadIdx.x >> 2, seg = threadIdx.x & 3;            // row a of the tile, 16 columns from seg * 16
+  const __nv_bfloat16* sp = src + (r0 + a) * cols + c0 + seg * 16;
+  uint32_t w[4];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint4 u = reinterpret_cast<const uint4*>(sp)[h];
+    const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+    const float2 f0 = __bfloat1622float2(b2[0]), f1 = __bfloat1622float2(b2[1]);
+    const float2 f2 = __bfloat1622float2(b2[2]), f3 = __bfloat1622float2(b2[3]);
+    w[2 * h] = (uint32_t)pack_e4m3x2(f0.x * inv_scale, f0.y * inv_scale) | ((uint32_t)pack_e4m3x2(f1.x * inv_scale, f1.y * inv_scale) << 16);
+    w[2 * h + 1] = (uint32_t)pack_e4m3x2(f2.x * inv_scale, f2.y * inv_scale) | ((uint32_t)pack_e4m3x2(f3.x * inv_scale, f3.y * inv_scale) << 16);
+  }
+  const uint4 packed = make_uint4(w[0], w[1], w[2], w[3]);
+  if (q) *reinterpret_cast<uint4*>(q + (r0 + a) * cols + c0 + seg * 16) = packed;
+  if (qT) {
+    *reinterpret_cast<uint4*>(&tile[a][seg * 16]) = packed;
+    __syncthreads();
+    uint8_t v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = tile[seg * 16 + j][a];
+    *reinterpret_cast<uint4*>(qT + (c0 + a) * rows + r0 + seg * 16) = *reinterpret_cast<const uint4*>(v);
+  }
+}
+
 }  // namespace mng
 
 using namespace mng;
+
+extern "C" int mng_quant_static_dual(const void* src, void* q, void* qT, long long rows, long long cols, float scale, void* stream) {
+  if (rows <= 0 || cols <= 0 || (rows % 64) || (cols % 64) || rows / 64 > 65535 || scale <= 0.f) return -1;
+  dim3 grid((unsigned)(cols / 64), (unsigned)(rows / 64));
+  quant_static_dual_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>((const __nv_bfloat16*)src, (uint8_t*)q, (uint8_t*)qT, rows, cols,
+                                                                   1.f / scale);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
 
 // parts: [S, n] fp32; W: [n] bf16; g0 covers elements [0, n0), g1 (may be null when n0 == n) the rest.
 // partials: `BANK_GRAD_BLOCKS` floats of scratch; counter: one zero-initialised word that the kernel leaves at zero.

@@ -426,14 +426,33 @@ class _SoftcapCE(torch.autograd.Function):
     def forward(ctx, x, w, targets, mtp_weights, prefix_targets, prefix_weight, a, b, c, grad_scale, fp8, scales):
         C = _C()
         x_s, w_s, grad_s = scales
+        if fp8 and CE_FUSED and _ce_fusable(x, w, mtp_weights):
+            # no [T, V] logits in memory: the lm_head GEMM runs twice with the loss statistics and then the gradient
+            # formed in its epilogues (csrc/epi_ce.cuh); the weight is quantised once, as stored and transposed
+            x8, xT8 = C.quant_static_dual(x, x_s, True, True)
+            w8, wT8 = C.quant_static_dual(w.contiguous(), w_s, True, True)
+            g_s = grad_s * grad_scale
+            losses, dl = C.lmhead_ce_fused(x8, wT8, x_s * w_s, targets, mtp_weights, prefix_targets, prefix_weight, a, b, c,
+                                           grad_scale / g_s)
+            ctx.save_for_backward(xT8, w8, dl)
+            ctx.cfg = (True, x_s, w_s, g_s)
+            ctx.x_is_t = True
+            return losses
+        ctx.x_is_t = False
         if fp8:
-            x8 = quant_static_e4m3(x, x_s)
-            w8 = quant_static_e4m3(w, w_s)
+            if x.shape[0] % 64 == 0 and x.shape[1] % 64 == 0 and w.shape[1] % 64 == 0:
+                # one pass each: e4m3 of x as stored (logits GEMM) and transposed (weight-gradient GEMM), e4m3 of w
+                x8, xs8 = C.quant_static_dual(x, x_s, True, True)
+                w8, _ = C.quant_static_dual(w.contiguous(), w_s, True, False)
+                ctx.x_is_t = True
+            else:
+                x8 = xs8 = quant_static_e4m3(x, x_s)
+                w8 = quant_static_e4m3(w, w_s)
             logits = gemm(x8, w8, b_mn=True, alpha=x_s * w_s)
             g_s = grad_s * grad_scale
             losses, dl = C.softcap_ce(logits, targets, mtp_weights, prefix_targets, prefix_weight, True, a, b, c,
                                       grad_scale / g_s)
-            ctx.save_for_backward(x8, w8, dl)
+            ctx.save_for_backward(xs8, w8, dl)
             ctx.cfg = (True, x_s, w_s, g_s)
         else:
             logits = gemm(x.contiguous(), w, b_mn=True)
@@ -451,7 +470,9 @@ class _SoftcapCE(torch.autograd.Function):
         if fp8:
             # 8-bit MN-major operands run at about 60 % of the K-major rate on both sides: transposing the small
             # [T, D] activation (38 MB) first makes A K-major and the GEMM 1.6x faster
-            if xq.shape[0] % 64 == 0 and xq.shape[1] % 64 == 0:
+            if ctx.x_is_t:
+                xt = xq
+            elif xq.shape[0] % 64 == 0 and xq.shape[1] % 64 == 0:
                 xt = _C().transpose_u8(xq)
             else:
                 xt = xq.view(torch.uint8).t().contiguous().view(xq.dtype)
@@ -459,6 +480,17 @@ class _SoftcapCE(torch.autograd.Function):
         else:
             dw = gemm(xq, dl, a_mn=True, b_mn=True, alpha=x_s * g_s)
         return dx, dw, None, None, None, None, None, None, None, None, None, None
+
+
+# 1: form loss and gradient in the epilogues of the lm_head GEMM (no [T, V] logits in memory: 4.9 GB less at T = 49,152).
+# Off by default: the two fused passes measure 1.9 + 2.8 ms on B200 against 2.0 + 1.9 ms for the logits GEMM plus the
+# stand-alone loss kernel (their epilogues are bound by instruction issue with two epilogue warps per scheduler).
+CE_FUSED = os.environ.get("MNG_CE_FUSED", "0") == "1"
+
+
+def _ce_fusable(x: Tensor, w: Tensor, mtp_weights: Tensor) -> bool:
+    return (x.shape[0] % 64 == 0 and x.shape[1] % 64 == 0 and w.shape[1] % 64 == 0 and x.shape[0] >= 256
+            and mtp_weights.numel() <= 3)
 
 
 def softcap_ce(x, w, targets, mtp_weights, prefix_targets, prefix_weight, a, b, c, grad_scale=1.0, fp8=True,
