@@ -2,6 +2,7 @@
 
     python build_ext.py            # incremental
     python build_ext.py --force    # rebuild everything
+    python build_ext.py --debug    # also build `_Cdbg*.so` with -DMNG_BOUNDS_CHECK (index checks that record, never trap)
 
 Each .cu file is compiled by nvcc with `-gencode arch=compute_100a,code=sm_100a -lineinfo` (no
 PyTorch headers, so this takes seconds and cross-compiles without a GPU); `binding.cpp` is the
@@ -38,12 +39,15 @@ def _run(cmd):
     return r.stdout
 
 
-def target_path() -> Path:
+def target_path(name: str = "_C") -> Path:
     suffix = sysconfig.get_config_var("EXT_SUFFIX") or ".so"
-    return ROOT / "modded_nanogpt_b200" / f"_C{suffix}"
+    return ROOT / "modded_nanogpt_b200" / f"{name}{suffix}"
 
 
-def build(force: bool = False, verbose: bool = True) -> Path:
+def build(force: bool = False, verbose: bool = True, debug: bool = False) -> Path:
+    """`debug=True` builds the bounds-checked variant `_Cdbg` (same sources, -DMNG_BOUNDS_CHECK) next to `_C`."""
+    name = "_Cdbg" if debug else "_C"
+    defs = ["-DMNG_BOUNDS_CHECK"] if debug else []
     import torch
     from torch.utils import cpp_extension as ce
 
@@ -54,19 +58,19 @@ def build(force: bool = False, verbose: bool = True) -> Path:
     hdr_digest = _digest(headers)
     jobs, objs = [], []
     for f in cu_files:
-        tag = _digest([f], hdr_digest + "nvcc")
+        tag = _digest([f], hdr_digest + "nvcc" + name)
         o = BUILD / f"{f.stem}.{tag}.o"
         objs.append(o)
         if force or not o.exists():
-            jobs.append([NVCC, *ARCH, "-lineinfo", "-O3", "-std=c++17", "--use_fast_math", "-Xcompiler", "-fPIC",
+            jobs.append([NVCC, *ARCH, "-lineinfo", "-O3", "-std=c++17", "--use_fast_math", "-Xcompiler", "-fPIC", *defs,
                          "-I", str(SRC), "-c", str(f), "-o", str(o)])
     inc = [a for p in ce.include_paths("cuda") for a in ("-I", p)]
     for f in cpp_files:
-        tag = _digest([f], hdr_digest + torch.__version__)
+        tag = _digest([f], hdr_digest + torch.__version__ + name)
         o = BUILD / f"{f.stem}.{tag}.o"
         objs.append(o)
         if force or not o.exists():
-            jobs.append(["g++", "-O2", "-std=c++17", "-fPIC", "-DTORCH_EXTENSION_NAME=_C", "-DTORCH_API_INCLUDE_EXTENSION_H",
+            jobs.append(["g++", "-O2", "-std=c++17", "-fPIC", f"-DTORCH_EXTENSION_NAME={name}", "-DTORCH_API_INCLUDE_EXTENSION_H", *defs,
                          f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}", *inc,
                          "-I", sysconfig.get_paths()["include"], "-I", str(SRC), "-c", str(f), "-o", str(o)])
     if jobs:
@@ -74,8 +78,8 @@ def build(force: bool = False, verbose: bool = True) -> Path:
             print(f"[build_ext] compiling {len(jobs)} file(s) for sm_100a", flush=True)
         with ThreadPoolExecutor(max_workers=min(8, len(jobs))) as ex:
             list(ex.map(_run, jobs))
-    out = target_path()
-    stamp = BUILD / "link.stamp"
+    out = target_path(name)
+    stamp = BUILD / f"link{name}.stamp"
     want = " ".join(o.name for o in objs)
     if force or jobs or not out.exists() or not stamp.exists() or stamp.read_text() != want:
         libdirs = ce.library_paths("cuda")
@@ -92,3 +96,5 @@ def build(force: bool = False, verbose: bool = True) -> Path:
 
 if __name__ == "__main__":
     build(force="--force" in sys.argv)
+    if "--debug" in sys.argv:
+        build(force="--force" in sys.argv, debug=True)

@@ -189,7 +189,14 @@ int mng_dc_mix_bwd(const float* dM, const void* P, const void* a, const void* w1
 
 // ---- embedding backward (embed.cu): grad[sorted_ids[j], :] += g[perm[j], :], accumulated in place (bf16) ----
 int mng_embed_bwd(const void* g, const long long* sorted_ids, const long long* perm, void* grad, long long n, int D,
-                  void* stream);
+                  long long table_rows, void* stream);
+
+// Debug build (-DMNG_BOUNDS_CHECK): source line of the last out-of-range index seen by the kernels of a translation
+// unit since the previous query (0 = none; always 0 in the regular build).
+unsigned int mng_bounds_embed(void);
+unsigned int mng_bounds_glue(void);
+unsigned int mng_bounds_dc(void);
+unsigned int mng_bounds_optim(void);
 
 // ---- attention forward (attn_sm100.cu) ------------------------------------------------------------------
 // q, k, v: [T, H, 128] bf16 with token stride `row_stride` elements (heads contiguous); doc_start[i] = first token of

@@ -611,7 +611,7 @@ void embed_bwd(const Tensor& g, const Tensor& sorted_ids, const Tensor& perm, Te
   c10::cuda::CUDAGuard guard(g.device());
   check(mng_embed_bwd(g.data_ptr(), reinterpret_cast<const long long*>(sorted_ids.data_ptr<int64_t>()),
                       reinterpret_cast<const long long*>(perm.data_ptr<int64_t>()), grad.data_ptr(), g.size(0), (int)g.size(1),
-                      cur_stream()),
+                      grad.size(0), cur_stream()),
         "mng_embed_bwd");
   g_launches += 1;
 }
@@ -723,6 +723,21 @@ std::vector<Tensor> gate_tail_bwd(const Tensor& pre, const Tensor& W2, const Ten
   return {dpre, dW2, db2, dscale};
 }
 
+// Debug build only: the largest source line at which a kernel saw an out-of-range index since the last call (0 = none).
+int64_t bounds_status() {
+  cudaDeviceSynchronize();
+  unsigned int v = 0;
+  for (unsigned int w : {mng_bounds_embed(), mng_bounds_glue(), mng_bounds_dc(), mng_bounds_optim()}) v = w > v ? w : v;
+  return (int64_t)v;
+}
+bool bounds_checked_build() {
+#ifdef MNG_BOUNDS_CHECK
+  return true;
+#else
+  return false;
+#endif
+}
+
 Tensor status_tensor(const Tensor& like) {
   status_ptr(like);
   return g_status;
@@ -765,5 +780,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gate_tail_fwd", &gate_tail_fwd);
   m.def("gate_tail_bwd", &gate_tail_bwd);
   m.def("status_tensor", &status_tensor);
+  m.def("bounds_status", &bounds_status);
+  m.def("bounds_checked_build", &bounds_checked_build);
   m.def("launch_count", &launch_count);
 }

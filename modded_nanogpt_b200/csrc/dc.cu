@@ -22,7 +22,8 @@ dc_mix_fwd_kernel(const float* __restrict__ S, const __nv_bfloat16* __restrict__
   if (t >= T) return;
   const long long blk = t >> 7;
   const long long k0 = blk * 128 - 128;              // key position of column 0
-  const int ds = doc_start[t];
+  int ds = doc_start[t];
+  if (!MNG_IN_RANGE(ds, t + 1)) ds = (int)t;                  // debug build only: a document cannot start after its token
   const long long head_stride = T * DC_R;            // nblk*128*256
   bool valid[8];
 #pragma unroll
@@ -109,6 +110,8 @@ dc_mix_bwd_kernel(const float* __restrict__ dM, const __nv_bfloat16* __restrict_
 }  // namespace mng
 
 using namespace mng;
+
+MNG_DEFINE_BOUNDS_QUERY(dc)
 
 extern "C" int mng_dc_mix_fwd(const float* S, const void* w1, const int* doc_start, void* P, void* a, long long T, int H,
                               int window, void* stream) {

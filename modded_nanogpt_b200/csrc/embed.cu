@@ -35,7 +35,8 @@ __device__ __forceinline__ void emb_flush(__nv_bfloat16* dst, const float (&acc)
 
 // blockDim.x = D / 8 (each thread owns 8 consecutive columns)
 __global__ void embed_bwd_kernel(const __nv_bfloat16* __restrict__ g, const long long* __restrict__ sorted_ids,
-                                 const long long* __restrict__ perm, __nv_bfloat16* __restrict__ grad, long long n, int D) {
+                                 const long long* __restrict__ perm, __nv_bfloat16* __restrict__ grad, long long n, int D,
+                                 long long table_rows) {
   const long long begin = (long long)blockIdx.x * EMB_CHUNK;
   const long long end = begin + EMB_CHUNK < n ? begin + EMB_CHUNK : n;
   const int col = threadIdx.x * 8;
@@ -50,6 +51,7 @@ __global__ void embed_bwd_kernel(const __nv_bfloat16* __restrict__ g, const long
       const long long jj = j + u < end ? j + u : end - 1;
       id[u] = sorted_ids[jj];
       src[u] = perm[jj];
+      if (!MNG_IN_RANGE(src[u], n)) src[u] = 0;               // debug build only: a bad permutation entry reads row 0
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const uint4*>(g + src[u] * D + col);
@@ -57,7 +59,7 @@ __global__ void embed_bwd_kernel(const __nv_bfloat16* __restrict__ g, const long
     for (int u = 0; u < 4; ++u) {
       if (j + u >= end) break;
       if (id[u] != cur) {
-        emb_flush(grad + cur * D + col, acc, open_left);
+        if (MNG_IN_RANGE(cur, table_rows)) emb_flush(grad + cur * D + col, acc, open_left);
 #pragma unroll
         for (int t = 0; t < 8; ++t) acc[t] = 0.f;
         cur = id[u];
@@ -72,17 +74,19 @@ __global__ void embed_bwd_kernel(const __nv_bfloat16* __restrict__ g, const long
     }
   }
   const bool open_right = end < n && sorted_ids[end] == cur;
-  emb_flush(grad + cur * D + col, acc, open_left || open_right);
+  if (MNG_IN_RANGE(cur, table_rows)) emb_flush(grad + cur * D + col, acc, open_left || open_right);
 }
 
 }  // namespace mng
 
+MNG_DEFINE_BOUNDS_QUERY(embed)
+
 extern "C" int mng_embed_bwd(const void* g, const long long* sorted_ids, const long long* perm, void* grad, long long n, int D,
-                             void* stream) {
+                             long long table_rows, void* stream) {
   if (n == 0) return 0;
   if (D % 8 || D / 8 > 1024) return -1;
   const unsigned grid = (unsigned)((n + mng::EMB_CHUNK - 1) / mng::EMB_CHUNK);
   mng::embed_bwd_kernel<<<grid, D / 8, 0, (cudaStream_t)stream>>>((const __nv_bfloat16*)g, sorted_ids, perm,
-                                                                   (__nv_bfloat16*)grad, n, D);
+                                                                   (__nv_bfloat16*)grad, n, D, table_rows);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }

@@ -45,7 +45,7 @@ lincomb_fwd_kernel(LinCombArgs a, __nv_bfloat16* __restrict__ out, long long row
   for (int j = 0; j < a.k; ++j) {
     const LinTerm& tm = a.t[j];
     float c = tm.scalar ? *tm.scalar : 1.f;
-    if (tm.gate) c *= gate_at(tm.gate, tm.gate_bf16, row * tm.gate_stride + tm.gate_col);
+    if (tm.gate && MNG_IN_RANGE(tm.gate_col, tm.gate_stride)) c *= gate_at(tm.gate, tm.gate_bf16, row * tm.gate_stride + tm.gate_col);
     c += tm.addc;
     const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(tm.x) + row * cols;
 #pragma unroll
@@ -454,6 +454,8 @@ using namespace mng;
     else KERNEL<4><<<grid, LC_WARPS * 32, 0, (cudaStream_t)stream>>>(__VA_ARGS__);                     \
     return cudaGetLastError() == cudaSuccess ? 0 : -2;                                                 \
   } while (0)
+
+MNG_DEFINE_BOUNDS_QUERY(glue)
 
 extern "C" int mng_lincomb_fwd(const LinCombArgs* a, void* out, long long rows, int cols, void* stream) {
   if (rows == 0) return 0;

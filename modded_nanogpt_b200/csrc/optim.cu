@@ -47,7 +47,7 @@ adam_kernel(PeerPtrs grads, PeerPtrs params, long long off, float* __restrict__ 
 #pragma unroll
     for (int r = 0; r < MNG_MAX_RANKS; ++r) {
       if (r < grads.n) {
-        if (row_mask && row_mask[r * mask_stride + row] == 0)
+        if (row_mask && MNG_IN_RANGE(row, mask_stride) && row_mask[r * mask_stride + row] == 0)
           raw[r] = make_uint4(0u, 0u, 0u, 0u);               // rank r did not touch this row: nothing crosses NVLink
         else
           raw[r] = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(grads.p[r]) + e * (F32 ? 4 : 2));
@@ -320,6 +320,8 @@ static inline unsigned grid_for(long long nvec) {
 }  // namespace mng
 
 using namespace mng;
+
+MNG_DEFINE_BOUNDS_QUERY(optim)
 
 extern "C" int mng_adam(const AdamDesc* d, void* stream) {
   const AdamDesc& a = *d;

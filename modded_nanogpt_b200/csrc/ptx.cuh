@@ -23,6 +23,28 @@ enum : uint32_t {
   ERR_BAD_ARG = 6,
 };
 
+// ---- debug build: index checks ---------------------------------------------------------------------
+// With -DMNG_BOUNDS_CHECK every data-dependent index that goes through MNG_IN_RANGE is compared with its limit; a
+// bad one records the source line in a per-translation-unit device word and the access is skipped (never a trap:
+// the context stays usable).  MNG_DEFINE_BOUNDS_QUERY(name) defines `mng_bounds_<name>()`, which returns that word
+// (0 = every index was in range) and clears it.  In the regular build the macro is `true` and costs nothing.
+#ifdef MNG_BOUNDS_CHECK
+static __device__ unsigned int mng_bounds_word;
+#define MNG_IN_RANGE(i, n) \
+  (((long long)(i) >= 0 && (long long)(i) < (long long)(n)) ? true : (atomicMax(&mng_bounds_word, (unsigned int)__LINE__), false))
+#define MNG_DEFINE_BOUNDS_QUERY(name)                                        \
+  extern "C" unsigned int mng_bounds_##name() {                              \
+    unsigned int v = 0, z = 0;                                               \
+    cudaMemcpyFromSymbol(&v, mng::mng_bounds_word, sizeof(v));               \
+    cudaMemcpyToSymbol(mng::mng_bounds_word, &z, sizeof(z));                 \
+    return v;                                                                \
+  }
+#else
+#define MNG_IN_RANGE(i, n) true
+#define MNG_DEFINE_BOUNDS_QUERY(name) \
+  extern "C" unsigned int mng_bounds_##name() { return 0; }
+#endif
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -35,3 +35,26 @@ def test_log_stats(tmp_path):
     assert abs(ls.t_cdf(0.0, 7) - 0.5) < 1e-12 and abs(ls.t_cdf(2.0, 10) - 0.963306) < 1e-4 and abs(ls.t_cdf(-1.0, 3) - 0.195501) < 1e-4
     t, df, p = ls.welch([1.0, 1.1, 0.9, 1.05], [1.5, 1.6, 1.4, 1.55])
     assert t < 0 and p < 0.01 and 3 < df <= 6 and not math.isnan(p)
+
+
+def test_loss_curve_figures(tmp_path):
+    from modded_nanogpt_b200.utils import figures as fg
+    for name, off in (("a", 0.0), ("b", 0.01)):
+        d = tmp_path / name
+        d.mkdir()
+        for i in range(3):
+            lines = [f"step:{s}/1285 val_loss:{10.8 - 7.5 * (s / 1285) ** 0.5 + off + 0.001 * i:.4f} train_time:{60 * s}ms step_avg:60.00ms"
+                     for s in (0, 250, 500, 750, 1000, 1250, 1285)]
+            (d / f"run{i}.txt").write_text("code\n" + "\n".join(lines) + "\n")
+    (tmp_path / "a" / "run2.txt").write_text("step:0/1285 val_loss:10.8 train_time:0ms step_avg:0ms\n")   # a run cut short
+    ca = fg.average_runs(str(tmp_path / "a"))
+    assert [s for s, *_ in ca] == [0]                                   # only steps every run reached are averaged
+    (tmp_path / "a" / "run2.txt").unlink()
+    ca, cb = fg.average_runs(str(tmp_path / "a")), fg.average_runs(str(tmp_path / "b"))
+    assert [s for s, *_ in ca] == [0, 250, 500, 750, 1000, 1250, 1285] and abs(ca[-1][1] - (3.3 + 0.0005)) < 1e-3
+    assert abs(cb[-1][1] - ca[-1][1] - 0.0095) < 1e-3 and ca[-1][2] == 77.1
+    assert fg._ticks(0, 1285) == [0, 250, 500, 750, 1000, 1250] and fg._ticks(3.2, 3.4, 4) == [3.2, 3.25, 3.3, 3.35, 3.4]
+    svg = fg.render_svg({"run a": ca, "run b": cb}, x="time", target=3.28, y_max=6.0)
+    assert svg.startswith("<svg") and svg.count("<path") == 2 and "target 3.28" in svg and "run b (final" in svg
+    import xml.dom.minidom
+    xml.dom.minidom.parseString(svg)                                    # well-formed
