@@ -11,7 +11,7 @@ Design differences from the reference file: weights live in the same parameter-b
 track-1 model (`attn_bank` [4*L padded, D, D] = Q,K,V,O per layer; `mlp_bank` [L, 2, 4D, D]), the
 head is stored transposed (D, V) and tied to `embed` through the optimizer, so the same
 `NorMuonAndAdam`, fused collectives and FP8 head/MLP kernels serve both tracks.  The small (8,16) gate
-matrices are Adam parameters here (the reference orthogonalises them with NorMuon).
+matrices are NorMuon parameters as in the reference, stacked into two banks padded to the rank count.
 `reference_state_dict()` / `load_reference_state_dict()` convert to and from the reference's
 per-module key layout (`blocks.{i}.attn.qkvo_w`, `blocks.{i}.mlp.c_fc`, `lm_head.weight` (V, D), ...).
 """
@@ -91,8 +91,13 @@ class GPTMedium(nn.Module):
             qkv = self.attn_bank[:4 * L].view(L, 4, D, D)
             qkv[:, :3].uniform_(-b_attn, b_attn)               # O projections stay zero
             self.mlp_bank[:L, 0].uniform_(-b_mlp, b_mlp)       # down projections stay zero
-        self.attn_gate_bank = nn.Parameter(torch.zeros(L, H, 16))
-        self.value_embed_gate_bank = nn.Parameter(torch.zeros(len(VE_LAYERS), H, 16))
+        # the small gate matrices are NorMuon parameters, as in the reference (`train_gpt_medium.py:1478`, groups padded
+        # to a multiple of the rank count, `:524-543`): whole (H, 16) matrices are sharded over the ranks
+        ag, vg = next_multiple_of_n(L, n=world_size), next_multiple_of_n(len(VE_LAYERS), n=world_size)
+        self.attn_gate_bank = nn.Parameter(torch.zeros(ag, H, 16))
+        self.attn_gate_bank.reshape = (ag, H, 16)
+        self.value_embed_gate_bank = nn.Parameter(torch.zeros(vg, H, 16))
+        self.value_embed_gate_bank.reshape = (vg, H, 16)
         self.smear_gate = _Weight(1, 16)
         self.skip_gates = nn.Parameter(torch.zeros(3, 1, 16))
         self.x0_lambdas = nn.Parameter(torch.zeros(2 * L))
@@ -136,15 +141,16 @@ class GPTMedium(nn.Module):
             "attn_bank": {"optim": "normuon", "comms": "sharded", "adam_betas": None},
             "mlp_bank": {"optim": "normuon", "comms": "sharded", "adam_betas": None},
             "scalars": {"optim": "adam", "comms": "replicated", "adam_betas": [0.9, 0.99], "lr_mul": 10.0, "wd_mul": 0.0},
-            "attn_gate_bank": adam(comms="replicated", lr_mul=0.1), "value_embed_gate_bank": adam(comms="replicated", lr_mul=0.1),
+            "attn_gate_bank": {"optim": "normuon", "comms": "sharded", "adam_betas": None, "lr_mul": 0.1},
+            "value_embed_gate_bank": {"optim": "normuon", "comms": "sharded", "adam_betas": None, "lr_mul": 0.1},
             "smear_gate": adam(comms="replicated", lr_mul=0.01, wd_mul=0.0), "skip_gates": adam(comms="replicated", lr_mul=0.01, wd_mul=0.0),
             "x0_lambdas": adam(comms="replicated", lr_mul=5.0, wd_mul=0.0),
             "lm_head": adam(comms="sharded", wd_mul=150.0), "value_embeds": adam(comms="sharded", lr_mul=75.0, wd_mul=5.0),
             "embed2": adam(comms="sharded", lr_mul=75.0, wd_mul=5.0), "embed": adam(comms="sharded", wd_mul=150.0),
         }
 
-    WORK_ORDER = ["scalars", "smear_gate", "skip_gates", "x0_lambdas", "attn_gate_bank", "value_embed_gate_bank",
-                  "value_embeds", "embed2", "lm_head", "embed", "attn_bank", "mlp_bank"]
+    WORK_ORDER = ["scalars", "smear_gate", "skip_gates", "x0_lambdas", "value_embeds", "embed2", "lm_head", "embed",
+                  "attn_gate_bank", "value_embed_gate_bank", "attn_bank", "mlp_bank"]
 
     # -- forward ---------------------------------------------------------------------------------
     def forward(self, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, bigram_input_seq: Tensor | None,

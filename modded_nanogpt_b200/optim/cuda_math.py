@@ -58,11 +58,21 @@ class CudaMath(TorchMath):
             X, Y = Y, X
         return X
 
+    @staticmethod
+    def kernel_shapes(rows: int, cols: int) -> bool:
+        """Matrices the tcgen05 / row kernels take: at least one 128-byte operand row per side and whole 16-byte
+        vectors per matrix.  Smaller ones (the (8, 16) gate matrices of track 2) use the PyTorch statement of the
+        same update; their cost is negligible."""
+        return min(rows, cols) >= 64 and (rows * cols) % 256 == 0
+
     def normuon_direction(self, grad_chunk: Tensor, state: dict, cfg: ParamConfig, grad_ptrs=None, off: int = 0,
                           grad_mul: float = 1.0) -> Tensor:
         C = lib()
         buf = state["momentum_buffer"]
         shape = buf.shape
+        if not self.kernel_shapes(shape[-2], shape[-1]):
+            assert grad_ptrs is None, "tiny matrices are reduced by the collective library, not by the fused kernels"
+            return super().normuon_direction(grad_chunk, state, cfg)
         X = self._buf(("X", cfg.label), shape, torch.bfloat16, buf.device)
         ss = self._buf(("ss", cfg.label), (shape[0],), torch.float32, buf.device)
         if grad_ptrs is None:
@@ -75,6 +85,9 @@ class CudaMath(TorchMath):
     def normuon_apply(self, p_slice: Tensor, state: dict, v: Tensor, cfg: ParamConfig, param_ptrs=None, off: int = 0) -> None:
         C = lib()
         mats, rows, cols = v.shape
+        if not self.kernel_shapes(rows, cols):
+            assert param_ptrs is None
+            return super().normuon_apply(p_slice, state, v, cfg)
         red_rows = rows >= cols
         eff_wd = cfg.wd_mul * cfg.weight_decay * cfg.lr
         mul = cfg.per_matrix_lr_mul or [1.0] * mats

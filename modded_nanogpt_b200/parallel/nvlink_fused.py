@@ -112,7 +112,7 @@ class NvlinkCollectives(TorchCollectives):
         if cfg.label not in self.offsets:
             return False
         if cfg.optim == "normuon":
-            return True
+            return self.math.kernel_shapes(cfg.reshape[-2], cfg.reshape[-1])      # tiny matrices: collective library
         po, _ = self.offsets[cfg.label]
         # shard length in elements must keep 16-byte vectors aligned
         return cfg.label in self._adam_ok
