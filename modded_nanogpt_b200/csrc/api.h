@@ -31,6 +31,9 @@ typedef struct {
   const float* alpha2_ptr;            // a second one (STORE, DPRE)
   const float* beta_ptr;              // optional device scalar folded into beta (STORE)
   float* dot_out;                     // DPRE: *dot_out += sum(acc * post) over the whole product (fp32 atomics), or null
+  void* out2;                         // epilogues that split the N columns over several [M, out_cols] outputs
+  void* out3;
+  int out_cols;
   const float* row_scale;
   const float* col_scale;
   void* out8;                         // RELU2: e4m3 copy of the output
@@ -83,6 +86,18 @@ int mng_lmhead_ce_fused(const void* x8, const void* wT8, int T, int V, int K, fl
                         const float* mtp_w, int n_predict, const long long* prefix_targets, const float* prefix_w, float A,
                         float B, float C, float grad_mul, float* losses, void* dlogits_e5m2, float* slab_sum, float* ztgt,
                         float* rowc, void* stream, uint32_t* status);
+
+// QKV projection with the attention pre-processing in its epilogue (epi_qkv.cuh): x [T, K] bf16, w [3*H*128, K] bf16
+// (rows ordered q heads, k heads, v heads) -> q, k, v [T, H*128] bf16, rstd_q / rstd_k [T, H] fp32, k_last [H, 64] bf16.
+// lam: device scalar multiplied into the projection; cos_t / sin_t: fp32 [positions, 32]; ve / vgate optional.
+int mng_qkv_proj(const void* x, const void* w, int T, int K, int H, const float* lam, const float* cos_t, const float* sin_t,
+                 const void* ve, const void* vgate, int vgate_stride, void* q, void* k, void* v, float* rstd_q, float* rstd_k,
+                 void* k_last, int paired, int key_offset, void* stream, uint32_t* status);
+// Backward of the pre-processing from its outputs (no copy of the raw projection is kept): d_qkv [T, 3*H*128].
+int mng_qkv_post_bwd_from_out(const void* q, const void* k, const void* k_last, const float* cos_t, const float* sin_t,
+                              const float* rstd_q, const float* rstd_k, const void* dq, const void* dk, const void* dv,
+                              const void* ve, const void* vgate, int vgate_stride, void* d_qkv, void* d_ve, void* d_vgate,
+                              int d_vgate_stride, long long T, int H, int paired, int key_offset, void* stream);
 
 // ---- softcapped cross entropy (ce.cu) -------------------------------------------------------------
 // One CTA per token row: z = A*sigmoid((logit+B)/C), loss = sum_k w_k (lse - z[t_{i+k}]) + w_p (lse - z[p_i]),

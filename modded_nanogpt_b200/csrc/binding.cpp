@@ -505,6 +505,56 @@ std::vector<Tensor> qkv_post_bwd(const Tensor& qkv, const Tensor& cos_t, const T
   return {dqkv, dve, dvg};
 }
 
+// QKV projection with norm / rotary / key offset / value-embedding add in the GEMM epilogue.
+// Returns q, k, v [T, H, 128], rstd_q, rstd_k [T*H], k_last [H, 64].
+std::vector<Tensor> qkv_proj(const Tensor& x, const Tensor& w, const Tensor& lam, const Tensor& cos_t, const Tensor& sin_t,
+                             const OptT& ve, const OptT& vgate, int64_t H, bool paired, bool key_offset) {
+  TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous() && x.scalar_type() == torch::kBFloat16);
+  TORCH_CHECK(w.dim() == 2 && w.is_contiguous() && w.scalar_type() == torch::kBFloat16 && w.size(0) == 3 * H * 128 && w.size(1) == x.size(1));
+  TORCH_CHECK(cos_t.scalar_type() == torch::kFloat32 && cos_t.is_contiguous() && cos_t.size(1) == 32 && sin_t.sizes() == cos_t.sizes());
+  const int64_t T = x.size(0);
+  TORCH_CHECK(cos_t.size(0) >= (paired ? 2 * T : T));
+  c10::cuda::CUDAGuard guard(x.device());
+  auto o = x.options();
+  Tensor q = torch::empty({T, H, 128}, o), k = torch::empty({T, H, 128}, o), v = torch::empty({T, H, 128}, o);
+  Tensor rq = torch::empty({T * H}, o.dtype(torch::kFloat32)), rk = torch::empty({T * H}, o.dtype(torch::kFloat32));
+  Tensor k_last = torch::zeros({H, 64}, o);
+  int vstride = 0;
+  if (vgate.has_value() && vgate->defined()) {
+    TORCH_CHECK(vgate->scalar_type() == torch::kBFloat16 && vgate->stride(1) == 1 && vgate->size(1) >= H);
+    vstride = (int)vgate->stride(0);
+  }
+  if (ve.has_value() && ve->defined()) TORCH_CHECK(ve->is_contiguous() && ve->numel() == T * H * 128 && ve->scalar_type() == torch::kBFloat16);
+  check(mng_qkv_proj(x.data_ptr(), w.data_ptr(), (int)T, (int)x.size(1), (int)H, fptr(lam), cos_t.data_ptr<float>(),
+                     sin_t.data_ptr<float>(), optr(ve), optr(vgate), vstride, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                     rq.data_ptr<float>(), rk.data_ptr<float>(), k_last.data_ptr(), paired, key_offset, cur_stream(), status_ptr(x)),
+        "mng_qkv_proj");
+  g_launches += 1;
+  return {q, k, v, rq, rk, k_last};
+}
+
+// d_qkv [T, 3*H*128], d_ve, d_vgate from the outputs of qkv_proj and the gradients of q, k, v.
+std::vector<Tensor> qkv_post_bwd_from_out(const Tensor& q, const Tensor& k, const Tensor& k_last, const Tensor& cos_t,
+                                          const Tensor& sin_t, const Tensor& rq, const Tensor& rk, const Tensor& dq,
+                                          const Tensor& dk, const Tensor& dv, const OptT& ve, const OptT& vgate, int64_t H,
+                                          bool paired, bool key_offset, bool need_dve, bool need_dvgate) {
+  const int64_t T = q.size(0);
+  TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && dq.is_contiguous() && dk.is_contiguous() && dv.is_contiguous());
+  c10::cuda::CUDAGuard guard(q.device());
+  Tensor dqkv = torch::empty({T, 3 * H * 128}, q.options()), dve, dvg;
+  const bool has_ve = ve.has_value() && ve->defined();
+  if (has_ve && need_dve) dve = torch::empty({T, H * 128}, q.options());
+  if (has_ve && need_dvgate) dvg = torch::empty({T, H}, q.options());
+  int vstride = (vgate.has_value() && vgate->defined()) ? (int)vgate->stride(0) : 0;
+  check(mng_qkv_post_bwd_from_out(q.data_ptr(), k.data_ptr(), k_last.data_ptr(), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),
+                                  rq.data_ptr<float>(), rk.data_ptr<float>(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), optr(ve),
+                                  optr(vgate), vstride, dqkv.data_ptr(), dve.defined() ? dve.data_ptr() : nullptr,
+                                  dvg.defined() ? dvg.data_ptr() : nullptr, (int)H, T, (int)H, paired, key_offset, cur_stream()),
+        "mng_qkv_post_bwd_from_out");
+  g_launches += 1;
+  return {dqkv, dve, dvg};
+}
+
 // alpha / gate: bf16 [T, >=H] views (row stride arbitrary, unit column stride) or None.
 Tensor xsa_gate_fwd(const Tensor& y, const Tensor& v, const OptT& alpha, const OptT& gate) {
   TORCH_CHECK(y.dim() == 3 && y.size(2) == 128 && y.is_contiguous() && v.is_contiguous() && y.scalar_type() == torch::kBFloat16);
@@ -767,6 +817,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("lincomb_bwd", &lincomb_bwd);
   m.def("qkv_post_fwd", &qkv_post_fwd);
   m.def("qkv_post_bwd", &qkv_post_bwd);
+  m.def("qkv_proj", &qkv_proj);
+  m.def("qkv_post_bwd_from_out", &qkv_post_bwd_from_out);
   m.def("xsa_gate_fwd", &xsa_gate_fwd);
   m.def("xsa_gate_bwd", &xsa_gate_bwd);
   m.def("embed_bwd", &embed_bwd);

@@ -3,6 +3,7 @@
 #include "gemm_sm100.cuh"
 #include "gemm_sm100_pair.cuh"
 #include "epi_ce.cuh"
+#include "epi_qkv.cuh"
 
 #include <cstdio>
 #include <cstring>
@@ -516,7 +517,12 @@ static int launch_pair(const GemmDesc& g, const typename Epi::Params& ep, int ma
   if (!B_MN) rc = cached_map(&maps.b, g.b, ES, g.K, g.N, g.batch, g.ldb, g.b_bstride, BK, 128);
   else rc = cached_map(&maps.b, g.b, ES, g.N, g.K, g.batch, g.ldb, g.b_bstride, 128 / ES, BK);
   if (rc) return rc - 1000;
-  if (epi_store16<Epi>::value) {
+  if (epi_custom_store<Epi>::value) {                       // several [M, out_cols] outputs share the N columns
+    rc = cached_map(&maps.out, g.out, 2, g.out_cols, g.M, g.batch, g.ldc, g.c_bstride, 64, 32);
+    if (!rc) rc = cached_map(&maps.out2, g.out2, 2, g.out_cols, g.M, g.batch, g.ldc, g.c_bstride, 64, 32);
+    if (!rc) rc = cached_map(&maps.out3, g.out3, 2, g.out_cols, g.M, g.batch, g.ldc, g.c_bstride, 64, 32);
+    if (rc) return rc - 1100;
+  } else if (epi_store16<Epi>::value) {
     rc = cached_map(&maps.out, g.out, 2, g.N, g.M, g.batch, g.ldc, g.c_bstride, 64, 32);
     if (rc) return rc - 1100;
   }
@@ -613,6 +619,26 @@ extern "C" int mng_lmhead_ce_fused(const void* x8, const void* wT8, int T, int V
   ce_finish_kernel<<<(unsigned)((T + 7) / 8), 256, 0, (cudaStream_t)stream>>>(p, losses, rowc, T, V);
   if (cudaGetLastError() != cudaSuccess) return -4;
   return launch_pair<1, false, false, 0, 0, TEpiCeGrad>(g, p, 0);
+}
+
+extern "C" int mng_qkv_proj(const void* x, const void* w, int T, int K, int H, const float* lam, const float* cos_t,
+                            const float* sin_t, const void* ve, const void* vgate, int vgate_stride, void* q, void* k, void* v,
+                            float* rstd_q, float* rstd_k, void* k_last, int paired, int key_offset, void* stream,
+                            uint32_t* status) {
+  if (T < 256 || K <= 0 || (K % 8) || H <= 0 || ((3 * H * 128) % 256)) return -1;
+  GemmDesc g{};
+  g.a = x; g.b = w; g.M = T; g.N = 3 * H * 128; g.K = K; g.batch = 1;
+  g.dtype_a = g.dtype_b = MNG_BF16;
+  g.lda = g.ldb = K;
+  g.out = q; g.out2 = k; g.out3 = v;
+  g.out_cols = H * 128;
+  g.ldc = H * 128;
+  g.stream = stream;
+  g.status = status;
+  QkvEpiParams p{lam, cos_t, sin_t, reinterpret_cast<const __nv_bfloat16*>(ve), reinterpret_cast<const __nv_bfloat16*>(vgate),
+                 vgate_stride, rstd_q, rstd_k, reinterpret_cast<__nv_bfloat16*>(k), reinterpret_cast<__nv_bfloat16*>(k_last),
+                 H, paired, key_offset};
+  return launch_pair<2, false, false, 1, 1, TEpiQkv>(g, p, 0);
 }
 
 extern "C" int mng_gemm(const GemmDesc* gp) {

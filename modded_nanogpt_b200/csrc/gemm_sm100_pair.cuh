@@ -33,6 +33,9 @@
 // calls tile_begin(ep, st, b, row, n0, M, N) before the four chunks (it may re-read single accumulator columns with
 // tmem_ld1 there), and tile_end(ep, st, b, row, n0, M, N) after them.  For these epilogues the chunk loop is
 // unrolled and the TMEM load of chunk c + 1 is in flight while chunk c is processed.
+// `static constexpr bool kCustomStore = true`: the epilogue issues the bulk stores of the warp's two staged
+// 32 x 64 boxes itself - issue_stores(ep, maps, stg, b, m0, n0, M, N), called by lane 0 - e.g. to route column ranges
+// to different output tensors or to shift a box by a row.
 #pragma once
 #include "gemm_sm100.cuh"
 
@@ -40,6 +43,8 @@ namespace mng {
 
 template <class E, class = void> struct epi_store16 { static constexpr bool value = true; };
 template <class E> struct epi_store16<E, decltype((void)E::kStore16)> { static constexpr bool value = E::kStore16; };
+template <class E, class = void> struct epi_custom_store { static constexpr bool value = false; };
+template <class E> struct epi_custom_store<E, decltype((void)E::kCustomStore)> { static constexpr bool value = E::kCustomStore; };
 template <class E, class = void> struct epi_hooks { static constexpr bool value = false; };
 template <class E> struct epi_hooks<E, decltype((void)E::kTileHooks)> { static constexpr bool value = E::kTileHooks; };
 
@@ -58,6 +63,7 @@ struct GemmPairSmem {
 
 struct PairMaps {
   CUtensorMap a, b, out, cin, out8;
+  CUtensorMap out2, out3;       // epilogues with `kCustomStore`: further bf16 outputs (same box shape as `out`)
 };
 
 template <int ES, bool A_MN, bool B_MN, uint32_t A_FMT, uint32_t B_FMT, class Epi>
@@ -115,6 +121,10 @@ gemm_tcgen05_pair_kernel(const __grid_constant__ PairMaps maps, GemmShape shape,
     tma_prefetch_desc(&maps.a);
     tma_prefetch_desc(&maps.b);
     if constexpr (STORE16) tma_prefetch_desc(&maps.out);
+    if constexpr (epi_custom_store<Epi>::value) {
+      tma_prefetch_desc(&maps.out2);
+      tma_prefetch_desc(&maps.out3);
+    }
     if constexpr (Epi::kCin) tma_prefetch_desc(&maps.cin);
     if constexpr (Epi::kOut8) tma_prefetch_desc(&maps.out8);
   }
@@ -320,7 +330,9 @@ gemm_tcgen05_pair_kernel(const __grid_constant__ PairMaps maps, GemmShape shape,
       __syncwarp();
       if (lane == 0) {
         if (m0 < shape.M) {
-          if constexpr (STORE16) {
+          if constexpr (epi_custom_store<Epi>::value) {
+            Epi::issue_stores(ep, maps, stg, b, m0, n0, shape.M, shape.N);
+          } else if constexpr (STORE16) {
             if (n0 < shape.N) tma_store_3d(&maps.out, stg, n0, m0, b);
             if (n0 + 64 < shape.N) tma_store_3d(&maps.out, stg + SM::BOX_BYTES, n0 + 64, m0, b);
           }

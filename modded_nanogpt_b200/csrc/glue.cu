@@ -343,6 +343,107 @@ qkv_post_bwd_kernel(const __nv_bfloat16* __restrict__ qkv, const float* __restri
   }
 }
 
+// Backward of the QKV post-processing from its OUTPUTS (interleaved-pair layout): for the projection whose epilogue
+// already produced q, k, v (csrc/epi_qkv.cuh) no copy of the raw projection exists.  The normalised pre-rotary values
+// are recovered from the outputs - the rotation is orthogonal, so n = R^T(out) for the rotating dims; the stationary
+// half of k sits one row down when the key offset is on (the last token's in k_last) - and
+//   d_x = rstd * (d_n - n * <d_n, n> / 128)        with d_n = R^T(d_out) (and the offset undone).
+__global__ void __launch_bounds__(QP_WARPS * 32)
+qkv_post_bwd_from_out_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+                             const __nv_bfloat16* __restrict__ k_last, const float* __restrict__ cos_t,
+                             const float* __restrict__ sin_t, const float* __restrict__ rstd_q, const float* __restrict__ rstd_k,
+                             const __nv_bfloat16* __restrict__ dq, const __nv_bfloat16* __restrict__ dk,
+                             const __nv_bfloat16* __restrict__ dv, const __nv_bfloat16* __restrict__ ve,
+                             const __nv_bfloat16* __restrict__ vgate, int vgate_stride, __nv_bfloat16* __restrict__ d_qkv,
+                             __nv_bfloat16* __restrict__ d_ve, __nv_bfloat16* __restrict__ d_vgate, int d_vgate_stride,
+                             long long T, int H, int paired, int key_offset) {
+  const int lane = threadIdx.x & 31;
+  const long long idx = (long long)blockIdx.x * QP_WARPS + (threadIdx.x >> 5);
+  if (idx >= T * H) return;
+  const long long t = idx / H;
+  const int h = (int)(idx % H);
+  const long long ld = 3LL * H * 128;
+  const long long pos = paired ? 2 * t + (h & 1) : t;
+  float cs[2] = {1.f, 1.f}, sn[2] = {0.f, 0.f};
+  const bool rot = lane < 16;                           // lane l owns dims 4l..4l+3: pairs 2l and 2l+1 rotate for l < 16
+  if (rot) {
+    cs[0] = cos_t[pos * 32 + 2 * lane]; cs[1] = cos_t[pos * 32 + 2 * lane + 1];
+    sn[0] = sin_t[pos * 32 + 2 * lane]; sn[1] = sin_t[pos * 32 + 2 * lane + 1];
+  }
+  auto ld4 = [&](const __nv_bfloat16* p, float (&f)[4]) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&u);
+    const float2 a = __bfloat1622float2(hh[0]), b = __bfloat1622float2(hh[1]);
+    f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+  };
+  auto unrot = [&](float (&f)[4]) {                     // transpose of the rotation on the two pairs of this lane
+    const float a0 = f[0], a1 = f[1], b0 = f[2], b1 = f[3];
+    f[0] = cs[0] * a0 - sn[0] * a1; f[1] = cs[0] * a1 + sn[0] * a0;
+    f[2] = cs[1] * b0 - sn[1] * b1; f[3] = cs[1] * b1 + sn[1] * b0;
+  };
+#pragma unroll
+  for (int which = 0; which < 2; ++which) {
+    const __nv_bfloat16* outp = which ? k : q;
+    const __nv_bfloat16* gp = which ? dk : dq;
+    float n[4], d[4];
+    ld4(outp + idx * 128 + lane * 4, n);
+    ld4(gp + idx * 128 + lane * 4, d);
+    if (rot) {
+      unrot(n);
+      unrot(d);
+    } else if (which == 1 && key_offset) {
+      // n[t, 64:] was stored at row t + 1 (and at row 0 for t = 0); its gradient arrives from there
+      float g0[4] = {0.f, 0.f, 0.f, 0.f};
+      if (t == 0) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) g0[u] = d[u];       // row 0 kept its own stationary half: n = out, gradient d
+      }
+      if (t + 1 < T) {
+        float nn[4], dd[4];
+        ld4(k + (idx + H) * 128 + lane * 4, nn);
+        ld4(dk + (idx + H) * 128 + lane * 4, dd);
+        if (t != 0) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) n[u] = nn[u];
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) d[u] = dd[u] + g0[u];
+      } else {
+        if (t != 0) ld4(k_last + h * 64 + (lane - 16) * 4, n);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) d[u] = g0[u];
+      }
+    }
+    const float r = (which ? rstd_k : rstd_q)[idx];
+    const float s = warp_sum(d[0] * n[0] + d[1] * n[1] + d[2] * n[2] + d[3] * n[3]) * (1.f / 128.f);
+    uint2 w;
+    w.x = pack_bf16x2(r * (d[0] - n[0] * s), r * (d[1] - n[1] * s));
+    w.y = pack_bf16x2(r * (d[2] - n[2] * s), r * (d[3] - n[3] * s));
+    *reinterpret_cast<uint2*>(d_qkv + t * ld + (which * H + h) * 128 + lane * 4) = w;
+  }
+  {
+    uint2 gu = *reinterpret_cast<const uint2*>(dv + idx * 128 + lane * 4);
+    *reinterpret_cast<uint2*>(d_qkv + t * ld + (2 * H + h) * 128 + lane * 4) = gu;
+    if (ve) {
+      const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&gu);
+      float2 ga = __bfloat1622float2(gh[0]), gb = __bfloat1622float2(gh[1]);
+      const float gt = vgate ? __bfloat162float(vgate[t * vgate_stride + h]) : 1.f;
+      if (d_ve) {
+        uint2 w;
+        w.x = pack_bf16x2(gt * ga.x, gt * ga.y); w.y = pack_bf16x2(gt * gb.x, gt * gb.y);
+        *reinterpret_cast<uint2*>(d_ve + idx * 128 + lane * 4) = w;
+      }
+      if (d_vgate) {
+        uint2 e = *reinterpret_cast<const uint2*>(ve + idx * 128 + lane * 4);
+        const __nv_bfloat162* eh = reinterpret_cast<const __nv_bfloat162*>(&e);
+        float2 ea = __bfloat1622float2(eh[0]), eb = __bfloat1622float2(eh[1]);
+        const float dot = warp_sum(ga.x * ea.x + ga.y * ea.y + gb.x * eb.x + gb.y * eb.y);
+        if (lane == 0) d_vgate[t * d_vgate_stride + h] = __float2bfloat16(dot);
+      }
+    }
+  }
+}
+
 // =====================================================================================================
 // Attention output gating, one warp per (token, head):
 //   y' = (y - tanh(alpha[t,h]) * (<y,v> / max(<v,v>, 1e-8)) * v) * gate[t,h]      (alpha, gate optional)
@@ -492,6 +593,20 @@ extern "C" int mng_qkv_post_bwd(const void* qkv, const float* cos_t, const float
       (const __nv_bfloat16*)qkv, cos_t, sin_t, rstd_q, rstd_k, (const __nv_bfloat16*)dq, (const __nv_bfloat16*)dk,
       (const __nv_bfloat16*)dv, (const __nv_bfloat16*)ve, (const __nv_bfloat16*)vgate, vgate_stride, (__nv_bfloat16*)d_qkv,
       (__nv_bfloat16*)d_ve, (__nv_bfloat16*)d_vgate, d_vgate_stride, T, H, paired, key_offset);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+extern "C" int mng_qkv_post_bwd_from_out(const void* q, const void* k, const void* k_last, const float* cos_t, const float* sin_t,
+                                         const float* rstd_q, const float* rstd_k, const void* dq, const void* dk, const void* dv,
+                                         const void* ve, const void* vgate, int vgate_stride, void* d_qkv, void* d_ve,
+                                         void* d_vgate, int d_vgate_stride, long long T, int H, int paired, int key_offset,
+                                         void* stream) {
+  const unsigned grid = (unsigned)((T * H + QP_WARPS - 1) / QP_WARPS);
+  qkv_post_bwd_from_out_kernel<<<grid, QP_WARPS * 32, 0, (cudaStream_t)stream>>>(
+      (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)k_last, cos_t, sin_t, rstd_q, rstd_k,
+      (const __nv_bfloat16*)dq, (const __nv_bfloat16*)dk, (const __nv_bfloat16*)dv, (const __nv_bfloat16*)ve,
+      (const __nv_bfloat16*)vgate, vgate_stride, (__nv_bfloat16*)d_qkv, (__nv_bfloat16*)d_ve, (__nv_bfloat16*)d_vgate,
+      d_vgate_stride, T, H, paired, key_offset);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 

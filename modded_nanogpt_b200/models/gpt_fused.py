@@ -170,15 +170,21 @@ def forward_fused(m, input_seq: Tensor, target_seq: Tensor, seqlens: Tensor, big
                 else:
                     gate_in = torch.cat([attn_in[:, :6], ve_t[:, :6]], dim=-1)
                 vgate = (2 * torch.sigmoid(F.linear(gate_in, m.ve_gate_bank[pl.ve_slot]))).contiguous()
-            if direct:
-                qkv = fused.bank_linear(attn_in, sa_lambdas[i, 0], qkv_w[sl], [qk_g[sl], vo_g[sl][:D]])
-            elif not torch.is_grad_enabled():
-                qkv = fused.linear_scaled(attn_in, qkv_w[sl], sa_lambdas[i, 0])
-            else:
-                qkv = F.linear(attn_in, sa_lambdas[i, 0] * torch.cat([qk_all[sl], vo_all[sl][:D]], dim=0))
             yarn = m.yarn_paired_head if pl.paired else m.yarn
             ct, st = (cos_p, sin_p) if pl.paired else (cos_t, sin_t)
-            q, k, v = qkv_post(qkv, ct, st, ve_t, vgate, vadd, H, pl.paired, pl.long_window and not pl.paired)
+            key_off = pl.long_window and not pl.paired
+            if direct and vadd is None and fused.qkv_proj_supported(attn_in, qkv_w[sl], H):
+                # projection with QK norm, rotary, key offset and value-embedding add in its epilogue
+                q, k, v = fused.qkv_proj(attn_in, sa_lambdas[i, 0], qkv_w[sl], [qk_g[sl], vo_g[sl][:D]], ct, st, ve_t, vgate,
+                                         H, pl.paired, key_off)
+            else:
+                if direct:
+                    qkv = fused.bank_linear(attn_in, sa_lambdas[i, 0], qkv_w[sl], [qk_g[sl], vo_g[sl][:D]])
+                elif not torch.is_grad_enabled():
+                    qkv = fused.linear_scaled(attn_in, qkv_w[sl], sa_lambdas[i, 0])
+                else:
+                    qkv = F.linear(attn_in, sa_lambdas[i, 0] * torch.cat([qk_all[sl], vo_all[sl][:D]], dim=0))
+                q, k, v = qkv_post(qkv, ct, st, ve_t, vgate, vadd, H, pl.paired, key_off)
             if pl.paired:
                 y = ops.attention(q.view(2 * T, H // 2, Dh), k.view(2 * T, H // 2, Dh), v.view(2 * T, H // 2, Dh),
                                   seq2 if seq2 is not None else 2 * seqlens, ws[pl.long_window], yarn.attn_scale, 2 * max_len,

@@ -302,6 +302,61 @@ class _BankLinear(torch.autograd.Function):
         return (dx.view(*dy.shape[:-1], K), dlam.to(dtype).reshape(shape), None) + (None,) * len(gv)
 
 
+class _QkvProj(torch.autograd.Function):
+    """q, k, v = post(x @ (lam * W)^T): the QKV projection with QK RMSNorm, rotary, partial key offset and the gated
+    value-embedding add (`train_gpt.py:1103-1116`) done in the GEMM's epilogue (csrc/epi_qkv.cuh), so the raw
+    [T, 3*H*128] projection is neither written nor kept.  Backward: the post-processing is undone from its outputs
+    (`qkv_post_bwd_from_out`), then the projection's backward as in `_BankLinear`."""
+
+    @staticmethod
+    def forward(ctx, x, lam, w, cos_t, sin_t, ve, vgate, H, paired, key_offset, *grad_views):
+        x2 = x.reshape(-1, x.shape[-1])
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        lam32 = lam.detach().reshape(()).float() if lam.dtype != torch.float32 else lam.detach().reshape(())
+        vec = None if ve is None else ve.contiguous()
+        q, k, v, rq, rk, k_last = _C().qkv_proj(x2, w, lam32, cos_t, sin_t, vec, vgate, H, paired, key_offset)
+        ctx.save_for_backward(x2, lam32, w, q, k, rq, rk, k_last, cos_t, sin_t, vec, vgate)
+        ctx.grad_views = grad_views
+        ctx.cfg = (H, paired, key_offset, lam.dtype, lam.shape, x.shape)
+        return q, k, v
+
+    @staticmethod
+    def backward(ctx, dq, dk, dv):
+        x2, lam32, w, q, k, rq, rk, k_last, cos_t, sin_t, ve, vgate = ctx.saved_tensors
+        H, paired, key_offset, ldt, lshape, xshape = ctx.cfg
+        need_dve = ve is not None and ctx.needs_input_grad[5]
+        need_dvg = vgate is not None and ctx.needs_input_grad[6]
+        dy2, dve, dvg = _C().qkv_post_bwd_from_out(q, k, k_last, cos_t, sin_t, rq, rk, dq.contiguous(), dk.contiguous(),
+                                                   dv.contiguous(), ve, vgate, H, paired, key_offset, need_dve, need_dvg)
+        N, K = w.shape
+        T = dy2.shape[0]
+        dx = gemm(dy2, w, b_mn=True, alpha_t=lam32)
+        S = _split_k(T, -(-N // 128) * -(-K // 128))
+        parts = torch.empty(S, N, K, dtype=torch.float32, device=dy2.device)
+        gemm(dy2.view(S, T // S, N), x2.view(S, T // S, K), a_mn=True, b_mn=True, out=parts, bn=128)
+        gv = ctx.grad_views
+        dlam = _C().bank_grad_acc(parts, w, lam32, gv[0], gv[1] if len(gv) > 1 else None)
+        if dve is not None:
+            dve = dve.view(ve.shape)
+        return (dx.view(xshape), dlam.to(ldt).reshape(lshape), None, None, None, dve, dvg, None, None, None) + (None,) * len(gv)
+
+
+def qkv_proj(x: Tensor, lam: Tensor, w: Tensor, grad_views: list, cos_t: Tensor, sin_t: Tensor, ve: Tensor | None,
+             vgate: Tensor | None, H: int, paired: bool, key_offset: bool):
+    """Returns q, k, v [T, H, 128].  `w` [3*H*128, K] contiguous (rows: q heads, k heads, v heads)."""
+    return _QkvProj.apply(x, lam, w.detach(), cos_t, sin_t, ve, vgate, H, paired, key_offset, *grad_views)
+
+
+def qkv_proj_supported(x: Tensor, w: Tensor, H: int) -> bool:
+    T = x.numel() // x.shape[-1]
+    return (QKV_FUSED and x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and T >= 256 and T % 64 == 0
+            and w.shape[0] == 3 * H * 128 and (3 * H * 128) % 256 == 0 and w.shape[1] % 64 == 0)
+
+
+QKV_FUSED = os.environ.get("MNG_QKV_FUSED", "1") != "0"      # 0: projection, then the separate post-processing kernel
+
+
 def bank_linear(x: Tensor, lam: Tensor, w: Tensor, grad_views: list) -> Tensor:
     """`w`: contiguous [N, K] bf16 weight (no autograd); `grad_views`: one or two contiguous bf16 gradient slices
     that together cover w's rows in order."""

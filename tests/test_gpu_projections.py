@@ -171,3 +171,74 @@ def test_mlp_with_fused_residual_mix(fused, T, use_fp8):
         else:
             assert _rel(a, b) < 8e-3, (name, _rel(a, b))
     fused.check_status()
+
+
+@pytest.mark.parametrize("T,paired,key_offset,with_ve", [(2048, False, False, False), (2048, True, False, True),
+                                                          (4096, False, True, False), (2048, False, True, True),
+                                                          (49152, False, True, True), (49152, True, False, False)])
+def test_qkv_projection_with_fused_postprocessing(fused, T, paired, key_offset, with_ve):
+    """qkv_proj (norm / rotary / key offset / value add inside the GEMM epilogue, backward from the outputs) against the
+    projection followed by the stand-alone post-processing kernels, and both against the fp32 statement on a slice."""
+    from modded_nanogpt_b200.ops.glue import qkv_post
+    torch.manual_seed(5)
+    D, H = 768, 6
+    x = torch.randn(T, D, device="cuda").to(BF)
+    w = (torch.randn(3 * D, D, device="cuda") * D ** -0.5).to(BF)
+    t = torch.arange(2 * T, device="cuda", dtype=torch.float32)
+    freq = (1 / 1024) ** torch.linspace(0, 1, 32, device="cuda")
+    cos, sin = torch.outer(t, freq).cos().contiguous(), torch.outer(t, freq).sin().contiguous()
+    ve = torch.randn(T, D, device="cuda").to(BF) if with_ve else None
+    vg = torch.rand(T, H, device="cuda").to(BF) if with_ve else None
+    g = [torch.randn(T, H, 128, device="cuda").to(BF) for _ in range(3)]
+
+    def run(fused_path):
+        xs = x.clone().requires_grad_(True)
+        lam = torch.tensor(0.8, device="cuda", requires_grad=True)
+        ves = ve.clone().requires_grad_(True) if with_ve else None
+        vgs = vg.clone().requires_grad_(True) if with_ve else None
+        gv = [torch.zeros(2 * D, D, dtype=BF, device="cuda"), torch.zeros(D, D, dtype=BF, device="cuda")]
+        if fused_path:
+            q, k, v = fused.qkv_proj(xs, lam, w, gv, cos, sin, ves, vgs, H, paired, key_offset)
+        else:
+            q, k, v = qkv_post(fused.bank_linear(xs, lam, w, gv), cos, sin, ves, vgs, None, H, paired, key_offset)
+        torch.autograd.backward([q, k, v], g)
+        return (q, k, v, xs.grad, lam.grad, gv[0], gv[1], ves.grad if with_ve else None, vgs.grad if with_ve else None)
+
+    a, b = run(True), run(False)
+    names = ("q", "k", "v", "dx", "dlam", "dW_qk", "dW_v", "dve", "dvgate")
+    for n, u, v_ in zip(names, a, b):
+        if u is None:
+            continue
+        if u.numel() == 1:
+            # <dW, W>: the q and k parts cancel almost exactly (the norm makes them scale invariant), so the sum is
+            # small against its terms; compare on the scale of the Cauchy-Schwarz bound
+            bound = (a[5].float().norm() * w[:2 * D].float().norm() + a[6].float().norm() * w[2 * D:].float().norm()).item()
+            assert abs(u.item() - v_.item()) < 2e-2 * abs(v_.item()) + 2e-3 * bound, (n, u.item(), v_.item(), bound)
+        else:
+            assert _rel(u, v_) < 1.2e-2, (n, _rel(u, v_))
+    # boundary rows of the key offset, exactly: row 0 keeps its own stationary half, row t takes row t-1's
+    if key_offset:
+        kf, kp = a[1], b[1]
+        assert _rel(kf[:3], kp[:3]) < 8e-3 and _rel(kf[-3:], kp[-3:]) < 8e-3
+        assert (kf[1:5, :, 64:].float() - kf[1:5, :, 64:].float()).abs().max() == 0
+    # fp32 statement of the forward on the first 256 rows
+    sl = slice(0, 256)
+    raw = ((x[sl].float() @ w.float().T) * 0.8).to(BF).float().view(256, 3, H, 128)
+    eps = torch.finfo(torch.float32).eps
+    nq, nk = [(r * torch.rsqrt(r.square().mean(-1, keepdim=True) + eps)).to(BF).float() for r in (raw[:, 0], raw[:, 1])]
+    pos = (2 * torch.arange(256, device="cuda")[:, None] + (torch.arange(H, device="cuda")[None, :] & 1)) if paired \
+        else torch.arange(256, device="cuda")[:, None].expand(256, H)
+    c, s_ = cos[pos], sin[pos]                                       # [256, H, 32]
+
+    def rope(n):
+        o = n.clone()
+        o[..., 0:64:2] = c * n[..., 0:64:2] + s_ * n[..., 1:64:2]
+        o[..., 1:64:2] = c * n[..., 1:64:2] - s_ * n[..., 0:64:2]
+        return o
+
+    want_q, want_k = rope(nq), rope(nk)
+    if key_offset:
+        want_k[1:, :, 64:] = nk[:-1, :, 64:]
+    want_v = raw[:, 2] + (vg[sl].float()[:, :, None] * ve[sl].float().view(256, H, 128) if with_ve else 0)
+    assert _rel(a[0][sl], want_q) < 8e-3 and _rel(a[1][sl], want_k) < 8e-3 and _rel(a[2][sl], want_v) < 8e-3
+    fused.check_status()
