@@ -26,6 +26,10 @@
 #include <mutex>
 #include <string>
 
+// All soft-max exponentials stay on the special-function unit: moving every other one to the FMA pipe (exp2_fma in
+// ptx.cuh) measured 19 % slower in the forward and 5 % slower in the backward on B200 - these kernels are bound by the
+// latency of their S -> P -> PV chains, not by the throughput of that unit.
+
 namespace mng {
 
 constexpr int ATT_THREADS = 192;

@@ -70,19 +70,6 @@ __device__ __forceinline__ float ce_exp2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
   return r;
 }
-// 2^x for x in [-126, 0] on the FMA and integer pipes (the special-function unit is what bounds these epilogues, and
-// it already evaluates one tanh per element): x = n + f with n integer, |f| <= 0.5; 2^f by a degree-4 polynomial
-// (relative error 4e-5), 2^n by an add into the exponent field.
-__device__ __forceinline__ float ce_exp2_poly(float x) {
-  const float t = x + 12582912.f;                        // 1.5 * 2^23: the integer part of x lands in the low mantissa bits
-  const float f = x - (t - 12582912.f);
-  float p = 0.0096181291f;
-  p = fmaf(p, f, 0.055504109f);
-  p = fmaf(p, f, 0.24022651f);
-  p = fmaf(p, f, 0.69314718f);
-  p = fmaf(p, f, 1.0f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
 // The epilogues send every other exponential to the polynomial: that balances the two pipes (8 issue slots of the FMA
 // pipe cost what one special-function instruction costs in its unit).
 
@@ -161,7 +148,7 @@ struct TEpiCeStats {
       float a, b;
       ce_sigmoid2(acc[j], acc[j + 1], p, a, b);
       s0 += ce_exp2(fmaf(p.k2, a, -p.k2));
-      s1 += ce_exp2_poly(fmaf(p.k2, b, -p.k2));
+      s1 += exp2_fma(fmaf(p.k2, b, -p.k2));
     }
     st.sum += s0 + s1;
   }
@@ -182,7 +169,7 @@ struct TEpiCeGrad {
   __device__ static uint32_t grad2(const Params& p, float c, float a0, float a1) {
     float s0, s1;
     ce_sigmoid2(a0, a1, p, s0, s1);
-    const float e0 = ce_exp2(fmaf(p.k2, s0, -p.k2)), e1 = ce_exp2_poly(fmaf(p.k2, s1, -p.k2));
+    const float e0 = ce_exp2(fmaf(p.k2, s0, -p.k2)), e1 = exp2_fma(fmaf(p.k2, s1, -p.k2));
     return (uint32_t)pack_e5m2x2(c * e0 * fmaf(-s0, s0, s0), c * e1 * fmaf(-s1, s1, s1));
   }
   __device__ static void apply(const Params& p, State& st, const float (&acc)[32], const uint4 (&)[4], uint4 (&)[4], uint4 (&out8)[2],

@@ -399,6 +399,22 @@ __device__ __forceinline__ uint16_t pack_e4m3x2(float a, float b) {   // saturat
 __device__ __forceinline__ uint16_t pack_e5m2x2(float a, float b) {
   return static_cast<uint16_t>(__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E5M2));
 }
+// 2^x on the FMA and integer pipes instead of the special-function unit, for x in [-126, 126] (x is clamped at -126;
+// -inf gives 2^-126): x = n + f with n integer, |f| <= 0.5; 2^f by a degree-4 polynomial (relative error 4e-5, far
+// below bf16 resolution), 2^n by an add into the exponent field.  Kernels whose element-wise phase is bound by the
+// 16-per-clock special-function unit (soft-max exponentials) send every other exponential here.
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = x + 12582912.f;                        // 1.5 * 2^23: the integer part of x lands in the low mantissa bits
+  const float f = x - (t - 12582912.f);
+  float p = 0.0096181291f;
+  p = fmaf(p, f, 0.055504109f);
+  p = fmaf(p, f, 0.24022651f);
+  p = fmaf(p, f, 0.69314718f);
+  p = fmaf(p, f, 1.0f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

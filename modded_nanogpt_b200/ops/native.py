@@ -3,6 +3,7 @@ On a machine with a GPU a missing extension is an error, never a silent fallback
 from __future__ import annotations
 
 import importlib
+import os
 
 import torch
 
@@ -14,7 +15,8 @@ def load():
     global _mod, _err
     if _mod is None and _err is None:
         try:
-            _mod = importlib.import_module("modded_nanogpt_b200._C")
+            # MNG_NATIVE=_Cdbg runs everything on the bounds-checked build (python build_ext.py --debug)
+            _mod = importlib.import_module("modded_nanogpt_b200." + os.environ.get("MNG_NATIVE", "_C"))
         except Exception as e:  # noqa: BLE001
             _err = e
     return _mod
