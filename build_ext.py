@@ -89,6 +89,10 @@ def build(force: bool = False, verbose: bool = True, debug: bool = False) -> Pat
         link += ["-lc10", "-lc10_cuda", "-ltorch_cpu", "-ltorch_cuda", "-ltorch", "-ltorch_python", "-lcudart"]
         _run(link)
         stamp.write_text(want)
+        live = {n for st in BUILD.glob("link*.stamp") for n in st.read_text().split()}
+        for o in BUILD.glob("*.o"):                          # objects of earlier source versions
+            if o.name not in live:
+                o.unlink()
         if verbose:
             print(f"[build_ext] linked {out.name}", flush=True)
     return out

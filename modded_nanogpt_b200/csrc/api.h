@@ -128,6 +128,27 @@ typedef struct {
 } AdamDesc;
 int mng_adam(const AdamDesc* d, void* stream);
 
+// One launch for up to MNG_SMALL_ADAM_MAX small replicated parameters.  base: the address of one buffer (an arena) on every
+// rank, or a single null entry when p_off / g_off are absolute addresses; each rank reads all ranks' gradients and updates
+// its own copy.
+#define MNG_SMALL_ADAM_MAX 16
+typedef struct {
+  long long p_off, g_off;   // byte offsets of the parameter and of its gradient from base
+  float* m;
+  float* v;
+  long long n;
+  int is_f32;               // parameter and gradient dtype: fp32 or bf16
+  float beta1, beta2, eps, step_size, eff_wd;
+} SmallAdamEntry;
+typedef struct {
+  PeerPtrs base;
+  int count;
+  float gmul;               // gradient multiplier (1 / ranks)
+  SmallAdamEntry e[MNG_SMALL_ADAM_MAX];
+} SmallAdamTable;
+int mng_adam_small(const SmallAdamTable* t, void* stream);
+int mng_fill_zero(void* p, long long bytes, void* stream);
+
 //   g = bf16(grad_mul * sum_r grads[r]); buf = lerp(buf, g, 1-mu); u = lerp(g, buf, mu);
 //   out = bf16(u); sumsq[mat] = sum(out^2)
 int mng_nesterov(const PeerPtrs* grads, long long off, float* buf, void* out_bf16, float* sumsq, long long mats,
@@ -136,10 +157,11 @@ int mng_nesterov(const PeerPtrs* grads, long long off, float* buf, void* out_bf1
 int mng_scale_by_norm(void* x_bf16, const float* sumsq, long long mats, long long per_mat, void* stream);
 // NorMuon second-moment normalisation + cautious weight decay on bf16 weight + uint16 mantissa.
 //   red_rows != 0: statistics per row (reduce over columns), else per column (reduce over rows).
-//   scale_scratch: mats * max(rows, cols) floats of scratch.
+//   scale_scratch: mats * (max(rows, cols) + 65) floats, all zero before the first call (the kernels leave the
+//   counters at its end zero again).  Learning rate of matrix m = lr_base * lr_mul_per_mat[m].
 int mng_normuon_apply(const PeerPtrs* params, long long off, void* mantissa_u16, const void* v_bf16, float* second_mom,
                       float* scale_scratch, long long mats, int rows, int cols, int red_rows, float beta2, float eff_wd,
-                      const float* eff_lr_per_mat, void* stream);
+                      float lr_base, const float* lr_mul_per_mat, void* stream);
 // ---- fused glue (glue.cu) -----------------------------------------------------------------------------
 #define LC_MAX_TERMS 6
 typedef struct {

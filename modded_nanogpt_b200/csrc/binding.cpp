@@ -298,8 +298,9 @@ std::vector<Tensor> lmhead_ce_fused(const Tensor& x8, const Tensor& wT8, double 
   return {losses, dl};
 }
 
-PeerPtrs peers_from(const std::vector<int64_t>& ptrs, int64_t self) {
+PeerPtrs peers_from(const std::vector<int64_t>& ptrs, int64_t self, int64_t mc = 0) {
   PeerPtrs p{};
+  p.mc = reinterpret_cast<void*>(mc);
   TORCH_CHECK(ptrs.size() >= 1 && ptrs.size() <= MNG_MAX_RANKS && self >= 0 && self < (int64_t)ptrs.size());
   p.n = (int)ptrs.size();
   p.self = (int)self;
@@ -311,7 +312,7 @@ PeerPtrs peers_from(const std::vector<int64_t>& ptrs, int64_t self) {
 // gradient / parameter buffers on each rank (length 1 = local only).
 void adam(const std::vector<int64_t>& grad_ptrs, const std::vector<int64_t>& param_ptrs, int64_t self, int64_t off, Tensor& exp_avg,
           Tensor& exp_avg_sq, int64_t n, bool p_is_f32, double beta1, double beta2, double eps, double step_size, double eff_wd,
-          double grad_mul, const c10::optional<Tensor>& row_mask, int64_t row_elems) {
+          double grad_mul, const c10::optional<Tensor>& row_mask, int64_t row_elems, int64_t grad_mc, int64_t param_mc) {
   c10::cuda::CUDAGuard guard(exp_avg.device());
   AdamDesc d{};
   if (row_mask.has_value() && row_mask->defined()) {        // [ranks, rows] uint8 in local memory
@@ -322,8 +323,8 @@ void adam(const std::vector<int64_t>& grad_ptrs, const std::vector<int64_t>& par
     d.mask_stride = row_mask->size(1);
     d.row_elems = (int)row_elems;
   }
-  d.grads = peers_from(grad_ptrs, grad_ptrs.size() == 1 ? 0 : self);
-  d.params = peers_from(param_ptrs, param_ptrs.size() == 1 ? 0 : self);
+  d.grads = peers_from(grad_ptrs, grad_ptrs.size() == 1 ? 0 : self, grad_mc);
+  d.params = peers_from(param_ptrs, param_ptrs.size() == 1 ? 0 : self, param_mc);
   d.off = off;
   d.exp_avg = exp_avg.data_ptr<float>();
   d.exp_avg_sq = exp_avg_sq.data_ptr<float>();
@@ -336,12 +337,46 @@ void adam(const std::vector<int64_t>& grad_ptrs, const std::vector<int64_t>& par
   g_launches += 1;
 }
 
+// A batch of small replicated parameters in one launch.  base_ptrs: the address of the buffer holding them on every rank
+// (p_offs / g_offs are byte offsets from it), or [0] with absolute addresses as offsets.  hyper: beta1, beta2, eps,
+// step_size, eff_wd per entry.
+void adam_small(const std::vector<int64_t>& base_ptrs, int64_t self, const std::vector<int64_t>& p_offs,
+                const std::vector<int64_t>& g_offs, std::vector<Tensor>& ms, std::vector<Tensor>& vs, const std::vector<int64_t>& ns,
+                const std::vector<int64_t>& is_f32, const std::vector<double>& hyper, double grad_mul) {
+  const size_t k = p_offs.size();
+  TORCH_CHECK(k >= 1 && g_offs.size() == k && ms.size() == k && vs.size() == k && ns.size() == k && is_f32.size() == k &&
+              hyper.size() == 5 * k);
+  c10::cuda::CUDAGuard guard(ms[0].device());
+  for (size_t lo = 0; lo < k; lo += MNG_SMALL_ADAM_MAX) {
+    SmallAdamTable t{};
+    t.base = peers_from(base_ptrs, base_ptrs.size() == 1 ? 0 : self);
+    t.gmul = (float)grad_mul;
+    t.count = (int)std::min<size_t>(MNG_SMALL_ADAM_MAX, k - lo);
+    for (int i = 0; i < t.count; ++i) {
+      const size_t j = lo + i;
+      TORCH_CHECK(ms[j].is_cuda() && ms[j].scalar_type() == torch::kFloat32 && ms[j].is_contiguous() && ms[j].numel() >= ns[j]);
+      TORCH_CHECK(vs[j].is_cuda() && vs[j].scalar_type() == torch::kFloat32 && vs[j].is_contiguous() && vs[j].numel() >= ns[j]);
+      t.e[i] = SmallAdamEntry{p_offs[j], g_offs[j], ms[j].data_ptr<float>(), vs[j].data_ptr<float>(), ns[j], (int)is_f32[j],
+                              (float)hyper[5 * j], (float)hyper[5 * j + 1], (float)hyper[5 * j + 2], (float)hyper[5 * j + 3],
+                              (float)hyper[5 * j + 4]};
+    }
+    check(mng_adam_small(&t, cur_stream()), "mng_adam_small");
+    g_launches += 1;
+  }
+}
+
+void fill_zero(Tensor& t) {
+  TORCH_CHECK(t.is_cuda() && t.is_contiguous());
+  c10::cuda::CUDAGuard guard(t.device());
+  check(mng_fill_zero(t.data_ptr(), (long long)t.numel() * t.element_size(), cur_stream()), "mng_fill_zero");
+}
+
 void nesterov(const std::vector<int64_t>& grad_ptrs, int64_t self, int64_t off, Tensor& buf, Tensor& out, Tensor& sumsq,
-              double momentum, double grad_mul) {
+              double momentum, double grad_mul, int64_t grad_mc) {
   TORCH_CHECK(buf.dim() == 3 && out.sizes() == buf.sizes() && buf.scalar_type() == torch::kFloat32 &&
               out.scalar_type() == torch::kBFloat16 && buf.is_contiguous() && out.is_contiguous() && sumsq.numel() == buf.size(0));
   c10::cuda::CUDAGuard guard(buf.device());
-  PeerPtrs g = peers_from(grad_ptrs, grad_ptrs.size() == 1 ? 0 : self);
+  PeerPtrs g = peers_from(grad_ptrs, grad_ptrs.size() == 1 ? 0 : self, grad_mc);
   check(mng_nesterov(&g, off, buf.data_ptr<float>(), out.data_ptr(), sumsq.data_ptr<float>(), buf.size(0),
                      buf.size(1) * buf.size(2), (float)momentum, (float)grad_mul, cur_stream()),
         "mng_nesterov");
@@ -356,16 +391,20 @@ void scale_by_norm(Tensor& x, const Tensor& sumsq) {
 }
 
 void normuon_apply(const std::vector<int64_t>& param_ptrs, int64_t self, int64_t off, Tensor& mantissa, const Tensor& v,
-                   Tensor& second_mom, Tensor& scratch, bool red_rows, double beta2, double eff_wd, const Tensor& eff_lr_per_mat) {
+                   Tensor& second_mom, Tensor& scratch, bool red_rows, double beta2, double eff_wd, double lr_base,
+                   const Tensor& lr_mul_per_mat, int64_t param_mc) {
   TORCH_CHECK(v.dim() == 3 && v.is_contiguous() && v.scalar_type() == torch::kBFloat16 && mantissa.is_contiguous());
-  TORCH_CHECK(mantissa.numel() == v.numel() && eff_lr_per_mat.numel() == v.size(0));
+  TORCH_CHECK(mantissa.numel() == v.numel() && lr_mul_per_mat.numel() == v.size(0) && lr_mul_per_mat.is_cuda() &&
+              lr_mul_per_mat.scalar_type() == torch::kFloat32);
   const int rows = (int)v.size(1), cols = (int)v.size(2);
-  TORCH_CHECK(second_mom.numel() == v.size(0) * (red_rows ? rows : cols) && scratch.numel() >= second_mom.numel());
+  TORCH_CHECK(second_mom.numel() == v.size(0) * (red_rows ? rows : cols));
+  TORCH_CHECK(scratch.scalar_type() == torch::kFloat32 && scratch.is_contiguous() &&
+              scratch.numel() >= v.size(0) * ((red_rows ? rows : cols) + 65), "scratch: mats * (max(rows, cols) + 65) zeroed floats");
   c10::cuda::CUDAGuard guard(v.device());
-  PeerPtrs p = peers_from(param_ptrs, param_ptrs.size() == 1 ? 0 : self);
+  PeerPtrs p = peers_from(param_ptrs, param_ptrs.size() == 1 ? 0 : self, param_mc);
   check(mng_normuon_apply(&p, off, mantissa.data_ptr(), v.data_ptr(), second_mom.data_ptr<float>(), scratch.data_ptr<float>(),
-                          v.size(0), rows, cols, red_rows, (float)beta2, (float)eff_wd, eff_lr_per_mat.data_ptr<float>(),
-                          cur_stream()),
+                          v.size(0), rows, cols, red_rows, (float)beta2, (float)eff_wd, (float)lr_base,
+                          lr_mul_per_mat.data_ptr<float>(), cur_stream()),
         "mng_normuon_apply");
   g_launches += 2;
 }
@@ -809,6 +848,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("quant_static_dual", &quant_static_dual);
   m.def("lmhead_ce_fused", &lmhead_ce_fused);
   m.def("adam", &adam);
+  m.def("adam_small", &adam_small);
+  m.def("fill_zero", &fill_zero);
   m.def("nesterov", &nesterov);
   m.def("scale_by_norm", &scale_by_norm);
   m.def("normuon_apply", &normuon_apply);

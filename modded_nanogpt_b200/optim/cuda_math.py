@@ -29,10 +29,10 @@ class CudaMath(TorchMath):
         self.rank = rank
         self._scratch: dict = {}
 
-    def _buf(self, key, shape, dtype, device):
+    def _buf(self, key, shape, dtype, device, zero: bool = False):
         t = self._scratch.get(key)
         if t is None or t.shape != torch.Size(shape) or t.dtype != dtype:
-            t = torch.empty(shape, dtype=dtype, device=device)
+            t = (torch.zeros if zero else torch.empty)(shape, dtype=dtype, device=device)
             self._scratch[key] = t
         return t
 
@@ -66,7 +66,7 @@ class CudaMath(TorchMath):
         return min(rows, cols) >= 64 and (rows * cols) % 256 == 0
 
     def normuon_direction(self, grad_chunk: Tensor, state: dict, cfg: ParamConfig, grad_ptrs=None, off: int = 0,
-                          grad_mul: float = 1.0) -> Tensor:
+                          grad_mul: float = 1.0, grad_mc: int = 0) -> Tensor:
         C = lib()
         buf = state["momentum_buffer"]
         shape = buf.shape
@@ -78,11 +78,12 @@ class CudaMath(TorchMath):
         if grad_ptrs is None:
             grad_chunk = grad_chunk.contiguous()
             grad_ptrs, off = [grad_chunk.data_ptr()], 0
-        C.nesterov(grad_ptrs, self.rank, off, buf, X, ss, float(cfg.momentum), grad_mul)
+        C.nesterov(grad_ptrs, self.rank, off, buf, X, ss, float(cfg.momentum), grad_mul, grad_mc)
         C.scale_by_norm(X, ss)
         return self.polar_express(X)
 
-    def normuon_apply(self, p_slice: Tensor, state: dict, v: Tensor, cfg: ParamConfig, param_ptrs=None, off: int = 0) -> None:
+    def normuon_apply(self, p_slice: Tensor, state: dict, v: Tensor, cfg: ParamConfig, param_ptrs=None, off: int = 0,
+                      param_mc: int = 0) -> None:
         C = lib()
         mats, rows, cols = v.shape
         if not self.kernel_shapes(rows, cols):
@@ -90,20 +91,23 @@ class CudaMath(TorchMath):
             return super().normuon_apply(p_slice, state, v, cfg)
         red_rows = rows >= cols
         eff_wd = cfg.wd_mul * cfg.weight_decay * cfg.lr
+        # the per-matrix multipliers never change: they stay on the device; the step's learning rate is a launch argument
         mul = cfg.per_matrix_lr_mul or [1.0] * mats
-        key = ("lr", cfg.label)
-        lrs_host = [cfg.lr_mul * m * cfg.lr for m in mul]
-        lrs = self._buf(key, (mats,), torch.float32, v.device)
-        lrs.copy_(torch.tensor(lrs_host, dtype=torch.float32), non_blocking=True)
-        scratch = self._buf(("sc", cfg.label), (mats * max(rows, cols),), torch.float32, v.device)
+        key = ("lr_mul", cfg.label)
+        muls = self._scratch.get(key)
+        if muls is None or muls[0] != tuple(mul):
+            muls = (tuple(mul), torch.tensor(list(mul), dtype=torch.float32, device=v.device))
+            self._scratch[key] = muls
+        scratch = self._buf(("sc", cfg.label), (mats * (max(rows, cols) + 65),), torch.float32, v.device, zero=True)
         if param_ptrs is None:
             assert p_slice.is_contiguous()
             param_ptrs, off = [p_slice.data_ptr()], 0
         C.normuon_apply(param_ptrs, self.rank, off, state["mantissa"], v.contiguous(), state["second_momentum_buffer"],
-                        scratch, red_rows, float(cfg.beta2), float(eff_wd), lrs)
+                        scratch, red_rows, float(cfg.beta2), float(eff_wd), float(cfg.lr_mul * cfg.lr), muls[1], param_mc)
 
     def adam(self, p_slice: Tensor, grad: Tensor, state: dict, cfg: ParamConfig, step_size: float, eff_wd: float,
-             grad_ptrs=None, param_ptrs=None, off: int = 0, grad_mul: float = 1.0, row_mask=None, row_elems: int = 0) -> None:
+             grad_ptrs=None, param_ptrs=None, off: int = 0, grad_mul: float = 1.0, row_mask=None, row_elems: int = 0,
+             grad_mc: int = 0, param_mc: int = 0) -> None:
         """`row_mask` ([ranks, rows] uint8, local) with `row_elems`: gradient rows a rank did not touch are not loaded."""
         n = p_slice.numel()
         is_f32 = p_slice.dtype == torch.float32
@@ -117,7 +121,22 @@ class CudaMath(TorchMath):
             grad_ptrs, param_ptrs, off = [grad.data_ptr()], [p_slice.data_ptr()], 0
         b1, b2 = cfg.adam_betas
         lib().adam(grad_ptrs, param_ptrs, self.rank, off, state["exp_avg"], state["exp_avg_sq"], n, is_f32, b1, b2, cfg.eps,
-                   step_size, eff_wd, grad_mul, row_mask, row_elems)
+                   step_size, eff_wd, grad_mul, row_mask, row_elems, grad_mc, param_mc)
+
+    def adam_batch(self, items, base_ptrs=None, grad_mul: float = 1.0) -> None:
+        """One launch for many small replicated parameters.  `items`: (param, grad_or_None, state, cfg, step_size, eff_wd,
+        p_off, g_off) with byte offsets from `base_ptrs` (every rank's address of the buffer that holds them); without
+        `base_ptrs` the tensors' own addresses are used.  Each rank sums all ranks' gradients and updates its own copy."""
+        p_offs, g_offs, ms, vs, ns, f32, hyper = [], [], [], [], [], [], []
+        for p, grad, state, cfg, step_size, eff_wd, p_off, g_off in items:
+            assert p.dtype in (torch.float32, torch.bfloat16) and p.is_contiguous()
+            if base_ptrs is None:
+                assert grad.is_contiguous() and grad.dtype == p.dtype
+                p_off, g_off = p.data_ptr(), grad.data_ptr()
+            p_offs.append(p_off); g_offs.append(g_off); ms.append(state["exp_avg"]); vs.append(state["exp_avg_sq"])
+            ns.append(p.numel()); f32.append(int(p.dtype == torch.float32))
+            hyper += [cfg.adam_betas[0], cfg.adam_betas[1], cfg.eps, step_size, eff_wd]
+        lib().adam_small(base_ptrs or [0], self.rank if base_ptrs else 0, p_offs, g_offs, ms, vs, ns, f32, hyper, grad_mul)
 
     def transpose_add(self, src: Tensor, dst: Tensor) -> None:
         if src.dtype == torch.bfloat16 and src.is_contiguous() and dst.is_contiguous():

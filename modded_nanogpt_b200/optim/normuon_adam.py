@@ -261,10 +261,20 @@ class NorMuonAndAdam:
         # fused path: collectives + math in one kernel per bank
         fused = getattr(self.coll, "fused", False)
 
+        # small replicated Adam parameters (gates, scalars, MUDD matrices): one kernel launch for all of them when the
+        # math object offers it and no library collective is needed (one rank, or gradients readable in peer memory)
+        small = []
+        can_batch = do_adam and hasattr(self.math, "adam_batch") and (self.world_size == 1 or (fused and hasattr(self.coll, "fused_small_adam")))
+
         # ---- phase 1: reductions -------------------------------------------------------
         for label in self.scatter_order:
             p, c = self.params[label], self.cfgs[label]
             if (c.optim == "adam" and not do_adam) or p.grad is None:
+                continue
+            if (can_batch and c.optim == "adam" and c.comms in ("replicated", "none") and p.is_cuda and p.numel() <= (1 << 20)
+                    and p.dtype in (torch.float32, torch.bfloat16) and p.grad.dtype == p.dtype and p.is_contiguous()
+                    and p.grad.is_contiguous() and (self.world_size == 1 or label in self.coll.offsets)):
+                small.append(label)
                 continue
             if label == "lm_head" and tied and em_p.grad is not None:
                 self.math.transpose_add(em_p.grad, p.grad)
@@ -279,6 +289,12 @@ class NorMuonAndAdam:
 
         # ---- phase 2: updates + gathers ------------------------------------------------
         gathers, lm_gather = [], None
+        if small:
+            if self.world_size == 1:
+                self.math.adam_batch([(self.params[l].data, self.params[l].grad, self.state[l], self.cfgs[l],
+                                       *self.adam_scalars(l), 0, 0) for l in small])
+            else:
+                self.coll.fused_small_adam(small, self)
         for label in self.work_order:
             if label not in self._pending:
                 continue
@@ -316,8 +332,12 @@ class NorMuonAndAdam:
         for g in gathers:
             g.wait()
         self._pending.clear()
+        if fused and hasattr(self.coll, "clear_grads"):
+            self.coll.clear_grads(do_adam)  # gradients live in one peer-mapped region: keep the buffers, one fill
         for label, p in self.params.items():
             if self.cfgs[label].optim == "adam" and not do_adam:
+                continue
+            if fused and hasattr(self.coll, "clear_grads"):
                 continue
             if fused and p.grad is not None:
                 self.coll.clear_grad(p)     # gradients live in peer-mapped memory: keep the buffer, zero it

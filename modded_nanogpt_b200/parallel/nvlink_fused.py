@@ -13,6 +13,10 @@ communication themselves (`csrc/optim.cu`):
   whether its gradient row was touched since the last Adam step and copies that mask into every peer's memory before
   the barrier; the Adam kernel then skips the peer loads of untouched rows (they are exactly zero), so only touched
   rows cross NVLink - the device-side counterpart of the host-driven row exchange of `train_gpt.py:263-346`;
+* when the arena has an NVSwitch multicast address (`MNG_MULTIMEM` unset or 1, and the symmetric-memory handle
+  offers one), the gradient read is a single `multimem.ld_reduce` per vector (the switch sums the ranks' copies, so
+  1/world of the bytes arrive) and the weight write a single `multimem.st`; the plain peer loads/stores remain the
+  path for `MNG_MULTIMEM=0`, for machines without multicast and for every test that lets a rank fail;
 * ordering: one `peer_barrier` kernel (release/acquire flags in the arena's signal pad, bounded
   spin that reports through the status word) after backward and one after the updates.
 
@@ -45,17 +49,37 @@ class NvlinkCollectives(TorchCollectives):
         assert self.world_size <= 8
         self.math = math
         self.device = env.device
+        import os
         layout, off = {}, PAD_BYTES
         params = [(getattr(p, "label", n), p) for n, p in model.named_parameters()]
         for label, p in params:
             nb = p.numel() * p.element_size()
-            layout[label] = (off, off + _align(nb), nb)
-            off += 2 * _align(nb)
+            layout[label] = [off, 0, nb]
+            off += _align(nb)
+        # the gradients follow the parameters as one contiguous region, the NorMuon ones first, so that clearing
+        # them after a step is one fill (NorMuon-only steps clear the first part)
+        if hasattr(model, "param_table"):
+            table = model.param_table()
+        else:
+            from ..trainer import track1_param_table
+            table = track1_param_table()
+        is_muon = lambda label: table.get(label, {}).get("optim") == "normuon"
+        self.grad_lo = off
+        for label, p in sorted(params, key=lambda lp: not is_muon(lp[0])):
+            if not is_muon(label) and not hasattr(self, "grad_muon_hi"):
+                self.grad_muon_hi = off
+            layout[label][1] = off
+            off += _align(layout[label][2])
+        if not hasattr(self, "grad_muon_hi"):
+            self.grad_muon_hi = off
+        self.grad_hi = off
         self.arena = symm.empty(off, dtype=torch.uint8, device=env.device)
         self.handle = symm.rendezvous(self.arena, dist.group.WORLD.group_name)
         self.arena.zero_()
         self.base_ptrs = [int(x) for x in self.handle.buffer_ptrs]
         assert len(self.base_ptrs) == self.world_size
+        mc = int(getattr(self.handle, "multicast_ptr", 0) or 0)
+        self.mc_base = mc if os.environ.get("MNG_MULTIMEM", "1") != "0" and self.world_size > 1 else 0
         self.offsets = {}
         for label, p in params:
             po, go, nb = layout[label]
@@ -104,6 +128,9 @@ class NvlinkCollectives(TorchCollectives):
         off = self.offsets[label][which]
         return [b + off for b in self.base_ptrs]
 
+    def _mc(self, label: str, which: int) -> int:
+        return self.mc_base + self.offsets[label][which] if self.mc_base else 0
+
     def peer_barrier(self):
         self.epoch += 1
         lib().peer_barrier(self.base_ptrs, self.rank, self.epoch, self.arena)
@@ -132,6 +159,20 @@ class NvlinkCollectives(TorchCollectives):
     def clear_grad(self, p):
         p.grad.zero_()
 
+    def clear_grads(self, do_adam: bool):
+        """One fill over the contiguous gradient region (NorMuon-only steps: its first part)."""
+        lib().fill_zero(self.arena[self.grad_lo:self.grad_hi if do_adam else self.grad_muon_hi])
+
+    def fused_small_adam(self, labels, optimizer):
+        """All small replicated Adam parameters in one launch: every rank reads all ranks' gradients straight from the
+        arena and updates its own copy (the all-reduce of `train_gpt.py:597-599`, one per parameter there)."""
+        items = []
+        for label in labels:
+            step_size, eff_wd = optimizer.adam_scalars(label)
+            po, go = self.offsets[label]
+            items.append((optimizer.params[label].data, None, optimizer.state[label], optimizer.cfgs[label], step_size, eff_wd, po, go))
+        self.math.adam_batch(items, base_ptrs=self.base_ptrs, grad_mul=1.0 / self.world_size)
+
     # -- called by NorMuonAndAdam.step ---------------------------------------------------------------
     def launch_fused_reduce(self, label, grad, cfg, state):
         return (None, None)           # nothing to launch: the update kernel reads the peers directly
@@ -149,8 +190,9 @@ class NvlinkCollectives(TorchCollectives):
         p = optimizer.params[label]
         if cfg.optim == "normuon":
             per_chunk = p.numel() // W
-            v = self.math.normuon_direction(None, state, cfg, grad_ptrs=gptrs, off=r * per_chunk, grad_mul=1.0 / W)
-            self.math.normuon_apply(None, state, v, cfg, param_ptrs=pptrs, off=r * per_chunk)
+            v = self.math.normuon_direction(None, state, cfg, grad_ptrs=gptrs, off=r * per_chunk, grad_mul=1.0 / W,
+                                            grad_mc=self._mc(label, 1))
+            self.math.normuon_apply(None, state, v, cfg, param_ptrs=pptrs, off=r * per_chunk, param_mc=self._mc(label, 0))
             return None
         step_size, eff_wd = optimizer.adam_scalars(label)
         if cfg.comms.startswith("sharded"):
@@ -158,10 +200,11 @@ class NvlinkCollectives(TorchCollectives):
             shard = p.data.view(-1)[r * n:(r + 1) * n]
             rm = self.row_masks.get(label)
             self.math.adam(shard, None, state, cfg, step_size, eff_wd, grad_ptrs=gptrs, param_ptrs=pptrs, off=r * n,
-                           grad_mul=1.0 / W, row_mask=rm["masks"] if rm else None, row_elems=rm["cols"] if rm else 0)
+                           grad_mul=1.0 / W, row_mask=rm["masks"] if rm else None, row_elems=rm["cols"] if rm else 0,
+                           grad_mc=self._mc(label, 1), param_mc=self._mc(label, 0))
             if rm:
                 rm["touched"].zero_()                         # the gradients are cleared after this step as well
         else:       # replicated: all ranks read all gradients and apply the same update to their own copy
             self.math.adam(p.data.view(-1), None, state, cfg, step_size, eff_wd, grad_ptrs=gptrs,
-                           param_ptrs=[pptrs[r]], off=0, grad_mul=1.0 / W)
+                           param_ptrs=[pptrs[r]], off=0, grad_mul=1.0 / W, grad_mc=self._mc(label, 1))
         return None

@@ -33,9 +33,15 @@ def main():
     mode = sys.argv[1] if len(sys.argv) > 1 else "optim"
     env = init_distributed(accum_base=8)
     results = {}
-    for comm in ("nccl", "fused_strict"):
+    multicast = False
+    for name, comm, mm in (("nccl", "nccl", "0"), ("fused_p2p", "fused_strict", "0"), ("fused_multimem", "fused_strict", "1")):
+        os.environ["MNG_MULTIMEM"] = mm        # "1": multimem.ld_reduce / multimem.st where the arena has a multicast address
         tr = build(env, comm)
         opt = tr.manager.optimizer
+        if name == "fused_p2p":
+            assert opt.coll.mc_base == 0
+        if name == "fused_multimem":
+            multicast = opt.coll.mc_base != 0
         assert getattr(opt.coll, "fused", False) == (comm != "nccl")
         assert bool(tr.manager.row_mask_labels) == (comm != "nccl" and env.world_size > 1)
         with torch.no_grad():      # away from the zero inits
@@ -64,21 +70,22 @@ def main():
             tr.manager.step_optimizers(step)
         torch.cuda.synchronize()
         fused.check_status()
-        results[comm] = {n: p.detach().float().clone() for n, p in tr.model.named_parameters()}
+        results[name] = {n: p.detach().float().clone() for n, p in tr.model.named_parameters()}
         # every rank must hold identical parameters after the gathers
         for n, p in tr.model.named_parameters():
             ref = p.detach().clone()
             dist.broadcast(ref, 0)
-            assert torch.equal(ref, p.detach()), f"{comm}: ranks disagree on {n}"
+            assert torch.equal(ref, p.detach()), f"{name}: ranks disagree on {n}"
         del tr
     worst = 0.0
-    for n, a in results["nccl"].items():
-        b = results["fused_strict"][n]
-        err = ((a - b).norm() / a.norm().clamp_min(1e-12)).item()
-        worst = max(worst, err)
-        assert err < 2e-2, (n, err)
+    for name in ("fused_p2p", "fused_multimem"):
+        for n, a in results["nccl"].items():
+            b = results[name][n]
+            err = ((a - b).norm() / a.norm().clamp_min(1e-12)).item()
+            worst = max(worst, err)
+            assert err < 2e-2, (name, n, err)
     if env.master:
-        print(f"MULTI_GPU_OK world={env.world_size} worst_rel_diff={worst:.3e}", flush=True)
+        print(f"MULTI_GPU_OK world={env.world_size} worst_rel_diff={worst:.3e} multicast={multicast}", flush=True)
     shutdown()
 
 

@@ -255,16 +255,53 @@ def test_adam_kernel(fused):
     from modded_nanogpt_b200.ops import native, reference as ref
     C = native.lib()
     torch.manual_seed(10)
-    for dt in (BF, torch.float32):
-        n = 4096 * 3
+    for dt, n in ((BF, 4096 * 3), (torch.float32, 4096 * 3), (BF, 8 * 1237), (torch.float32, 4 * 1237), (BF, 8), (BF, 3 * 10**6 + 8)):
         p = (torch.randn(n, device="cuda") * 0.1).to(dt)
         g = (torch.randn(n, device="cuda") * 0.01).to(dt)
         m, v = torch.rand(n, device="cuda") * 0.01, torch.rand(n, device="cuda") * 1e-4
         pr, mr, vr = p.clone(), m.clone(), v.clone()
-        C.adam([g.data_ptr()], [p.data_ptr()], 0, 0, m, v, n, dt == torch.float32, 0.9, 0.99, 1e-10, 3e-3, 2e-4, 1.0, None, 0)
+        C.adam([g.data_ptr()], [p.data_ptr()], 0, 0, m, v, n, dt == torch.float32, 0.9, 0.99, 1e-10, 3e-3, 2e-4, 1.0, None, 0, 0, 0)
         ref.adam_update_(pr, g, mr, vr, 0.9, 0.99, 1e-10, 3e-3, 2e-4)
         assert torch.allclose(m, mr, rtol=1e-5, atol=1e-8) and torch.allclose(v, vr, rtol=1e-5, atol=1e-10)
         assert (p.float() - pr.float()).abs().max() < (2e-3 if dt == BF else 1e-6)
+
+
+def test_adam_small_batch(fused):
+    """One launch updates a batch of small parameters of any size and of either dtype; two "ranks" are two gradient
+    buffers at the same offset from two bases in this GPU's memory."""
+    from modded_nanogpt_b200.ops import native, reference as ref
+    C = native.lib()
+    torch.manual_seed(13)
+    specs = [(22, torch.float32), (1, torch.float32), (82, BF), (98304, BF), (5248, torch.float32), (12, BF)] * 3   # 18 > one table
+    arenas = [torch.zeros(4 << 20, dtype=torch.uint8, device="cuda") for _ in range(2)]
+    off, entries, refs = 0, [], []
+    for n, dt in specs:
+        nb = n * (4 if dt == torch.float32 else 2)
+        views = []
+        for a in arenas:
+            pv = a[off:off + nb].view(dt)
+            gv = a[off + (1 << 21):off + (1 << 21) + nb].view(dt)
+            views.append((pv, gv))
+        p0 = (torch.randn(n, device="cuda") * 0.1).to(dt)
+        gs = [(torch.randn(n, device="cuda") * 0.01).to(dt) for _ in arenas]
+        for (pv, gv), g in zip(views, gs):
+            pv.copy_(p0)
+            gv.copy_(g)
+        m, v = torch.rand(n, device="cuda") * 0.01, torch.rand(n, device="cuda") * 1e-4
+        hyper = [0.9, 0.99, 1e-10, 3e-3 * (1 + len(entries)), 2e-4]
+        pr, mr, vr = p0.clone(), m.clone(), v.clone()
+        gavg = ((gs[0].float() + gs[1].float()) * 0.5).to(dt)
+        ref.adam_update_(pr, gavg, mr, vr, *hyper)
+        entries.append((off, off + (1 << 21), m, v, n, int(dt == torch.float32), hyper))
+        refs.append((views[0][0], pr, m, mr, v, vr, dt))
+        off += -(-nb // 256) * 256
+    assert off < (1 << 21)
+    C.adam_small([a.data_ptr() for a in arenas], 0, [e[0] for e in entries], [e[1] for e in entries], [e[2] for e in entries],
+                 [e[3] for e in entries], [e[4] for e in entries], [e[5] for e in entries], [h for e in entries for h in e[6]], 0.5)
+    for pv, pr, m, mr, v, vr, dt in refs:
+        assert torch.allclose(m, mr, rtol=1e-5, atol=1e-8) and torch.allclose(v, vr, rtol=1e-5, atol=1e-10)
+        assert (pv.float() - pr.float()).abs().max() < (2e-3 if dt == BF else 1e-6)
+    _ok(fused)
 
 
 def test_adam_kernel_row_mask(fused):
@@ -286,7 +323,7 @@ def test_adam_kernel_row_mask(fused):
         pp = p.clone()
         m, v = torch.zeros(cnt, device="cuda"), torch.zeros(cnt, device="cuda")
         C.adam([g.data_ptr() for g in grads], [pp.data_ptr(), pp.data_ptr()], 0, off, m, v, cnt, False, 0.9, 0.99, 1e-10,
-               3e-3, 2e-4, 0.5, mk, cols if mk is not None else 0)
+               3e-3, 2e-4, 0.5, mk, cols if mk is not None else 0, 0, 0)
         outs.append((pp, m, v))
     for a, b in zip(*outs):
         assert torch.equal(a, b)
@@ -297,13 +334,13 @@ def test_normuon_kernels(fused):
     from modded_nanogpt_b200.ops import native, reference as ref
     C = native.lib()
     torch.manual_seed(11)
-    for (mats, rows, cols) in ((3, 256, 768), (2, 3072, 768), (2, 768, 768)):
+    for (mats, rows, cols) in ((3, 256, 768), (2, 3072, 768), (2, 768, 768), (2, 768, 3072)):
         g = (torch.randn(mats, rows, cols, device="cuda") * 1e-3).to(BF)
         buf = torch.randn(mats, rows, cols, device="cuda") * 1e-3
         bufr = buf.clone()
         out = torch.empty_like(g)
         ss = torch.empty(mats, device="cuda")
-        C.nesterov([g.data_ptr()], 0, 0, buf, out, ss, 0.9, 1.0)
+        C.nesterov([g.data_ptr()], 0, 0, buf, out, ss, 0.9, 1.0, 0)
         ur = ref.nesterov_momentum_(g.float(), bufr, 0.9)
         assert torch.allclose(buf, bufr, rtol=1e-5, atol=1e-9) and _rel(out, ur) < 4e-3
         assert torch.allclose(ss, out.float().square().sum((-2, -1)), rtol=1e-4)
@@ -320,8 +357,11 @@ def test_normuon_kernels(fused):
         p = (torch.randn(mats, rows, cols, device="cuda") * 0.05).to(BF)
         mant = torch.randint(0, 65536, (mats, rows, cols), device="cuda").to(torch.uint16)
         pr, mantr = p.clone(), mant.clone()
-        lrs = torch.tensor([0.02 * (1 + i) for i in range(mats)], device="cuda")
-        C.normuon_apply([p.data_ptr()], 0, 0, mant, v, sm, torch.empty(mats * max(rows, cols), device="cuda"), red_rows, 0.9, 0.03, lrs)
+        muls = torch.tensor([1.0 + i for i in range(mats)], device="cuda")
+        lrs = 0.02 * muls
+        scratch = torch.zeros(mats * (max(rows, cols) + 65), device="cuda")
+        C.normuon_apply([p.data_ptr()], 0, 0, mant, v, sm, scratch, red_rows, 0.9, 0.03, 0.02, muls, 0)
+        assert int(scratch[-mats:].view(torch.int32).abs().sum()) == 0          # the per-matrix counters are left at zero
         vr = ref.normuon_variance_reduction_(v.clone(), smr, 0.9, -1 if red_rows else -2)
         for i in range(mats):
             ref.cautious_update_mantissa_(pr[i], mantr[i], vr[i], 0.03, float(lrs[i]))
