@@ -137,6 +137,35 @@ def build_case(name, T, bn, fused):
                 out = (F.linear(F.gelu(F.linear(x, w1)), w2) + b2) * sc.to(BF)
             out.backward(dout)
         return run, 3 * 2 * T * D * 64, T * D * 2
+    if name in ("dc_ours", "dc_ref"):       # DC correction of layer 10 (window 112, 6 heads), forward + backward, packed documents
+        g = torch.Generator(device=dev).manual_seed(0)
+        q, k, v, base = (torch.randn(T, 6, 128, device=dev, generator=g).to(BF).requires_grad_(True) for _ in range(4))
+        w1 = torch.randn(T, 6, device=dev, generator=g).to(BF).requires_grad_(True)
+        w2 = (torch.randn(T, 6, device=dev, generator=g) * 0.1).to(BF).requires_grad_(True)
+        lens = torch.exp(torch.randn(4 * T // 600, generator=torch.Generator().manual_seed(0)) + 6.4).clamp(2, 2048).long()
+        starts = torch.cat([torch.zeros(1, dtype=torch.long), lens.cumsum(0)])
+        starts = starts[starts < T]
+        cu = torch.full((max(len(starts) + 1, 64),), T, dtype=torch.int32)
+        cu[:len(starts)] = starts.int()
+        cu = cu.to(dev)
+        dout = torch.randn(T, 6, 128, device=dev, generator=g).to(BF)
+        if name == "dc_ours":
+            from modded_nanogpt_b200.ops.dc import dc_correction
+            fwd = lambda: dc_correction(base, q, k, v, w1, w2, cu, 0.12, 112)
+        else:                               # the reference's Triton kernels (`dc_triton_kernels.py:1266`), unmodified
+            ref = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+            if not os.path.exists(os.path.join(ref, "dc_triton_kernels.py")):
+                raise SystemExit(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not staged on this machine"}))
+            sys.path.insert(0, ref)
+            from dc_triton_kernels import dc_attention_postonly_nodd_correction_add_base_triton as ref_dc
+            fwd = lambda: ref_dc(base, q[None], k[None], v[None], (w1[None], w2[None]), None, scaling=0.12, window=112, seq_lens=cu)
+
+        def run():
+            for t in (q, k, v, base, w1, w2):
+                t.grad = None
+            fwd().backward(dout.view_as(base) if name == "dc_ours" else dout)
+        # scores + PV over the 112-key window, forward, and about 2.5x that backward
+        return run, int(3.5 * 4 * 128 * 6 * T * 112), 4 * T * 6 * 256
     if name.startswith("attn"):             # attn[bwd]_{ours|fa2}_{short|long|paired}: packed documents, sliding window
         op, impl, kind = name.split("_")
         Tq, Hh, window = (2 * T, 3, 2 * 640) if kind == "paired" else (T, 6, 640 if kind == "short" else 1408)
@@ -177,7 +206,7 @@ def build_case(name, T, bn, fused):
 
 CASES = ["proj_qkv_ours", "proj_qkv_lib", "proj_o_ours", "proj_o_lib", "gatemlp_ours", "gatemlp_lib", "gemm_bf16_up", "gemm_bf16_dpre", "gemm_bf16_down", "gemm_bf16_dw", "gemm_fp8_relu2", "gemm_fp8_down", "gemm_bf16_qkv",
          "gemm_bf16_o", "gemm_bf16_o_null", "gemm_bf16_up_null", "gemm_fp8_logits", "gemm_fp8_logits_kk", "gemm_fp8_lmhead_dw_kmajor_a", "gemm_fp8_lmhead_dx", "gemm_fp8_lmhead_dw", "softcap_ce_e5m2", "softcap_ce_bf16", "lmhead_ce_fwdbwd",
-         "attn_ours_short", "attn_fa2_short", "attn_ours_long", "attn_fa2_long", "attn_ours_paired", "attn_fa2_paired",
+         "dc_ours", "dc_ref", "attn_ours_short", "attn_fa2_short", "attn_ours_long", "attn_fa2_long", "attn_ours_paired", "attn_fa2_paired",
          "attnbwd_ours_short", "attnbwd_fa2_short", "attnbwd_ours_long", "attnbwd_fa2_long", "attnbwd_ours_paired", "attnbwd_fa2_paired"]
 
 

@@ -176,20 +176,21 @@ adam_small_kernel(const __grid_constant__ SmallAdamTable t) {
 // out = bf16(u);  sumsq[matrix] += out^2.   per_mat % 8 == 0.
 __global__ void __launch_bounds__(256)
 nesterov_kernel(PeerPtrs grads, long long off, float* __restrict__ buf, __nv_bfloat16* __restrict__ out,
-                float* __restrict__ sumsq, long long mats, long long per_mat, float mu, float gmul) {
-  // A CTA takes chunks of 16 x 8 groups of 32 vectors (32 KB of gradient) in grid-stride order; inside a chunk its eight
+                float* __restrict__ sumsq, long long mats, long long per_mat, float mu, float gmul, int its) {
+  // A CTA takes chunks of its x 8 groups (its <= 16) of 32 vectors (32 KB of gradient) in grid-stride order; inside a chunk its eight
   // warps interleave.  A warp keeps the sum of squares of its groups in a register and adds it to the matrix's total
-  // at the end of the chunk or when the matrix changes: 16 times fewer adds to one address (they serialise) than one
+  // at the end of the chunk or when the matrix changes: `its` times fewer adds to one address (they serialise) than one
   // per group, while neighbouring CTAs still sweep neighbouring addresses.
   const long long vec_per_mat = per_mat / 8;                 // a multiple of 32: a group never straddles matrices
   const long long ngroups = mats * vec_per_mat / 32;
-  const long long nchunks = (ngroups + 127) / 128;
+  const long long per_chunk = 8LL * its;
+  const long long nchunks = (ngroups + per_chunk - 1) / per_chunk;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (long long chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x) {
   float ss = 0.f;
   long long cur = -1;
-  for (int it = 0; it < 16; ++it) {
-    const long long grp = chunk * 128 + it * 8 + warp;
+  for (int it = 0; it < its; ++it) {
+    const long long grp = chunk * per_chunk + it * 8 + warp;
     if (grp >= ngroups) break;
     const long long i = grp * 32 + lane;
     const long long mat = i / vec_per_mat;
@@ -484,8 +485,13 @@ extern "C" int mng_nesterov(const PeerPtrs* grads, long long off, float* buf, vo
   if (per_mat % 256) return -1;                              // 32 vectors of 8: a warp's group stays inside one matrix
   cudaStream_t s = (cudaStream_t)stream;
   cudaMemsetAsync(sumsq, 0, sizeof(float) * mats, s);
-  nesterov_kernel<<<grid_for(mats * per_mat / 8), 256, 0, s>>>(*grads, off, buf, (__nv_bfloat16*)out_bf16, sumsq, mats, per_mat,
-                                                               momentum, grad_mul);
+  // chunk length: long enough to thin out the adds to one address, short enough that every SM has several chunks
+  const long long groups = mats * per_mat / 256;
+  long long its = groups / (8LL * 148 * 4);
+  its = its < 1 ? 1 : (its > 16 ? 16 : its);
+  const long long nchunks = (groups + 8 * its - 1) / (8 * its);
+  const unsigned grid = (unsigned)(nchunks < 148 * 8 ? nchunks : 148 * 8);
+  nesterov_kernel<<<grid, 256, 0, s>>>(*grads, off, buf, (__nv_bfloat16*)out_bf16, sumsq, mats, per_mat, momentum, grad_mul, (int)its);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 

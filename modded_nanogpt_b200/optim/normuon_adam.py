@@ -23,6 +23,8 @@ fused CUDA kernels).
 """
 from __future__ import annotations
 
+import contextlib
+import os
 from dataclasses import asdict, dataclass
 
 import torch
@@ -241,6 +243,14 @@ class NorMuonAndAdam:
             self.sparse.share_rows(grad)
             self._pending[label] = ("sparse", grad)
 
+    def _update_lanes(self):
+        """Side streams for the independent updates of one step (CUDA parameters only; MNG_OPT_STREAMS=0: none)."""
+        if not hasattr(self, "_lanes"):
+            p = next(iter(self.params.values()))
+            on = p.is_cuda and os.environ.get("MNG_OPT_STREAMS", "1") != "0"
+            self._lanes = [torch.cuda.Stream(device=p.device) for _ in range(4)] if on else None
+        return self._lanes
+
     def _shard_of(self, label: str) -> Tensor:
         p, c = self.params[label], self.cfgs[label]
         if c.optim == "normuon":
@@ -295,6 +305,16 @@ class NorMuonAndAdam:
                                        *self.adam_scalars(l), 0, 0) for l in small])
             else:
                 self.coll.fused_small_adam(small, self)
+        # Updates that involve no library collective (one rank, or the fused peer-memory kernels) are independent of
+        # one another: the bandwidth-bound Adam kernels run on one side stream and the NorMuon banks - chains of small
+        # GEMMs, latency-bound once the banks are sharded - on three others, so the step costs the longest chain
+        # instead of their sum.
+        lanes = self._update_lanes() if (fused or self.world_size == 1) else None
+        if lanes:
+            main = torch.cuda.current_stream()
+            for s in lanes:
+                s.wait_stream(main)
+        n_muon = 0
         for label in self.work_order:
             if label not in self._pending:
                 continue
@@ -304,23 +324,32 @@ class NorMuonAndAdam:
                 grad_chunk = self.sparse.merge(grad_chunk)
             elif handle is not None:
                 handle.wait()
-            if fused and self.coll.handles(c):
-                g = self.coll.fused_update_and_gather(label, grad_chunk, c, self.state[label], self, do_adam)
-            else:
-                p_slice = self._shard_of(label)
-                if c.optim == "adam":
-                    self._adam_update(label, p_slice, grad_chunk)
+            lane = None
+            if lanes and (self.world_size == 1 or self.coll.handles(c)):
+                lane = lanes[0] if c.optim == "adam" else lanes[1 + n_muon % (len(lanes) - 1)]
+                n_muon += c.optim != "adam"
+            with (torch.cuda.stream(lane) if lane is not None else contextlib.nullcontext()):
+                if fused and self.coll.handles(c):
+                    g = self.coll.fused_update_and_gather(label, grad_chunk, c, self.state[label], self, do_adam)
                 else:
-                    v = self.math.normuon_direction(grad_chunk, self.state[label], c)
-                    self.math.normuon_apply(p_slice, self.state[label], v, c)
-                g = None
-                if c.comms.startswith("sharded") and self.world_size > 1:
-                    g = self.coll.all_gather(self._full_of(label), p_slice)
+                    p_slice = self._shard_of(label)
+                    if c.optim == "adam":
+                        self._adam_update(label, p_slice, grad_chunk)
+                    else:
+                        v = self.math.normuon_direction(grad_chunk, self.state[label], c)
+                        self.math.normuon_apply(p_slice, self.state[label], v, c)
+                    g = None
+                    if c.comms.startswith("sharded") and self.world_size > 1:
+                        g = self.coll.all_gather(self._full_of(label), p_slice)
             if g is not None:
                 if label == "lm_head":
                     lm_gather = g
                 else:
                     gathers.append(g)
+
+        if lanes:
+            for s in lanes:
+                main.wait_stream(s)
 
         # ---- phase 3 -------------------------------------------------------------------
         if fused:

@@ -167,7 +167,10 @@ def test_mlp_with_fused_residual_mix(fused, T, use_fp8):
             assert _rel(a, b) < tol, (name, _rel(a, b))
     for name, a, b in zip(names, got, unf):                       # same kernels, mix moved into the epilogues
         if a.numel() == 1:
-            assert abs(a.item() - b.item()) < 5e-3 * abs(b.item()) + 1e-2, (name, a.item(), b.item())
+            # bf16: the same products in both paths.  FP8: the unfused path sums g . (e4m3(post) e4m3(W2)), the fused one
+            # (g W2) . post with the bf16 operands of the backward GEMM: they differ by a quantisation error per term
+            slack = 2 * tol * run.term_norm[name] if use_fp8 else 1e-2
+            assert abs(a.item() - b.item()) < 5e-3 * abs(b.item()) + slack, (name, a.item(), b.item())
         else:
             assert _rel(a, b) < 8e-3, (name, _rel(a, b))
     fused.check_status()
