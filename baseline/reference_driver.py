@@ -170,10 +170,13 @@ def drive(args, ref_dir: str) -> dict:
             extra += 1
     frames_before_timing = compiled_frames()
 
+    from modded_nanogpt_b200.utils.timing import ClockSampler          # nvidia-smi polling thread (read-only queries)
+
     def timed(read_loss):
         nonlocal step
         dist.barrier()
         torch.cuda.synchronize()
+        sampler = ClockSampler(int(os.environ["LOCAL_RANK"])).start() if rank == 0 else None
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0 = time.perf_counter()
         e0.record()
@@ -185,12 +188,13 @@ def drive(args, ref_dir: str) -> dict:
         dist.barrier()
         torch.cuda.synchronize()
         wall = (time.perf_counter() - t0) * 1e3
+        clocks = sampler.stop() if sampler else None
         t = torch.tensor([e0.elapsed_time(e1), wall], dtype=torch.float64, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t[0]), float(t[1]), last
+        return float(t[0]), float(t[1]), last, clocks
 
-    dev_ms, _, _ = timed(False)
-    e2e_ms, e2e_wall, last = timed(True)
+    dev_ms, _, _, clocks = timed(False)
+    e2e_ms, e2e_wall, last, clocks_e2e = timed(True)
     recompiles_in_timed = compiled_frames() - frames_before_timing
     tokens = stage.batch_size * K
     T = stage.batch_size // 8
@@ -209,7 +213,7 @@ def drive(args, ref_dir: str) -> dict:
         "e2e": {"value": tokens / (max(e2e_ms, e2e_wall) / 1e3), "unit": "tokens/s", "ms_per_step": max(e2e_ms, e2e_wall) / K,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "last_loss": last},
         "extra_warmup_steps": extra, "recompiles_in_timed_regions": recompiles_in_timed,
-        "gpu_launches": None,
+        "gpu_launches": None, "clocks": clocks, "clocks_e2e": clocks_e2e,
     }
     dist.barrier()
     dist.destroy_process_group()
@@ -312,10 +316,13 @@ def drive_track2(args, ref_dir: str) -> dict:
             extra += 1
     frames0 = compiled_frames()
 
+    from modded_nanogpt_b200.utils.timing import ClockSampler          # nvidia-smi polling thread (read-only queries)
+
     def timed(read_loss):
         nonlocal step
         dist.barrier()
         torch.cuda.synchronize()
+        sampler = ClockSampler(int(os.environ["LOCAL_RANK"])).start() if rank == 0 else None
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0 = time.perf_counter()
         e0.record()
@@ -327,12 +334,13 @@ def drive_track2(args, ref_dir: str) -> dict:
         dist.barrier()
         torch.cuda.synchronize()
         wall = (time.perf_counter() - t0) * 1e3
+        clocks = sampler.stop() if sampler else None
         t = torch.tensor([e0.elapsed_time(e1), wall], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t[0]), float(t[1]), last
+        return float(t[0]), float(t[1]), last, clocks
 
-    dev_ms, _, _ = timed(False)
-    e2e_ms, e2e_wall, last = timed(True)
+    dev_ms, _, _, clocks = timed(False)
+    e2e_ms, e2e_wall, last, clocks_e2e = timed(True)
     tokens = batch * K
     T = batch // 8
     out = {
@@ -347,6 +355,7 @@ def drive_track2(args, ref_dir: str) -> dict:
         "e2e": {"value": tokens / (max(e2e_ms, e2e_wall) / 1e3), "unit": "tokens/s", "ms_per_step": max(e2e_ms, e2e_wall) / K,
                 "h2d_bytes_per_step": ga * (T * 4 + T * 8 + 4 * 1024), "d2h_bytes_per_step": 4, "last_loss": last},
         "extra_warmup_steps": extra, "recompiles_in_timed_regions": compiled_frames() - frames0, "gpu_launches": None,
+        "clocks": clocks, "clocks_e2e": clocks_e2e,
     }
     dist.barrier()
     dist.destroy_process_group()
