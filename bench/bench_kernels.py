@@ -95,6 +95,52 @@ def build_case(name, T, bn, fused):
             x.grad = w.grad = None
             fused.softcap_ce(x, w, tg, mtp, pt, pw, 23.0, 5.0, 7.5, grad_scale=1.0, fp8=True).sum().backward()
         return run, 3 * 2 * T * D * V, T * V * 3
+    if name in ("qkvproj_fused", "qkvproj_unfused"):   # QKV projection + QK norm + rotary + key offset + value add, forward + backward
+        from modded_nanogpt_b200.ops.glue import qkv_post
+        Hh = 6
+        x = r(T, D).to(BF).requires_grad_(True)
+        w = (r(3 * D, D) * D ** -0.5).to(BF)
+        lam = torch.tensor(0.8, device=dev, requires_grad=True)
+        t = torch.arange(T, device=dev, dtype=torch.float32)
+        freq = (1 / 1024) ** torch.linspace(0, 1, 32, device=dev)
+        cos, sin = torch.outer(t, freq).cos().contiguous(), torch.outer(t, freq).sin().contiguous()
+        ve = r(T, D).to(BF).requires_grad_(True)
+        vg = torch.rand(T, Hh, device=dev).to(BF).requires_grad_(True)
+        gv = [torch.zeros(2 * D, D, dtype=BF, device=dev), torch.zeros(D, D, dtype=BF, device=dev)]
+        gs = [r(T, Hh, 128).to(BF) for _ in range(3)]
+
+        def run():
+            x.grad = lam.grad = ve.grad = vg.grad = None
+            if name == "qkvproj_fused":
+                q, k, v = fused.qkv_proj(x, lam, w, gv, cos, sin, ve, vg, Hh, False, True)
+            else:
+                q, k, v = qkv_post(fused.bank_linear(x, lam, w, gv), cos, sin, ve, vg, None, Hh, False, True)
+            torch.autograd.backward([q, k, v], gs)
+        return run, 3 * 2 * T * D * 3 * D, T * 3 * D * 2
+    if name in ("mlpmix_fused", "mlpmix_unfused"):     # a x + b relu(norm(x) W1^T)^2 W2 with FP8 forward, forward + backward
+        from modded_nanogpt_b200.ops.glue import Term, lincomb
+        bank = torch.empty(1, 2, H, D, device=dev)
+        bank[0, 0].uniform_(-1, 1).mul_(3 ** 0.5 * 0.5 * D ** -0.5)
+        bank[0, 1].normal_(0, 0.02)
+        bank = bank.to(BF)
+        x = r(T, D).to(BF).requires_grad_(True)
+        g = (r(T, D) * 0.05).to(BF)
+        st = fused.quantize_mlp_weights(bank, None, torch.ones(1, device=dev), torch.ones(1, device=dev), True)
+        st.act_scale.fill_(0.25)
+        st = st.layer(0)
+        a_ = torch.tensor(1.05, device=dev, requires_grad=True)
+        b_ = torch.tensor(0.8, device=dev, requires_grad=True)
+        gv = (torch.zeros(H, D, dtype=BF, device=dev), torch.zeros(H, D, dtype=BF, device=dev))
+
+        def run():
+            x.grad = a_.grad = b_.grad = None
+            if name == "mlpmix_fused":
+                y = fused.norm_relu2_mlp_mix(x, bank[0, 0], bank[0, 1], a_, b_, st, gv)
+            else:
+                h, xr = fused.norm_relu2_mlp(x, bank[0, 0], bank[0, 1], st, gv, fork=True)
+                y = lincomb([Term(xr, scalar=a_), Term(h, scalar=b_)])
+            y.backward(g)
+        return run, 3 * 2 * 2 * T * D * H, T * D * 2
     if name.startswith("proj_"):            # proj_{qkv|o}_{ours|lib}: bank-backed projection, forward + backward
         _, which, impl = name.split("_")
         N = 3 * D if which == "qkv" else D
@@ -204,7 +250,7 @@ def build_case(name, T, bn, fused):
     raise SystemExit(f"unknown case {name}")
 
 
-CASES = ["proj_qkv_ours", "proj_qkv_lib", "proj_o_ours", "proj_o_lib", "gatemlp_ours", "gatemlp_lib", "gemm_bf16_up", "gemm_bf16_dpre", "gemm_bf16_down", "gemm_bf16_dw", "gemm_fp8_relu2", "gemm_fp8_down", "gemm_bf16_qkv",
+CASES = ["qkvproj_fused", "qkvproj_unfused", "mlpmix_fused", "mlpmix_unfused", "proj_qkv_ours", "proj_qkv_lib", "proj_o_ours", "proj_o_lib", "gatemlp_ours", "gatemlp_lib", "gemm_bf16_up", "gemm_bf16_dpre", "gemm_bf16_down", "gemm_bf16_dw", "gemm_fp8_relu2", "gemm_fp8_down", "gemm_bf16_qkv",
          "gemm_bf16_o", "gemm_bf16_o_null", "gemm_bf16_up_null", "gemm_fp8_logits", "gemm_fp8_logits_kk", "gemm_fp8_lmhead_dw_kmajor_a", "gemm_fp8_lmhead_dx", "gemm_fp8_lmhead_dw", "softcap_ce_e5m2", "softcap_ce_bf16", "lmhead_ce_fwdbwd",
          "dc_ours", "dc_ref", "attn_ours_short", "attn_fa2_short", "attn_ours_long", "attn_fa2_long", "attn_ours_paired", "attn_fa2_paired",
          "attnbwd_ours_short", "attnbwd_fa2_short", "attnbwd_ours_long", "attnbwd_fa2_long", "attnbwd_ours_paired", "attnbwd_fa2_paired"]
