@@ -16,6 +16,14 @@ __device__ __forceinline__ void ld8(const __nv_bfloat16* p, float (&f)[8]) {
     f[2 * t] = v.x; f[2 * t + 1] = v.y;
   }
 }
+__device__ __forceinline__ void cvt8(const uint4& u, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    float2 v = __bfloat1622float2(h[t]);
+    f[2 * t] = v.x; f[2 * t + 1] = v.y;
+  }
+}
 __device__ __forceinline__ void st8(__nv_bfloat16* p, const float (&f)[8]) {
   uint4 w;
   w.x = pack_bf16x2(f[0], f[1]); w.y = pack_bf16x2(f[2], f[3]); w.z = pack_bf16x2(f[4], f[5]); w.w = pack_bf16x2(f[6], f[7]);
@@ -79,49 +87,79 @@ lincomb_bwd_kernel(LinCombArgs a, LinCombGrads gr, const __nv_bfloat16* __restri
     for (int i = 0; i < MAXV; ++i)
       if (i < nv) ld8(g + row * cols + (i * 32 + lane) * 8, gv[i]);
   }
-  for (int j = 0; j < a.k; ++j) {
-    const LinTerm& tm = a.t[j];
-    const LinGrad& og = gr.t[j];
-    float spart = 0.f;
+  // Terms are handled two at a time with all of their loads (x for the dot products, dx where it is accumulated
+  // into) issued before the first use: the stores of one term would otherwise fence off the loads of the next.
+  for (int j0 = 0; j0 < a.k; j0 += 2) {
+    uint4 rx[2][MAXV], rd[2][MAXV];
+    // two terms of one tensor share a gradient buffer (the first writes, the second adds): then the second one's
+    // read has to follow the first one's store
+    const bool late1 = j0 + 1 < a.k && gr.t[j0 + 1].dx != nullptr && gr.t[j0 + 1].dx == gr.t[j0].dx;
     if (live) {
-      const float s = tm.scalar ? *tm.scalar : 1.f;
-      const float gt = tm.gate ? gate_at(tm.gate, tm.gate_bf16, row * tm.gate_stride + tm.gate_col) : 1.f;
-      const float c = tm.addc + s * gt;
-      float dot = 0.f;
-      const bool need_dot = og.dgate || og.dscalar;
-      const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(tm.x) + row * cols;
-      __nv_bfloat16* dx = og.dx ? reinterpret_cast<__nv_bfloat16*>(og.dx) + row * cols : nullptr;
 #pragma unroll
-      for (int i = 0; i < MAXV; ++i) {
-        if (i < nv) {
-          if (need_dot) {
-            float f[8];
-            ld8(x + (i * 32 + lane) * 8, f);
+      for (int u = 0; u < 2; ++u) {
+        const int j = j0 + u;
+        if (j < a.k) {
+          const LinGrad& og = gr.t[j];
+          const bool need_dot = og.dgate || og.dscalar;
+          const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(a.t[j].x) + row * cols;
+          const __nv_bfloat16* dx = og.dx ? reinterpret_cast<const __nv_bfloat16*>(og.dx) + row * cols : nullptr;
 #pragma unroll
-            for (int t = 0; t < 8; ++t) dot += gv[i][t] * f[t];
-          }
-          if (dx) {
-            float o[8];
-            if (og.dx_accumulate) {
-              ld8(dx + (i * 32 + lane) * 8, o);
-#pragma unroll
-              for (int t = 0; t < 8; ++t) o[t] = fmaf(c, gv[i][t], o[t]);
-            } else {
-#pragma unroll
-              for (int t = 0; t < 8; ++t) o[t] = c * gv[i][t];
+          for (int i = 0; i < MAXV; ++i) {
+            if (i < nv) {
+              if (need_dot) rx[u][i] = *reinterpret_cast<const uint4*>(x + (i * 32 + lane) * 8);
+              if (dx && og.dx_accumulate && !(u == 1 && late1)) rd[u][i] = *reinterpret_cast<const uint4*>(dx + (i * 32 + lane) * 8);
             }
-            st8(dx + (i * 32 + lane) * 8, o);
           }
         }
       }
-      if (need_dot) {
-        dot = warp_sum(dot);
-        if (og.dgate && lane == 0)
-          reinterpret_cast<__nv_bfloat16*>(og.dgate)[row * og.dgate_stride + og.dgate_col] = __float2bfloat16(s * dot);
-        spart = gt * dot;
-      }
     }
-    if (og.dscalar && lane == 0) s_part[j][warp] = spart;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int j = j0 + u;
+      if (j >= a.k) break;
+      const LinTerm& tm = a.t[j];
+      const LinGrad& og = gr.t[j];
+      float spart = 0.f;
+      if (live) {
+        const float s = tm.scalar ? *tm.scalar : 1.f;
+        const float gt = tm.gate ? gate_at(tm.gate, tm.gate_bf16, row * tm.gate_stride + tm.gate_col) : 1.f;
+        const float c = tm.addc + s * gt;
+        float dot = 0.f;
+        const bool need_dot = og.dgate || og.dscalar;
+        __nv_bfloat16* dx = og.dx ? reinterpret_cast<__nv_bfloat16*>(og.dx) + row * cols : nullptr;
+#pragma unroll
+        for (int i = 0; i < MAXV; ++i) {
+          if (i < nv) {
+            if (need_dot) {
+              float f[8];
+              cvt8(rx[u][i], f);
+#pragma unroll
+              for (int t = 0; t < 8; ++t) dot += gv[i][t] * f[t];
+            }
+            if (dx) {
+              float o[8];
+              if (og.dx_accumulate) {
+                if (u == 1 && late1) rd[u][i] = *reinterpret_cast<const uint4*>(dx + (i * 32 + lane) * 8);
+                cvt8(rd[u][i], o);
+#pragma unroll
+                for (int t = 0; t < 8; ++t) o[t] = fmaf(c, gv[i][t], o[t]);
+              } else {
+#pragma unroll
+                for (int t = 0; t < 8; ++t) o[t] = c * gv[i][t];
+              }
+              st8(dx + (i * 32 + lane) * 8, o);
+            }
+          }
+        }
+        if (need_dot) {
+          dot = warp_sum(dot);
+          if (og.dgate && lane == 0)
+            reinterpret_cast<__nv_bfloat16*>(og.dgate)[row * og.dgate_stride + og.dgate_col] = __float2bfloat16(s * dot);
+          spart = gt * dot;
+        }
+      }
+      if (og.dscalar && lane == 0) s_part[j][warp] = spart;
+    }
   }
   __syncthreads();
   if (threadIdx.x < a.k && gr.t[threadIdx.x].dscalar) {
@@ -370,24 +408,34 @@ qkv_post_bwd_from_out_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfl
     cs[0] = cos_t[pos * 32 + 2 * lane]; cs[1] = cos_t[pos * 32 + 2 * lane + 1];
     sn[0] = sin_t[pos * 32 + 2 * lane]; sn[1] = sin_t[pos * 32 + 2 * lane + 1];
   }
-  auto ld4 = [&](const __nv_bfloat16* p, float (&f)[4]) {
-    const uint2 u = *reinterpret_cast<const uint2*>(p);
+  auto cvt4 = [](uint2 u, float (&f)[4]) {
     const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&u);
     const float2 a = __bfloat1622float2(hh[0]), b = __bfloat1622float2(hh[1]);
     f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
   };
+  auto ldu = [](const __nv_bfloat16* p) { return *reinterpret_cast<const uint2*>(p); };
   auto unrot = [&](float (&f)[4]) {                     // transpose of the rotation on the two pairs of this lane
     const float a0 = f[0], a1 = f[1], b0 = f[2], b1 = f[3];
     f[0] = cs[0] * a0 - sn[0] * a1; f[1] = cs[0] * a1 + sn[0] * a0;
     f[2] = cs[1] * b0 - sn[1] * b1; f[3] = cs[1] * b1 + sn[1] * b0;
   };
+  // every load of this (token, head) is issued before the first row sum: one memory round trip per warp
+  const long long e = idx * 128 + lane * 4;
+  const bool shifted = !rot && key_offset;              // stationary half of k: lives one row down
+  const uint2 uq = ldu(q + e), udq = ldu(dq + e), uk = ldu(k + e), udk = ldu(dk + e), udv = ldu(dv + e);
+  uint2 uk2 = make_uint2(0u, 0u), udk2 = make_uint2(0u, 0u), uve = make_uint2(0u, 0u);
+  if (shifted) {
+    if (t + 1 < T) { uk2 = ldu(k + e + H * 128); udk2 = ldu(dk + e + H * 128); }
+    else if (t != 0) uk2 = ldu(k_last + h * 64 + (lane - 16) * 4);
+  }
+  if (ve && d_vgate) uve = ldu(ve + e);
+  const float rq = rstd_q[idx], rk = rstd_k[idx];
+  const float gt = (ve && vgate) ? __bfloat162float(vgate[t * vgate_stride + h]) : 1.f;
 #pragma unroll
   for (int which = 0; which < 2; ++which) {
-    const __nv_bfloat16* outp = which ? k : q;
-    const __nv_bfloat16* gp = which ? dk : dq;
     float n[4], d[4];
-    ld4(outp + idx * 128 + lane * 4, n);
-    ld4(gp + idx * 128 + lane * 4, d);
+    cvt4(which ? uk : uq, n);
+    cvt4(which ? udk : udq, d);
     if (rot) {
       unrot(n);
       unrot(d);
@@ -399,22 +447,18 @@ qkv_post_bwd_from_out_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfl
         for (int u = 0; u < 4; ++u) g0[u] = d[u];       // row 0 kept its own stationary half: n = out, gradient d
       }
       if (t + 1 < T) {
-        float nn[4], dd[4];
-        ld4(k + (idx + H) * 128 + lane * 4, nn);
-        ld4(dk + (idx + H) * 128 + lane * 4, dd);
-        if (t != 0) {
-#pragma unroll
-          for (int u = 0; u < 4; ++u) n[u] = nn[u];
-        }
+        float dd[4];
+        cvt4(udk2, dd);
+        if (t != 0) cvt4(uk2, n);
 #pragma unroll
         for (int u = 0; u < 4; ++u) d[u] = dd[u] + g0[u];
       } else {
-        if (t != 0) ld4(k_last + h * 64 + (lane - 16) * 4, n);
+        if (t != 0) cvt4(uk2, n);
 #pragma unroll
         for (int u = 0; u < 4; ++u) d[u] = g0[u];
       }
     }
-    const float r = (which ? rstd_k : rstd_q)[idx];
+    const float r = which ? rk : rq;
     const float s = warp_sum(d[0] * n[0] + d[1] * n[1] + d[2] * n[2] + d[3] * n[3]) * (1.f / 128.f);
     uint2 w;
     w.x = pack_bf16x2(r * (d[0] - n[0] * s), r * (d[1] - n[1] * s));
@@ -422,22 +466,19 @@ qkv_post_bwd_from_out_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfl
     *reinterpret_cast<uint2*>(d_qkv + t * ld + (which * H + h) * 128 + lane * 4) = w;
   }
   {
-    uint2 gu = *reinterpret_cast<const uint2*>(dv + idx * 128 + lane * 4);
-    *reinterpret_cast<uint2*>(d_qkv + t * ld + (2 * H + h) * 128 + lane * 4) = gu;
+    *reinterpret_cast<uint2*>(d_qkv + t * ld + (2 * H + h) * 128 + lane * 4) = udv;
     if (ve) {
-      const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&gu);
-      float2 ga = __bfloat1622float2(gh[0]), gb = __bfloat1622float2(gh[1]);
-      const float gt = vgate ? __bfloat162float(vgate[t * vgate_stride + h]) : 1.f;
+      float g[4];
+      cvt4(udv, g);
       if (d_ve) {
         uint2 w;
-        w.x = pack_bf16x2(gt * ga.x, gt * ga.y); w.y = pack_bf16x2(gt * gb.x, gt * gb.y);
-        *reinterpret_cast<uint2*>(d_ve + idx * 128 + lane * 4) = w;
+        w.x = pack_bf16x2(gt * g[0], gt * g[1]); w.y = pack_bf16x2(gt * g[2], gt * g[3]);
+        *reinterpret_cast<uint2*>(d_ve + e) = w;
       }
       if (d_vgate) {
-        uint2 e = *reinterpret_cast<const uint2*>(ve + idx * 128 + lane * 4);
-        const __nv_bfloat162* eh = reinterpret_cast<const __nv_bfloat162*>(&e);
-        float2 ea = __bfloat1622float2(eh[0]), eb = __bfloat1622float2(eh[1]);
-        const float dot = warp_sum(ga.x * ea.x + ga.y * ea.y + gb.x * eb.x + gb.y * eb.y);
+        float ev[4];
+        cvt4(uve, ev);
+        const float dot = warp_sum(g[0] * ev[0] + g[1] * ev[1] + g[2] * ev[2] + g[3] * ev[3]);
         if (lane == 0) d_vgate[t * d_vgate_stride + h] = __float2bfloat16(dot);
       }
     }

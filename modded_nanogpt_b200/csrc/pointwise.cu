@@ -87,7 +87,11 @@ rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __r
   if (row < rows) {
   const int nv = cols >> 8;
   float xv[MAXV][8], gv[MAXV][8];
+  uint4 old[MAXV];                                        // the addend is loaded with x and dy, not after the row sums
   float ss = 0.f, dot = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i)
+    if (i < nv && addend) old[i] = *reinterpret_cast<const uint4*>(addend + row * cols + (i * 32 + lane) * 8);
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
     if (i < nv) {
@@ -116,8 +120,7 @@ rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __r
 #pragma unroll
       for (int t = 0; t < 8; ++t) r[t] = gv[i][t] * rstd - xv[i][t] * c;
       if (addend) {
-        uint4 old = *reinterpret_cast<const uint4*>(addend + row * cols + (i * 32 + lane) * 8);
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&old);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&old[i]);
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
           float2 f = __bfloat1622float2(h[t]);
