@@ -68,4 +68,7 @@ def softcap_ce(x, w, targets, mtp_weights, prefix_targets, prefix_weight, a, b, 
 
 
 def softcap_ce_eval(x, w, targets, a, b, c) -> Tensor:
+    if use_kernel("ce", x) and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.shape[0] % 8 == 0:
+        from . import fused
+        return fused.softcap_ce_eval(x, w, targets, a, b, c)
     return ref.softcap_ce_eval(x, w, targets, a, b, c)

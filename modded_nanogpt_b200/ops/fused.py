@@ -556,6 +556,21 @@ def softcap_ce(x, w, targets, mtp_weights, prefix_targets, prefix_weight, a, b, 
                             prefix_weight, a, b, c, grad_scale, fp8, scales)
 
 
+def softcap_ce_eval(x: Tensor, w: Tensor, targets: Tensor, a: float, b: float, c: float, chunk: int = 16384) -> Tensor:
+    """Evaluation loss per token (`train_gpt.py:1689-1692`): bf16 logits on the own GEMM, chunk by chunk, and the
+    streaming loss kernel with a single target per row (its gradient output is scratch here)."""
+    C = _C()
+    T = x.shape[0]
+    out = torch.empty(T, dtype=torch.float32, device=x.device)
+    one = torch.ones(1, dtype=torch.float32, device=x.device)
+    x, targets = x.contiguous(), targets.contiguous()
+    for s in range(0, T, chunk):
+        e = min(T, s + chunk)
+        logits = gemm(x[s:e], w, b_mn=True)
+        out[s:e] = C.softcap_ce(logits, targets[s:e], one, None, None, False, a, b, c, 1.0)[0]
+    return out
+
+
 # --------------------------------------------------------------------------------------------------
 # attention / DC: tcgen05 kernels are selected here once available for the shape
 

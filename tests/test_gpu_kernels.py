@@ -3,6 +3,7 @@ import math
 
 import pytest
 import torch
+import torch.nn.functional as F
 
 pytestmark = pytest.mark.gpu
 
@@ -233,6 +234,24 @@ def test_fused_lm_head_ce(fused, fp8):
     fused.check_status()
 
 
+def test_eval_loss_on_own_kernels(fused):
+    """The evaluation loss (bf16 logits GEMM + streaming loss kernel, chunked) against the PyTorch statement."""
+    from modded_nanogpt_b200.ops import functional, reference as ref
+    torch.manual_seed(21)
+    T, D, V = 1000 * 8, 768, 50304
+    x = torch.randn(T, D, device="cuda").to(BF)
+    w = (torch.randn(D, V, device="cuda") * 0.03).to(BF)
+    tg = torch.randint(0, V, (T,), device="cuda")
+    got = fused.softcap_ce_eval(x, w, tg, 23.0, 5.0, 7.5, chunk=3000)          # chunks of uneven size
+    want = ref.softcap_ce_eval(x, w, tg, 23.0, 5.0, 7.5)
+    exact = F.cross_entropy(23.0 * torch.sigmoid(((x.float() @ w.float()) + 5.0) / 7.5), tg, reduction="none")
+    assert got.shape == want.shape and torch.isfinite(got).all()
+    assert (got - exact).abs().max() < 6e-2 and abs(got.mean().item() - exact.mean().item()) < 2e-3
+    assert (got - exact).abs().mean() <= (want - exact).abs().mean() * 1.5 + 1e-3   # at least as close as the bf16 softcap
+    assert torch.equal(functional.softcap_ce_eval(x, w, tg, 23.0, 5.0, 7.5), fused.softcap_ce_eval(x, w, tg, 23.0, 5.0, 7.5))
+    _ok(fused)
+
+
 def test_fp8_linear_t(fused):
     torch.manual_seed(7)
     T, D, V = 512, 256, 1024
@@ -368,6 +387,43 @@ def test_normuon_kernels(fused):
         assert torch.allclose(sm, smr, rtol=1e-4, atol=1e-9)
         full = lambda a, b: ((a.view(torch.int16).to(torch.int32) << 16) | (b.view(torch.int16).to(torch.int32) & 0xFFFF)).view(torch.float32)
         assert (full(p, mant) - full(pr, mantr)).abs().max() < 2e-4
+
+
+def test_normuon_kernels_with_two_rank_buffers(fused):
+    """The reduce-scatter and all-gather sides of the NorMuon kernels with two "ranks" that are two buffers of this GPU:
+    the Nesterov kernel sums both gradient buffers at an offset, the update kernel reads rank 1's weights and stores the
+    new ones into both."""
+    from modded_nanogpt_b200.ops import native, reference as ref
+    C = native.lib()
+    torch.manual_seed(14)
+    mats, rows, cols = 2, 768, 768
+    full = 3                                                                   # matrices in the whole bank; this "rank" owns 1..2
+    gs = [(torch.randn(full, rows, cols, device="cuda") * 1e-3).to(BF) for _ in range(2)]
+    off = rows * cols
+    buf = torch.randn(mats, rows, cols, device="cuda") * 1e-3
+    bufr = buf.clone()
+    out, ss = torch.empty(mats, rows, cols, dtype=BF, device="cuda"), torch.empty(mats, device="cuda")
+    C.nesterov([g.data_ptr() for g in gs], 1, off, buf, out, ss, 0.9, 0.5, 0)
+    gavg = ((gs[0][1:].float() + gs[1][1:].float()) * 0.5).to(BF)
+    ur = ref.nesterov_momentum_(gavg.float(), bufr, 0.9)
+    assert torch.allclose(buf, bufr, rtol=1e-5, atol=1e-9) and _rel(out, ur) < 4e-3
+    v = torch.randn(mats, rows, cols, device="cuda").to(BF) * 0.05
+    sm = torch.rand(mats, rows, 1, device="cuda") * 1e-3
+    smr = sm.clone()
+    ps = [(torch.randn(full, rows, cols, device="cuda") * 0.05).to(BF) for _ in range(2)]
+    ps[0][1:] = ps[1][1:]                                                      # replicas agree before the step
+    untouched = [p[0].clone() for p in ps]
+    mant = torch.randint(0, 65536, (mats, rows, cols), device="cuda").to(torch.uint16)
+    pr, mantr = ps[1][1:].clone(), mant.clone()
+    muls = torch.ones(mats, device="cuda")
+    scratch = torch.zeros(mats * (max(rows, cols) + 65), device="cuda")
+    C.normuon_apply([p.data_ptr() for p in ps], 1, off, mant, v, sm, scratch, True, 0.9, 0.03, 0.02, muls, 0)
+    vr = ref.normuon_variance_reduction_(v.clone(), smr, 0.9, -1)
+    for i in range(mats):
+        ref.cautious_update_mantissa_(pr[i], mantr[i], vr[i], 0.03, 0.02)
+    assert torch.equal(ps[0][1:], ps[1][1:]) and (ps[1][1:].float() - pr.float()).abs().max() < 2e-3
+    assert torch.equal(ps[0][0], untouched[0]) and torch.equal(ps[1][0], untouched[1])      # outside the shard: not written
+    _ok(fused)
 
 
 def test_embed_bwd_accumulates_in_place(fused):
