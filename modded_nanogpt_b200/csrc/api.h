@@ -40,6 +40,8 @@ typedef struct {
   const float* act_scale;
   unsigned int* amax_bits;
   int max_ctas;                       // 0 = one CTA per SM
+  int symmetric;                      // STORE, M == N a multiple of 128: the product is symmetric; only the upper-triangular
+                                      // 128 x 128 tiles are computed and every off-diagonal tile is stored twice
   void* stream;
   uint32_t* status;
 } GemmDesc;

@@ -43,7 +43,8 @@ void gemm(const Tensor& a, const Tensor& b, Tensor& out, bool a_mn, bool b_mn, i
           double beta, const c10::optional<Tensor>& cin, const c10::optional<Tensor>& alpha_t,
           const c10::optional<Tensor>& row_scale, const c10::optional<Tensor>& col_scale, const c10::optional<Tensor>& out8,
           const c10::optional<Tensor>& act_scale, const c10::optional<Tensor>& amax_bits, int64_t max_ctas,
-          const c10::optional<Tensor>& alpha2_t, const c10::optional<Tensor>& beta_t, const c10::optional<Tensor>& dot_out) {
+          const c10::optional<Tensor>& alpha2_t, const c10::optional<Tensor>& beta_t, const c10::optional<Tensor>& dot_out,
+          bool symmetric) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda());
   TORCH_CHECK(a.dim() == b.dim() && (a.dim() == 2 || a.dim() == 3) && out.dim() == a.dim());
   TORCH_CHECK(a.stride(-1) == 1 && b.stride(-1) == 1 && out.stride(-1) == 1, "innermost dims must be contiguous");
@@ -97,6 +98,9 @@ void gemm(const Tensor& a, const Tensor& b, Tensor& out, bool a_mn, bool b_mn, i
   }
   g.act_scale = fptr(act_scale);
   g.max_ctas = (int)max_ctas;
+  g.symmetric = symmetric;
+  TORCH_CHECK(!symmetric || (epilogue == MNG_EPI_STORE && g.M == g.N && g.M % 128 == 0 && !g.row_scale && !g.col_scale),
+              "symmetric: plain store epilogue, square output, a multiple of 128");
   g.stream = cur_stream();
   g.status = status_ptr(a);
   check(mng_gemm(&g), "mng_gemm");

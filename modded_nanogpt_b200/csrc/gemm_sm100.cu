@@ -52,6 +52,7 @@ struct EpiStore {
     const float* beta_ptr;
     long long ld, bstride;      // elements
     float alpha, beta;
+    int symmetric;              // 128 x 128 tiles of the upper triangle only: tiles off the diagonal are stored twice
   };
   struct State {};
   __device__ static void finish(const Params&, State&) {}
@@ -95,6 +96,16 @@ struct EpiStore {
           }
         }
         __syncwarp();
+      }
+      if (p.symmetric && (row0 >> 7) != (col0 >> 7) && live) {
+        // mirror image of an off-diagonal tile: element (row, col0 + j) also goes to (col0 + j, row).  The 32 lanes
+        // hold 32 consecutive rows, so each of these stores covers one run of 64 (bf16) or 128 (fp32) bytes.
+        const long long moff = base + (long long)col0 * p.ld + row;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if constexpr (OUT_F32) (reinterpret_cast<float*>(p.out) + moff)[j * p.ld] = v[j];
+          else (reinterpret_cast<__nv_bfloat16*>(p.out) + moff)[j * p.ld] = __float2bfloat16(v[j]);
+        }
       }
 #pragma unroll
       for (int j = 0; j < B / 16; ++j) {
@@ -485,10 +496,12 @@ static int launch_one(const GemmDesc& g, const typename Epi::Params& ep, int max
     if (e != cudaSuccess) return -2000 - (int)e;
     attr_set = true;
   }
-  const int tiles = ((g.M + GEMM_BM - 1) / GEMM_BM) * ((g.N + BN - 1) / BN) * g.batch;
+  const int tn = (g.N + BN - 1) / BN;
+  const bool sym = g.symmetric && BN == GEMM_BM;
+  const int tiles = (sym ? tn * (tn + 1) / 2 : ((g.M + GEMM_BM - 1) / GEMM_BM) * tn) * g.batch;
   int grid = tiles < num_sms() ? tiles : num_sms();
   if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
-  GemmShape shape{g.M, g.N, g.K, g.batch};
+  GemmShape shape{g.M, g.N, g.K, g.batch, sym ? 1 : 0};
   kern<<<grid, GEMM_THREADS, SM::TOTAL, (cudaStream_t)g.stream>>>(ma, mb, shape, ep, g.status);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : -3000 - (int)e;
@@ -579,13 +592,22 @@ static int launch_store_pair(const GemmDesc& g) {
 
 template <int ES, bool A_MN, bool B_MN, uint32_t AF, uint32_t BF>
 static int launch_store(const GemmDesc& g) {
+  if (g.symmetric) {                                          // upper-triangular 128 x 128 tiles, mirrored by the epilogue
+    if (g.M != g.N || (g.M % 128) || g.row_scale || g.col_scale) return -13;
+    if (g.out_f32) {
+      EpiStore<true>::Params p{g.out, g.cin, nullptr, nullptr, g.alpha_ptr, g.alpha2_ptr, g.beta_ptr, g.ldc, g.c_bstride, g.alpha, g.beta, 1};
+      return launch_one<128, ES, A_MN, B_MN, AF, BF, EpiStore<true>>(g, p, g.max_ctas);
+    }
+    EpiStore<false>::Params p{g.out, g.cin, nullptr, nullptr, g.alpha_ptr, g.alpha2_ptr, g.beta_ptr, g.ldc, g.c_bstride, g.alpha, g.beta, 1};
+    return launch_one<128, ES, A_MN, B_MN, AF, BF, EpiStore<false>>(g, p, g.max_ctas);
+  }
   if (g.bn == 512 && pair_ok(g)) return launch_store_pair<ES, A_MN, B_MN, AF, BF>(g);
   if (g.out_f32) {
-    EpiStore<true>::Params p{g.out, g.cin, g.row_scale, g.col_scale, g.alpha_ptr, g.alpha2_ptr, g.beta_ptr, g.ldc, g.c_bstride, g.alpha, g.beta};
+    EpiStore<true>::Params p{g.out, g.cin, g.row_scale, g.col_scale, g.alpha_ptr, g.alpha2_ptr, g.beta_ptr, g.ldc, g.c_bstride, g.alpha, g.beta, g.symmetric};
     return g.bn >= 256 ? launch_one<256, ES, A_MN, B_MN, AF, BF, EpiStore<true>>(g, p, g.max_ctas)
                        : launch_one<128, ES, A_MN, B_MN, AF, BF, EpiStore<true>>(g, p, g.max_ctas);
   }
-  EpiStore<false>::Params p{g.out, g.cin, g.row_scale, g.col_scale, g.alpha_ptr, g.alpha2_ptr, g.beta_ptr, g.ldc, g.c_bstride, g.alpha, g.beta};
+  EpiStore<false>::Params p{g.out, g.cin, g.row_scale, g.col_scale, g.alpha_ptr, g.alpha2_ptr, g.beta_ptr, g.ldc, g.c_bstride, g.alpha, g.beta, g.symmetric};
   return g.bn >= 256 ? launch_one<256, ES, A_MN, B_MN, AF, BF, EpiStore<false>>(g, p, g.max_ctas)
                      : launch_one<128, ES, A_MN, B_MN, AF, BF, EpiStore<false>>(g, p, g.max_ctas);
 }

@@ -23,7 +23,27 @@ constexpr int GEMM_STAGE_K_BYTES = 128;   // bytes of K per row and stage (one s
 
 struct GemmShape {
   int M, N, K, batch;
+  int symmetric;   // single-CTA kernel with BN = 128 only: M == N and the product is symmetric, so only the tiles on and
+                   // above the diagonal are computed (the epilogue mirrors them: `triton_kernels.py:51-55` does the same)
 };
+
+// Tile index -> (batch, first row, first column).  Symmetric mode walks the upper triangle row by row.
+template <int BN>
+__device__ __forceinline__ void gemm_tile_coords(const GemmShape& shape, int tile, int tiles_m, int tiles_n, int& b, int& m0, int& n0) {
+  if (shape.symmetric) {
+    const int per = tiles_n * (tiles_n + 1) / 2;
+    b = tile / per;
+    int r = tile - b * per, i = 0;
+    while (r >= tiles_n - i) { r -= tiles_n - i; ++i; }      // row i holds tiles_n - i tiles: columns i .. tiles_n - 1
+    m0 = i * GEMM_BM;
+    n0 = (i + r) * BN;
+  } else {
+    b = tile / (tiles_m * tiles_n);
+    const int r = tile - b * tiles_m * tiles_n;
+    m0 = (r / tiles_n) * GEMM_BM;
+    n0 = (r % tiles_n) * BN;
+  }
+}
 
 template <int BN, int ES>   // ES = operand element size in bytes
 struct GemmSmem {
@@ -127,7 +147,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_cons
   const int lane = threadIdx.x & 31;
   const int tiles_m = (shape.M + GEMM_BM - 1) / GEMM_BM;
   const int tiles_n = (shape.N + BN - 1) / BN;
-  const int num_tiles = tiles_m * tiles_n * shape.batch;
+  const int num_tiles = (shape.symmetric ? tiles_n * (tiles_n + 1) / 2 : tiles_m * tiles_n) * shape.batch;
   const int num_kb = (shape.K + BK - 1) / BK;
   constexpr uint32_t TMEM_COLS = 2 * BN;                // two accumulator buffers (256 or 512 columns)
 
@@ -160,10 +180,8 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_cons
       int stage = 0;
       uint32_t phase = 0;
       for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-        const int b = tile / (tiles_m * tiles_n);
-        const int r = tile - b * tiles_m * tiles_n;
-        const int m0 = (r / tiles_n) * GEMM_BM;
-        const int n0 = (r % tiles_n) * BN;
+        int b, m0, n0;
+        gemm_tile_coords<BN>(shape, tile, tiles_m, tiles_n, b, m0, n0);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag)) {
             if (*abort_flag == 0) { *abort_flag = ERR_WAIT_SMEM_EMPTY; atomicCAS(status, 0u, ERR_WAIT_SMEM_EMPTY); }
@@ -242,10 +260,8 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_cons
     typename Epi::State est{};                         // per-thread state carried across tiles (e.g. a running max)
     ChunkIO io{bars + SM::BAR_BYTES + (warp - 2) * SM::STG_BYTES, lane};
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const int b = tile / (tiles_m * tiles_n);
-      const int r = tile - b * tiles_m * tiles_n;
-      const int m0 = (r / tiles_n) * GEMM_BM;
-      const int n0 = (r % tiles_n) * BN;
+      int b, m0, n0;
+      gemm_tile_coords<BN>(shape, tile, tiles_m, tiles_n, b, m0, n0);
       if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag)) {
         if (*abort_flag == 0) { *abort_flag = ERR_WAIT_TMEM_FULL; atomicCAS(status, 0u, ERR_WAIT_TMEM_FULL); }
         break;

@@ -45,17 +45,20 @@ def gemm(a: Tensor, b: Tensor, *, a_mn: bool = False, b_mn: bool = False, out: T
          alpha_t: Tensor | None = None, row_scale: Tensor | None = None, col_scale: Tensor | None = None,
          epilogue: int = EPI_STORE, out8: Tensor | None = None, act_scale: Tensor | None = None,
          amax_bits: Tensor | None = None, max_ctas: int = 0, alpha2_t: Tensor | None = None,
-         beta_t: Tensor | None = None, dot_out: Tensor | None = None) -> Tensor:
+         beta_t: Tensor | None = None, dot_out: Tensor | None = None, symmetric: bool = False) -> Tensor:
     """out = epilogue(A @ B^T) on the tcgen05 kernel.  A is [.., M, K] (or [.., K, M] with a_mn),
     B is [.., N, K] (or [.., K, N] with b_mn); fp32 accumulation.  `alpha_t`, `alpha2_t`, `beta_t`: one-element fp32
     device tensors multiplied into alpha / beta (`beta_t` alone means beta = 1 * beta_t); `dot_out` (EPI_DPRE):
-    one-element fp32 accumulator that receives sum(acc * cin)."""
+    one-element fp32 accumulator that receives sum(acc * cin).  `symmetric`: the caller knows the product (and `cin`)
+    to be symmetric; only the upper-triangular 128 x 128 tiles are computed and mirrored (M == N, a multiple of 128)."""
     if beta_t is not None and beta == 0.0:
         beta = 1.0
     M = a.shape[-1] if a_mn else a.shape[-2]
     N = b.shape[-1] if b_mn else b.shape[-2]
     if out is None:
         out = torch.empty((*a.shape[:-2], M, N), dtype=out_dtype, device=a.device)
+    if symmetric:
+        bn = 128
     if bn is None:
         batch = a.shape[0] if a.dim() == 3 else 1
         tiles256 = -(-M // 128) * -(-N // 256) * batch
@@ -67,7 +70,7 @@ def gemm(a: Tensor, b: Tensor, *, a_mn: bool = False, b_mn: bool = False, out: T
         if PAIR_GEMM and out.dtype == torch.bfloat16 and -(-M // 256) * -(-N // 256) * batch >= NUM_SMS // 2:
             bn = 512
     _C().gemm(a, b, out, a_mn, b_mn, epilogue, bn, alpha, beta, cin, alpha_t, row_scale, col_scale, out8, act_scale,
-              amax_bits, max_ctas, alpha2_t, beta_t, dot_out)
+              amax_bits, max_ctas, alpha2_t, beta_t, dot_out, symmetric)
     return out
 
 

@@ -14,6 +14,8 @@ momentum update) and the last kernel stores the new weights into every rank's pa
 """
 from __future__ import annotations
 
+import os
+
 import torch
 from torch import Tensor
 
@@ -21,6 +23,9 @@ from ..ops import fused
 from ..ops import reference as ref
 from ..ops.native import lib
 from .normuon_adam import ParamConfig, TorchMath
+
+
+SYMMETRIC_PE = os.environ.get("MNG_PE_SYMMETRIC", "1") != "0"
 
 
 class CudaMath(TorchMath):
@@ -45,12 +50,15 @@ class CudaMath(TorchMath):
         A = self._buf(("A", mats, n), (mats, n, n), torch.bfloat16, X.device)
         B = self._buf(("B", mats, n), (mats, n, n), torch.bfloat16, X.device)
         Y = self._buf(("Y", mats, rows, cols), (mats, rows, cols), torch.bfloat16, X.device)
+        # A = X^T X (or X X^T) and B = b A + c A A are symmetric: from 3 x 3 tiles of 128 x 128 on, computing the upper
+        # triangle and mirroring it (`triton_kernels.py:51-55`) is less work than the full product on the larger tiles
+        sym = SYMMETRIC_PE and n % 128 == 0 and n >= 384
         for a, b, c in ref.POLAR_EXPRESS_COEFFS:
             if tall:
-                fused.gemm(X, X, a_mn=True, b_mn=True, out=A)                       # A = X^T X
+                fused.gemm(X, X, a_mn=True, b_mn=True, out=A, symmetric=sym)        # A = X^T X
             else:
-                fused.gemm(X, X, out=A)                                             # A = X X^T
-            fused.gemm(A, A, b_mn=True, out=B, alpha=c, beta=b, cin=A)              # B = b A + c A A
+                fused.gemm(X, X, out=A, symmetric=sym)                              # A = X X^T
+            fused.gemm(A, A, b_mn=True, out=B, alpha=c, beta=b, cin=A, symmetric=sym)   # B = b A + c A A
             if tall:
                 fused.gemm(X, B, b_mn=True, out=Y, alpha=1.0, beta=a, cin=X)        # X' = a X + X B
             else:

@@ -52,6 +52,29 @@ def test_gemm_bf16_mn_major(fused, a_mn, b_mn, bn):
     _ok(fused)
 
 
+@pytest.mark.parametrize("n,rows,batch", [(768, 3072, 2), (384, 256, 3), (1024, 1024, 1)])
+def test_gemm_symmetric_products(fused, n, rows, batch):
+    """Gram products and b A + c A A computed on the upper-triangular tiles and mirrored: equal to the full product on
+    the same kernel, exactly symmetric, and close to the fp32 statement."""
+    torch.manual_seed(7)
+    X = (torch.randn(batch, rows, n, device="cuda") * rows ** -0.5).to(BF)
+    full = fused.gemm(X, X, a_mn=True, b_mn=True, bn=128)                      # X^T X, both operands MN-major
+    sym = fused.gemm(X, X, a_mn=True, b_mn=True, symmetric=True)
+    assert torch.equal(sym, sym.transpose(-1, -2))
+    assert torch.equal(torch.triu(sym), torch.triu(full))                       # the computed tiles are the same tiles
+    assert _rel(sym, X.float().transpose(-1, -2) @ X.float()) < 4e-3
+    Xt = X.transpose(-1, -2).contiguous()                                       # [batch, n, rows]: X X^T with K-major operands
+    sym2 = fused.gemm(Xt, Xt, symmetric=True)
+    assert torch.equal(sym2, sym2.transpose(-1, -2)) and _rel(sym2, Xt.float() @ Xt.float().transpose(-1, -2)) < 4e-3
+    A = sym
+    B = fused.gemm(A, A, b_mn=True, alpha=0.5, beta=-2.0, cin=A, symmetric=True)
+    want = -2.0 * A.float() + 0.5 * (A.float() @ A.float())
+    assert torch.equal(B, B.transpose(-1, -2)) and _rel(B, want) < 6e-3
+    B32 = fused.gemm(A, A, b_mn=True, symmetric=True, out_dtype=torch.float32)
+    assert torch.equal(B32, B32.transpose(-1, -2)) and _rel(B32, A.float() @ A.float()) < 2e-3
+    _ok(fused)
+
+
 def test_gemm_alpha_beta_scales(fused):
     torch.manual_seed(2)
     M, N, K = 256, 256, 256
@@ -387,6 +410,28 @@ def test_normuon_kernels(fused):
         assert torch.allclose(sm, smr, rtol=1e-4, atol=1e-9)
         full = lambda a, b: ((a.view(torch.int16).to(torch.int32) << 16) | (b.view(torch.int16).to(torch.int32) & 0xFFFF)).view(torch.float32)
         assert (full(p, mant) - full(pr, mantr)).abs().max() < 2e-4
+
+
+@pytest.mark.parametrize("shape", [(2, 3072, 768), (3, 768, 768), (4, 256, 768), (2, 768, 3072)])
+def test_polar_express_on_the_gemm_kernels(fused, shape, monkeypatch):
+    """Polar Express on the batched tcgen05 GEMMs (symmetric products on mirrored upper-triangular tiles where the
+    shape allows) against the fp32 statement: same result with and without the symmetric path, singular values near 1."""
+    from modded_nanogpt_b200.ops import reference as ref
+    from modded_nanogpt_b200.optim import cuda_math
+    torch.manual_seed(9)
+    g = torch.randn(*shape, device="cuda")
+    x0 = (g / (g.norm(dim=(-2, -1), keepdim=True) * 1.02 + 1e-6)).to(BF)
+    outs = {}
+    for sym in (True, False):
+        monkeypatch.setattr(cuda_math, "SYMMETRIC_PE", sym)
+        outs[sym] = cuda_math.CudaMath().polar_express(x0.clone()).float()
+    assert _rel(outs[True], outs[False]) < 2e-2
+    want = ref.polar_express(g, torch.float32)
+    assert _rel(outs[True], want) < 8e-2                                          # bf16 iterations against fp32 ones
+    if shape[-1] != shape[-2]:
+        sv = torch.linalg.svdvals(outs[True])
+        assert sv.max() < 1.35 and sv.min() > 0.45, (sv.min().item(), sv.max().item())
+    _ok(fused)
 
 
 def test_normuon_kernels_with_two_rank_buffers(fused):
