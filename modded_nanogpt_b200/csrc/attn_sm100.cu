@@ -42,8 +42,19 @@ struct AttnParams {
   float* lse;
   int T, H, window;
   float scale_log2;       // softmax scale * log2(e)
+  int* work;              // items beyond the first of each CTA are claimed here; null = static stride of gridDim.x
 };
 
+// Work counter of the forward kernel (items beyond the first of each CTA are claimed from it); zeroed by a memset that
+// precedes the launch on the stream.  One per device: forward calls on different streams of one device must not overlap.
+static __device__ int g_atf_work[1];
+
+// Persistent: two CTAs per SM; a CTA starts on item blockIdx.x and claims further items (item = (128-query tile, head),
+// heads fastest, long-history tiles first) from a device counter, so that packed documents of different lengths balance
+// out.  TMEM, the barriers and the K/V buffers live across items and every barrier phase runs on counters that continue
+// across items: the next item's Q / K / V loads and its first score MMAs overlap the drain of the previous item's
+// accumulator (per-tile fixed cost of the one-CTA-per-tile launch: 7.9 us of a ~17 us tile at the training shapes).
+// The producer publishes each item number in a two-slot ring in shared memory before it signals q_full; -1 ends the walk.
 __global__ void __launch_bounds__(ATT_THREADS, 2)
 attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                 const __grid_constant__ CUtensorMap tv, AttnParams p, uint32_t* status) {
@@ -61,15 +72,24 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
   uint64_t* s_full = bars + 5;
   uint64_t* p_ready = bars + 6;
   uint64_t* o_done = bars + 7;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  uint64_t* q_empty = bars + 8;      // the item's score MMAs have read Q: the producer may load the next item's
+  uint64_t* o_free = bars + 9;       // the four soft-max warps have drained O: the next item's PV MMAs may overwrite it
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
   volatile uint32_t* abort_flag = tmem_slot + 1;
+  volatile int* item_ring = reinterpret_cast<volatile int*>(tmem_slot + 2);   // [2]: item of the it-th step of this CTA
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.y;
-  const int q0 = (gridDim.x - 1 - blockIdx.x) * 128;       // late (long-history) tiles first
-  const int q_last = min(q0 + 127, p.T - 1);
-  const int kv_lo = max(p.doc_start[q0], q0 - p.window);
-  const int nb = (q_last - kv_lo) / 128 + 1;
+  const int tiles = (p.T + 127) / 128;
+  const int items = tiles * p.H;
+  // query tile start, head, first key and number of 128-key blocks of an item
+  auto item_geom = [&](int item, int& h, int& q0, int& kv_lo, int& nb) {
+    const int tile = item / p.H;
+    h = item - tile * p.H;
+    q0 = (tiles - 1 - tile) * 128;                           // late (long-history) tiles first
+    const int q_last = min(q0 + 127, p.T - 1);
+    kv_lo = max(p.doc_start[q0], q0 - p.window);
+    nb = (q_last - kv_lo) / 128 + 1;
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -80,6 +100,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
     mbar_init(s_full, 1);
     mbar_init(p_ready, 4);
     mbar_init(o_done, 1);
+    mbar_init(q_empty, 1);
+    mbar_init(o_free, 4);
     *abort_flag = 0;
     mbar_fence_init();
     tma_prefetch_desc(&tq);
@@ -102,19 +124,36 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_expect_tx(q_full, ATT_TILE_BYTES);
-      tma_load_3d(sQ, &tq, q_full, 0, h, q0);
-      tma_load_3d(sQ + 16384, &tq, q_full, 64, h, q0);
-      for (int j = 0; j < nb; ++j) {
-        const int kb = kv_lo + j * 128;
-        if (!mbar_wait(k_empty, (j & 1) ^ 1, abort_flag)) { ATT_FAIL(ERR_WAIT_SMEM_EMPTY); break; }
-        mbar_expect_tx(k_full, ATT_TILE_BYTES);
-        tma_load_3d(sK, &tk, k_full, 0, h, kb);
-        tma_load_3d(sK + 16384, &tk, k_full, 64, h, kb);
-        if (!mbar_wait(v_empty, (j & 1) ^ 1, abort_flag)) { ATT_FAIL(ERR_WAIT_SMEM_EMPTY); break; }
-        mbar_expect_tx(v_full, ATT_TILE_BYTES);
-        tma_load_3d(sV, &tv, v_full, 0, h, kb);
-        tma_load_3d(sV + 16384, &tv, v_full, 64, h, kb);
+      uint32_t jt = 0, it = 0;                               // blocks / items issued so far by this CTA
+      int item = blockIdx.x;
+      bool ok = true;
+      while (ok) {
+        // Q buffer and ring slot it & 1 are free once the score MMAs of the item before have completed
+        if (!mbar_wait(q_empty, (it & 1) ^ 1, abort_flag)) { ATT_FAIL(ERR_WAIT_SMEM_EMPTY); break; }
+        if (item >= items) {
+          item_ring[it & 1] = -1;
+          mbar_arrive(q_full);                               // no copy: a plain arrive completes the phase
+          break;
+        }
+        item_ring[it & 1] = item;
+        int h, q0, kv_lo, nb;
+        item_geom(item, h, q0, kv_lo, nb);
+        mbar_expect_tx(q_full, ATT_TILE_BYTES);
+        tma_load_3d(sQ, &tq, q_full, 0, h, q0);
+        tma_load_3d(sQ + 16384, &tq, q_full, 64, h, q0);
+        for (int j = 0; j < nb; ++j, ++jt) {
+          const int kb = kv_lo + j * 128;
+          if (!mbar_wait(k_empty, (jt & 1) ^ 1, abort_flag)) { ATT_FAIL(ERR_WAIT_SMEM_EMPTY); ok = false; break; }
+          mbar_expect_tx(k_full, ATT_TILE_BYTES);
+          tma_load_3d(sK, &tk, k_full, 0, h, kb);
+          tma_load_3d(sK + 16384, &tk, k_full, 64, h, kb);
+          if (!mbar_wait(v_empty, (jt & 1) ^ 1, abort_flag)) { ATT_FAIL(ERR_WAIT_SMEM_EMPTY); ok = false; break; }
+          mbar_expect_tx(v_full, ATT_TILE_BYTES);
+          tma_load_3d(sV, &tv, v_full, 0, h, kb);
+          tma_load_3d(sV + 16384, &tv, v_full, 64, h, kb);
+        }
+        item = p.work ? (int)gridDim.x + atomicAdd(p.work, 1) : item + (int)gridDim.x;
+        ++it;
       }
     }
   } else if (warp == 1) {
@@ -124,137 +163,161 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
       // descriptors differ only in the 14-bit start-address field (address >> 4): build once, then add offsets
       const uint64_t dQ = make_smem_desc(smem_u32(sQ), 16, 1024), dK = make_smem_desc(smem_u32(sK), 16, 1024);
       const uint64_t dV = make_smem_desc(smem_u32(sV), 16384, 1024);
-      bool ok = mbar_wait(q_full, 0, abort_flag);
-      if (!ok) ATT_FAIL(ERR_WAIT_TMA_FULL);
-      for (int j = 0; ok && j < nb; ++j) {
-        if (!mbar_wait(k_full, j & 1, abort_flag)) { ATT_FAIL(ERR_WAIT_TMA_FULL); break; }
-        tc_fence_after();
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint32_t off = ((k >> 2) * 16384 + (k & 3) * 32) >> 4;
-          umma_f16(tmem_S, dQ + off, dK + off, IDESC_S, k != 0);
+      uint32_t jt = 0;
+      bool ok = true;
+      for (uint32_t it = 0; ok; ++it) {
+        if (!mbar_wait(q_full, it & 1, abort_flag)) { ATT_FAIL(ERR_WAIT_TMA_FULL); break; }
+        const int item = item_ring[it & 1];
+        if (item < 0) {
+          mbar_arrive(s_full);                               // wakes the soft-max warps, which then read the end mark
+          break;
         }
-        umma_commit(k_empty);
-        umma_commit(s_full);
-        if (!mbar_wait(p_ready, j & 1, abort_flag)) { ATT_FAIL(ERR_WAIT_TMEM_EMPTY); break; }
-        if (!mbar_wait(v_full, j & 1, abort_flag)) { ATT_FAIL(ERR_WAIT_TMA_FULL); break; }
-        tc_fence_after();
+        int h, q0, kv_lo, nb;
+        item_geom(item, h, q0, kv_lo, nb);
+        for (int j = 0; j < nb; ++j, ++jt) {
+          if (!mbar_wait(k_full, jt & 1, abort_flag)) { ATT_FAIL(ERR_WAIT_TMA_FULL); ok = false; break; }
+          tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < 8; ++k)                          // 16 keys per MMA: 8 TMEM columns of packed bf16
-          umma_f16_ts(tmem_O, tmem_S + k * 8, dV + ((k * 2048) >> 4), IDESC_PV, (j | k) != 0);
-        umma_commit(v_empty);
-        umma_commit(o_done);
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t off = ((k >> 2) * 16384 + (k & 3) * 32) >> 4;
+            umma_f16(tmem_S, dQ + off, dK + off, IDESC_S, k != 0);
+          }
+          umma_commit(k_empty);
+          if (j == nb - 1) umma_commit(q_empty);             // last reader of this item's Q
+          umma_commit(s_full);
+          if (!mbar_wait(p_ready, jt & 1, abort_flag)) { ATT_FAIL(ERR_WAIT_TMEM_EMPTY); ok = false; break; }
+          if (!mbar_wait(v_full, jt & 1, abort_flag)) { ATT_FAIL(ERR_WAIT_TMA_FULL); ok = false; break; }
+          if (j == 0 && !mbar_wait(o_free, (it & 1) ^ 1, abort_flag)) { ATT_FAIL(ERR_WAIT_TMEM_EMPTY); ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < 8; ++k)                        // 16 keys per MMA: 8 TMEM columns of packed bf16
+            umma_f16_ts(tmem_O, tmem_S + k * 8, dV + ((k * 2048) >> 4), IDESC_PV, (j | k) != 0);
+          umma_commit(v_empty);
+          umma_commit(o_done);
+        }
       }
     }
   } else {
     const int sub = warp & 3;                                // TMEM sub-partition of this warp
     const int r = sub * 32 + lane;
-    const int i = q0 + r;
-    const bool row_ok = i < p.T;
-    const int lo_i = row_ok ? max(p.doc_start[i], i - p.window) : 0;
-    const int hi_i = row_ok ? i : -1;
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
     const float c = p.scale_log2;
-    float m_used = -INFINITY, l = 0.f;
+    uint32_t jt = 0;
     bool alive = true;
-    for (int j = 0; j < nb; ++j) {
-      const int kb = kv_lo + j * 128;
-      if (!mbar_wait(s_full, j & 1, abort_flag)) { ATT_FAIL(ERR_WAIT_TMEM_FULL); alive = false; break; }
-      tc_fence_after();
-      const bool full = kb >= lo_i && kb + 127 <= hi_i;      // no masking needed for this row in this block
-      const unsigned span = (unsigned)(hi_i - lo_i);
-      const bool any_vis = hi_i >= lo_i;
-      // the whole 128-column row of S in registers: four loads in flight, one wait
-      uint32_t v0[32], v1[32], v2[32], v3[32];
-      tmem_ld32(tmem_S + lane_off, v0);
-      tmem_ld32(tmem_S + lane_off + 32, v1);
-      tmem_ld32(tmem_S + lane_off + 64, v2);
-      tmem_ld32(tmem_S + lane_off + 96, v3);
-      tmem_ld_wait();
-      float mx = -INFINITY;
-      if (full) {
-#pragma unroll
-        for (int t = 0; t < 32; ++t)
-          mx = fmaxf(mx, fmaxf(fmaxf(__uint_as_float(v0[t]), __uint_as_float(v1[t])), fmaxf(__uint_as_float(v2[t]), __uint_as_float(v3[t]))));
-      } else {
-        const int col0 = kb - lo_i;
-#pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          if (!((unsigned)(col0 + t) <= span && any_vis)) v0[t] = 0xff800000u;          // -inf: exp2 gives exactly 0
-          if (!((unsigned)(col0 + 32 + t) <= span && any_vis)) v1[t] = 0xff800000u;
-          if (!((unsigned)(col0 + 64 + t) <= span && any_vis)) v2[t] = 0xff800000u;
-          if (!((unsigned)(col0 + 96 + t) <= span && any_vis)) v3[t] = 0xff800000u;
-          mx = fmaxf(mx, fmaxf(fmaxf(__uint_as_float(v0[t]), __uint_as_float(v1[t])), fmaxf(__uint_as_float(v2[t]), __uint_as_float(v3[t]))));
-        }
-      }
-      mx *= c;
-      float alpha = 1.f;
-      if (mx > m_used + 8.f || (m_used == -INFINITY && mx > -INFINITY)) {
-        alpha = (m_used == -INFINITY) ? 0.f : exp2f(m_used - mx);
-        m_used = mx;
-        l *= alpha;
-      }
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {  // rescale the accumulator rows of this warp
-        if (!mbar_wait(o_done, (j - 1) & 1, abort_flag)) { ATT_FAIL(ERR_WAIT_TMEM_FULL); alive = false; break; }
+    for (uint32_t it = 0; alive; ++it) {
+      // The first score tile of the step (or the issuing thread's end signal) also tells that the ring slot is written.
+      // s_full runs at most one phase ahead of these warps (the next score MMA needs their p_ready); q_full can run two
+      // phases ahead of them when an item has a single block, so it cannot be waited on here.
+      if (!mbar_wait(s_full, jt & 1, abort_flag)) { ATT_FAIL(ERR_WAIT_TMEM_FULL); break; }
+      const int item = item_ring[it & 1];
+      if (item < 0) break;
+      int h, q0, kv_lo, nb;
+      item_geom(item, h, q0, kv_lo, nb);
+      const int i = q0 + r;
+      const bool row_ok = i < p.T;
+      const int lo_i = row_ok ? max(p.doc_start[i], i - p.window) : 0;
+      const int hi_i = row_ok ? i : -1;
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j < nb; ++j, ++jt) {
+        const int kb = kv_lo + j * 128;
+        if (j > 0 && !mbar_wait(s_full, jt & 1, abort_flag)) { ATT_FAIL(ERR_WAIT_TMEM_FULL); alive = false; break; }
         tc_fence_after();
-#pragma unroll 1
-        for (int cc = 0; cc < 4; ++cc) {
-          uint32_t v[32];
-          tmem_ld32(tmem_O + lane_off + cc * 32, v);
-          tmem_ld_wait();
+        const bool full = kb >= lo_i && kb + 127 <= hi_i;    // no masking needed for this row in this block
+        const unsigned span = (unsigned)(hi_i - lo_i);
+        const bool any_vis = hi_i >= lo_i;
+        // the whole 128-column row of S in registers: four loads in flight, one wait
+        uint32_t v0[32], v1[32], v2[32], v3[32];
+        tmem_ld32(tmem_S + lane_off, v0);
+        tmem_ld32(tmem_S + lane_off + 32, v1);
+        tmem_ld32(tmem_S + lane_off + 64, v2);
+        tmem_ld32(tmem_S + lane_off + 96, v3);
+        tmem_ld_wait();
+        float mx = -INFINITY;
+        if (full) {
 #pragma unroll
-          for (int t = 0; t < 32; ++t) v[t] = __float_as_uint(__uint_as_float(v[t]) * alpha);
-          tmem_st32(tmem_O + lane_off + cc * 32, v);
-        }
-      }
-      // rows that have seen no key yet keep m_used = -inf: use 0 so that exp2(-inf - 0) = 0 and not NaN
-      const float mneg = (m_used == -INFINITY) ? 0.f : -m_used;
-      auto emit = [&](const uint32_t (&vv)[32], int cc) {
-        uint32_t pk[16];
+          for (int t = 0; t < 32; ++t)
+            mx = fmaxf(mx, fmaxf(fmaxf(__uint_as_float(v0[t]), __uint_as_float(v1[t])), fmaxf(__uint_as_float(v2[t]), __uint_as_float(v3[t]))));
+        } else {
+          const int col0 = kb - lo_i;
 #pragma unroll
-        for (int t = 0; t < 16; ++t) {
-          const float p0 = exp2f(fmaf(__uint_as_float(vv[2 * t]), c, mneg));
-          const float p1 = exp2f(fmaf(__uint_as_float(vv[2 * t + 1]), c, mneg));
-          l += p0 + p1;
-          pk[t] = pack_bf16x2(p0, p1);
-        }
-        tmem_st16(tmem_S + lane_off + cc * 16, pk);
-      };
-      emit(v0, 0);
-      emit(v1, 1);
-      emit(v2, 2);
-      emit(v3, 3);
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_ready);
-    }
-    if (alive) {
-      if (!mbar_wait(o_done, (nb - 1) & 1, abort_flag)) {
-        ATT_FAIL(ERR_WAIT_TMEM_FULL);
-      } else {
-        tc_fence_after();
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        __nv_bfloat16* orow = p.out + ((size_t)i * p.H + h) * 128;
-#pragma unroll 1
-        for (int cc = 0; cc < 4; ++cc) {
-          uint32_t v[32];
-          tmem_ld32(tmem_O + lane_off + cc * 32, v);
-          tmem_ld_wait();
-          if (row_ok) {
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              uint4 w;
-              w.x = pack_bf16x2(__uint_as_float(v[8 * t]) * inv, __uint_as_float(v[8 * t + 1]) * inv);
-              w.y = pack_bf16x2(__uint_as_float(v[8 * t + 2]) * inv, __uint_as_float(v[8 * t + 3]) * inv);
-              w.z = pack_bf16x2(__uint_as_float(v[8 * t + 4]) * inv, __uint_as_float(v[8 * t + 5]) * inv);
-              w.w = pack_bf16x2(__uint_as_float(v[8 * t + 6]) * inv, __uint_as_float(v[8 * t + 7]) * inv);
-              *reinterpret_cast<uint4*>(orow + cc * 32 + t * 8) = w;
-            }
+          for (int t = 0; t < 32; ++t) {
+            if (!((unsigned)(col0 + t) <= span && any_vis)) v0[t] = 0xff800000u;          // -inf: exp2 gives exactly 0
+            if (!((unsigned)(col0 + 32 + t) <= span && any_vis)) v1[t] = 0xff800000u;
+            if (!((unsigned)(col0 + 64 + t) <= span && any_vis)) v2[t] = 0xff800000u;
+            if (!((unsigned)(col0 + 96 + t) <= span && any_vis)) v3[t] = 0xff800000u;
+            mx = fmaxf(mx, fmaxf(fmaxf(__uint_as_float(v0[t]), __uint_as_float(v1[t])), fmaxf(__uint_as_float(v2[t]), __uint_as_float(v3[t]))));
           }
         }
-        if (row_ok) p.lse[(size_t)h * p.T + i] = (m_used + log2f(l)) * 0.6931471805599453f;
+        mx *= c;
+        float alpha = 1.f;
+        if (mx > m_used + 8.f || (m_used == -INFINITY && mx > -INFINITY)) {
+          alpha = (m_used == -INFINITY) ? 0.f : exp2f(m_used - mx);
+          m_used = mx;
+          l *= alpha;
+        }
+        if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {  // rescale the accumulator rows of this warp
+          if (!mbar_wait(o_done, (jt - 1) & 1, abort_flag)) { ATT_FAIL(ERR_WAIT_TMEM_FULL); alive = false; break; }
+          tc_fence_after();
+#pragma unroll 1
+          for (int cc = 0; cc < 4; ++cc) {
+            uint32_t v[32];
+            tmem_ld32(tmem_O + lane_off + cc * 32, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int t = 0; t < 32; ++t) v[t] = __float_as_uint(__uint_as_float(v[t]) * alpha);
+            tmem_st32(tmem_O + lane_off + cc * 32, v);
+          }
+        }
+        // rows that have seen no key yet keep m_used = -inf: use 0 so that exp2(-inf - 0) = 0 and not NaN
+        const float mneg = (m_used == -INFINITY) ? 0.f : -m_used;
+        auto emit = [&](const uint32_t (&vv)[32], int cc) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int t = 0; t < 16; ++t) {
+            const float p0 = exp2f(fmaf(__uint_as_float(vv[2 * t]), c, mneg));
+            const float p1 = exp2f(fmaf(__uint_as_float(vv[2 * t + 1]), c, mneg));
+            l += p0 + p1;
+            pk[t] = pack_bf16x2(p0, p1);
+          }
+          tmem_st16(tmem_S + lane_off + cc * 16, pk);
+        };
+        emit(v0, 0);
+        emit(v1, 1);
+        emit(v2, 2);
+        emit(v3, 3);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_ready);
       }
+      if (!alive) break;
+      if (!mbar_wait(o_done, (jt - 1) & 1, abort_flag)) { ATT_FAIL(ERR_WAIT_TMEM_FULL); break; }
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = p.out + ((size_t)i * p.H + h) * 128;
+#pragma unroll 1
+      for (int cc = 0; cc < 4; ++cc) {
+        uint32_t v[32];
+        tmem_ld32(tmem_O + lane_off + cc * 32, v);
+        tmem_ld_wait();
+        if (cc == 3) {                                       // this warp's rows of O are in registers: release the accumulator
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(o_free);
+        }
+        if (row_ok) {
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(v[8 * t]) * inv, __uint_as_float(v[8 * t + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(v[8 * t + 2]) * inv, __uint_as_float(v[8 * t + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(v[8 * t + 4]) * inv, __uint_as_float(v[8 * t + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(v[8 * t + 6]) * inv, __uint_as_float(v[8 * t + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + cc * 32 + t * 8) = w;
+          }
+        }
+      }
+      if (row_ok) p.lse[(size_t)h * p.T + i] = (m_used + log2f(l)) * 0.6931471805599453f;
     }
   }
 #undef ATT_FAIL
@@ -329,8 +392,36 @@ extern "C" int mng_attn_fwd(const void* q, const void* k, const void* v, const i
     if (cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM) != cudaSuccess) return -3;
     attr = true;
   }
-  AttnParams p{doc_start, reinterpret_cast<__nv_bfloat16*>(out), lse, T, H, window, scale * 1.4426950408889634f};
-  dim3 grid((T + 127) / 128, H);
+  // the work counter is a __device__ symbol: its address and the SM count belong to the current device
+  constexpr int kMaxDevices = 64;
+  static int* work_of[kMaxDevices] = {};
+  static int sms_of[kMaxDevices] = {};
+  static std::mutex mu;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -6;
+  int* work = nullptr;
+  int sms = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!work_of[dev]) {
+      if (cudaGetSymbolAddress(reinterpret_cast<void**>(&work_of[dev]), g_atf_work) != cudaSuccess ||
+          cudaDeviceGetAttribute(&sms_of[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+        work_of[dev] = nullptr;
+        return -6;
+      }
+    }
+    work = work_of[dev];
+    sms = sms_of[dev];
+  }
+  // MNG_ATTN_FWD=tile: one CTA per (tile, head) item (same kernel, no claims)
+  static const bool per_item = [] { const char* e = getenv("MNG_ATTN_FWD"); return e && std::string(e) == "tile"; }();
+  const int items = ((T + 127) / 128) * H;
+  const int resident = 2 * sms;                              // two CTAs per SM (shared memory and TMEM columns)
+  const bool claim = !per_item && items > resident;
+  if (claim && cudaMemsetAsync(work, 0, sizeof(int), (cudaStream_t)stream) != cudaSuccess) return -5;
+  AttnParams p{doc_start, reinterpret_cast<__nv_bfloat16*>(out), lse, T, H, window, scale * 1.4426950408889634f,
+               claim ? work : nullptr};
+  dim3 grid(claim ? resident : items);
   attn_fwd_kernel<<<grid, ATT_THREADS, ATT_SMEM, (cudaStream_t)stream>>>(tq, tk, tv, p, status);
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
