@@ -7,10 +7,10 @@
 // (`train_gpt.py:1139-1141`) on one packed sequence; documents are given as `doc_start[i]` = index of the
 // first token of the document that holds token i.
 //
-// One CTA = 128 queries of one head, 192 threads, two CTAs per SM (96 KB of shared memory and 256 TMEM
-// columns each), so that one CTA's softmax overlaps the other's MMAs:
-//   warp 0    TMA producer: Q tile once, then K and V tiles of 128 keys (single buffers, refilled as soon as
-//             the MMA that read them has completed);
+// One work item = 128 queries of one head.  CTAs of 192 threads, two per SM (96 KB of shared memory and 256 TMEM
+// columns each), so that one CTA's softmax overlaps the other's MMAs; a CTA claims item after item from a device counter:
+//   warp 0    TMA producer: claims the items, Q tile once per item, then K and V tiles of 128 keys (single buffers,
+//             refilled as soon as the MMA that read them has completed);
 //   warp 1    tcgen05 issuer: S = Q K^T (both operands K-major from shared memory) into TMEM columns [0,128);
 //             O += P V with P read from TMEM (bf16, aliasing S) and V MN-major from shared memory, into [128,256);
 //   warps 2-5 softmax: thread = query row.  Two passes over the S tile in TMEM (row maximum, then
