@@ -498,6 +498,9 @@ xsa_gate_fwd_kernel(const __nv_bfloat16* __restrict__ y, const __nv_bfloat16* __
   const long long t = idx / H;
   const int h = (int)(idx % H);
   uint2 yu = *reinterpret_cast<const uint2*>(y + idx * 128 + lane * 4);
+  // the per-head scalars are fetched with the rows, not behind the row sums
+  const float alpha_raw = alpha ? __bfloat162float(alpha[t * alpha_stride + h]) : 0.f;
+  const float gt = gate ? __bfloat162float(gate[t * gate_stride + h]) : 1.f;
   const __nv_bfloat162* yh = reinterpret_cast<const __nv_bfloat162*>(&yu);
   float2 ya = __bfloat1622float2(yh[0]), yb = __bfloat1622float2(yh[1]);
   float o0 = ya.x, o1 = ya.y, o2 = yb.x, o3 = yb.y;
@@ -507,11 +510,10 @@ xsa_gate_fwd_kernel(const __nv_bfloat16* __restrict__ y, const __nv_bfloat16* __
     float2 va = __bfloat1622float2(vh[0]), vb = __bfloat1622float2(vh[1]);
     const float yv = warp_sum(ya.x * va.x + ya.y * va.y + yb.x * vb.x + yb.y * vb.y);
     const float vv = fmaxf(warp_sum(va.x * va.x + va.y * va.y + vb.x * vb.x + vb.y * vb.y), 1e-8f);
-    const float c = tanhf(__bfloat162float(alpha[t * alpha_stride + h])) * yv / vv;
+    const float c = tanhf(alpha_raw) * yv / vv;
     o0 -= c * va.x; o1 -= c * va.y; o2 -= c * vb.x; o3 -= c * vb.y;
   }
   if (gate) {
-    const float gt = __bfloat162float(gate[t * gate_stride + h]);
     o0 *= gt; o1 *= gt; o2 *= gt; o3 *= gt;
   }
   uint2 w;
@@ -529,8 +531,13 @@ xsa_gate_bwd_kernel(const __nv_bfloat16* __restrict__ y, const __nv_bfloat16* __
   if (idx >= T * H) return;
   const long long t = idx / H;
   const int h = (int)(idx % H);
+  // every load first: the per-head scalars would otherwise be fetched behind the row sums
   uint2 yu = *reinterpret_cast<const uint2*>(y + idx * 128 + lane * 4);
   uint2 gu = *reinterpret_cast<const uint2*>(dout + idx * 128 + lane * 4);
+  uint2 vu = make_uint2(0u, 0u);
+  if (alpha) vu = *reinterpret_cast<const uint2*>(v + idx * 128 + lane * 4);
+  const float alpha_raw = alpha ? __bfloat162float(alpha[t * alpha_stride + h]) : 0.f;
+  const float gt = gate ? __bfloat162float(gate[t * gate_stride + h]) : 1.f;
   const __nv_bfloat162* yh = reinterpret_cast<const __nv_bfloat162*>(&yu);
   const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&gu);
   float2 ya = __bfloat1622float2(yh[0]), yb = __bfloat1622float2(yh[1]);
@@ -539,7 +546,6 @@ xsa_gate_bwd_kernel(const __nv_bfloat16* __restrict__ y, const __nv_bfloat16* __
   float c = 0.f, th = 0.f, yv = 0.f, vv = 1.f;
   bool clamped = false;
   if (alpha) {
-    uint2 vu = *reinterpret_cast<const uint2*>(v + idx * 128 + lane * 4);
     const __nv_bfloat162* vh = reinterpret_cast<const __nv_bfloat162*>(&vu);
     float2 va = __bfloat1622float2(vh[0]), vb = __bfloat1622float2(vh[1]);
     V[0] = va.x; V[1] = va.y; V[2] = vb.x; V[3] = vb.y;
@@ -547,10 +553,9 @@ xsa_gate_bwd_kernel(const __nv_bfloat16* __restrict__ y, const __nv_bfloat16* __
     vv = warp_sum(V[0] * V[0] + V[1] * V[1] + V[2] * V[2] + V[3] * V[3]);
     clamped = vv < 1e-8f;
     vv = fmaxf(vv, 1e-8f);
-    th = tanhf(__bfloat162float(alpha[t * alpha_stride + h]));
+    th = tanhf(alpha_raw);
     c = th * yv / vv;
   }
-  const float gt = gate ? __bfloat162float(gate[t * gate_stride + h]) : 1.f;
   // z = y - c v ; out = z * gt
   if (dgate) {
     float zdot = warp_sum(G[0] * (Y[0] - c * V[0]) + G[1] * (Y[1] - c * V[1]) + G[2] * (Y[2] - c * V[2]) + G[3] * (Y[3] - c * V[3]));

@@ -13,11 +13,11 @@ communication themselves (`csrc/optim.cu`):
   whether its gradient row was touched since the last Adam step and copies that mask into every peer's memory before
   the barrier; the Adam kernel then skips the peer loads of untouched rows (they are exactly zero), so only touched
   rows cross NVLink - the device-side counterpart of the host-driven row exchange of `train_gpt.py:263-346`;
-* with `MNG_MULTIMEM=1`, when the symmetric-memory handle offers an NVSwitch multicast address for the arena, the
-  gradient read is a single `multimem.ld_reduce` per vector (the switch sums the ranks' copies, so 1/world of the
-  bytes arrive) and the weight write a single `multimem.st`; the plain peer loads/stores are the default (they
-  measured faster at 2 GPUs, where every multicast access crosses the switch even for the rank's own copy), the path
-  for machines without multicast and for every test that lets a rank fail;
+* from 8 ranks on (or with `MNG_MULTIMEM=1`), when the symmetric-memory handle offers an NVSwitch multicast address for
+  the arena, the gradient read is a single `multimem.ld_reduce` per vector (the switch sums the ranks' copies, so
+  1/world of the bytes arrive) and the weight write a single `multimem.st`; the plain peer loads/stores are the path
+  below that (they measured faster at 2 GPUs, where every multicast access crosses the switch even for the rank's own
+  copy, and equal at 4), with `MNG_MULTIMEM=0`, on machines without multicast and in every test that lets a rank fail;
 * ordering: one `peer_barrier` kernel (release/acquire flags in the arena's signal pad, bounded
   spin that reports through the status word) after backward and one after the updates.
 
@@ -80,7 +80,11 @@ class NvlinkCollectives(TorchCollectives):
         self.base_ptrs = [int(x) for x in self.handle.buffer_ptrs]
         assert len(self.base_ptrs) == self.world_size
         mc = int(getattr(self.handle, "multicast_ptr", 0) or 0)
-        self.mc_base = mc if os.environ.get("MNG_MULTIMEM", "0") == "1" and self.world_size > 1 else 0
+        # measured on B200 (Adam + NorMuon step, peer loads vs multimem): 2 ranks 3.15 vs 5.15 ms, 4 ranks 3.69 vs 3.68 ms,
+        # 8 ranks 4.03 vs 3.35 ms: the switch-side reduction pays once most of a shard's gradient bytes are remote
+        want = os.environ.get("MNG_MULTIMEM", "auto")
+        use_mc = want == "1" or (want == "auto" and self.world_size > 4)
+        self.mc_base = mc if use_mc and self.world_size > 1 else 0
         self.offsets = {}
         for label, p in params:
             po, go, nb = layout[label]
