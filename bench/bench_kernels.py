@@ -183,6 +183,15 @@ def build_case(name, T, bn, fused):
                 out = (F.linear(F.gelu(F.linear(x, w1)), w2) + b2) * sc.to(BF)
             out.backward(dout)
         return run, 3 * 2 * T * D * 64, T * D * 2
+    if name == "adam_bf16":             # sharded Adam kernel on one rank: T * 1024 bf16 parameters, fp32 moments
+        from modded_nanogpt_b200.ops import native
+        n = T * 1024
+        pw = (r(n) * 0.1).to(BF)
+        gw = (r(n) * 0.01).to(BF)
+        m_, v_ = torch.zeros(n, device=dev), torch.zeros(n, device=dev)
+        C = native.lib()
+        return (lambda: C.adam([gw.data_ptr()], [pw.data_ptr()], 0, 0, m_, v_, n, False, 0.9, 0.99, 1e-10, 3e-3, 2e-4, 1.0, None, 0,
+                               0, 0)), 0, n * 22
     if name in ("dc_ours", "dc_ref"):       # DC correction of layer 10 (window 112, 6 heads), forward + backward, packed documents
         g = torch.Generator(device=dev).manual_seed(0)
         q, k, v, base = (torch.randn(T, 6, 128, device=dev, generator=g).to(BF).requires_grad_(True) for _ in range(4))
@@ -252,7 +261,7 @@ def build_case(name, T, bn, fused):
 
 CASES = ["qkvproj_fused", "qkvproj_unfused", "mlpmix_fused", "mlpmix_unfused", "proj_qkv_ours", "proj_qkv_lib", "proj_o_ours", "proj_o_lib", "gatemlp_ours", "gatemlp_lib", "gemm_bf16_up", "gemm_bf16_dpre", "gemm_bf16_down", "gemm_bf16_dw", "gemm_fp8_relu2", "gemm_fp8_down", "gemm_bf16_qkv",
          "gemm_bf16_o", "gemm_bf16_o_null", "gemm_bf16_up_null", "gemm_fp8_logits", "gemm_fp8_logits_kk", "gemm_fp8_lmhead_dw_kmajor_a", "gemm_fp8_lmhead_dx", "gemm_fp8_lmhead_dw", "softcap_ce_e5m2", "softcap_ce_bf16", "lmhead_ce_fwdbwd",
-         "dc_ours", "dc_ref", "attn_ours_short", "attn_fa2_short", "attn_ours_long", "attn_fa2_long", "attn_ours_paired", "attn_fa2_paired",
+         "adam_bf16", "dc_ours", "dc_ref", "attn_ours_short", "attn_fa2_short", "attn_ours_long", "attn_fa2_long", "attn_ours_paired", "attn_fa2_paired",
          "attnbwd_ours_short", "attnbwd_fa2_short", "attnbwd_ours_long", "attnbwd_fa2_long", "attnbwd_ours_paired", "attnbwd_fa2_paired"]
 
 
