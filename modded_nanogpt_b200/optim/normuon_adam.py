@@ -52,6 +52,7 @@ class ParamConfig:
     momentum: float | None = None
     beta2: float | None = None
     per_matrix_lr_mul: list | None = None
+    table_comms: str = ""       # `comms` as the parameter table states it (`comms` itself becomes "none" on one rank)
 
 
 class TorchMath:
@@ -113,6 +114,8 @@ class NorMuonAndAdam:
         self.scatter_order = [l for l in scatter_order if l in present]
         self.work_order = [l for l in work_order if l in present]
         assert set(self.scatter_order) == present and set(self.work_order) == present
+        for c in self.cfgs.values():
+            c.table_comms = c.comms
         if self.world_size == 1:
             for c in self.cfgs.values():
                 c.comms = "none"
@@ -281,7 +284,8 @@ class NorMuonAndAdam:
             p, c = self.params[label], self.cfgs[label]
             if (c.optim == "adam" and not do_adam) or p.grad is None:
                 continue
-            if (can_batch and c.optim == "adam" and c.comms in ("replicated", "none") and p.is_cuda and p.numel() <= (1 << 20)
+            if (can_batch and c.optim == "adam" and c.table_comms == "replicated" and p.numel() <= (1 << 20)
+                    and (p.is_cuda or getattr(self.math, "batch_on_cpu", False))
                     and p.dtype in (torch.float32, torch.bfloat16) and p.grad.dtype == p.dtype and p.is_contiguous()
                     and p.grad.is_contiguous() and (self.world_size == 1 or label in self.coll.offsets)):
                 small.append(label)

@@ -121,3 +121,51 @@ def test_two_ranks_match_one_rank(tiny_corpus, tmp_path, cfg_name):
         worst = max(worst, (va.float() - vb.float()).abs().max().item())
     assert worst < 5e-4, worst
     assert not torch.equal(a["model"]["embed.weight"], a["model"]["lm_head.weight"].T)   # untied after split
+
+
+def _train_batched(rank, world, root, out, steps, batched):
+    import torch
+    from modded_nanogpt_b200.config import Hyperparameters, TrainingSchedule, small_track1_model, tiny_stages
+    from modded_nanogpt_b200.optim.normuon_adam import TorchMath
+    from modded_nanogpt_b200.runtime.dist import init_distributed, shutdown
+    from modded_nanogpt_b200.trainer import Trainer
+    from modded_nanogpt_b200.utils.logging import RunLogger
+
+    class BatchingMath(TorchMath):
+        """The interface of the kernel-backed math object for small parameters, stated as a loop over `adam`."""
+        batch_on_cpu = True
+        calls = []
+
+        def adam_batch(self, items, base_ptrs=None, grad_mul=1.0):
+            assert base_ptrs is None and grad_mul == 1.0
+            BatchingMath.calls.append([cfg.label for _, _, _, cfg, _, _, _, _ in items])
+            for p, grad, state, cfg, step_size, eff_wd, _, _ in items:
+                self.adam(p, grad, state, cfg, step_size, eff_wd)
+
+    env = init_distributed(accum_base=2)
+    hp = Hyperparameters(data_path=root, num_scheduled_iterations=steps, num_extension_iterations=0,
+                         val_batch_size=2048, val_tokens=4096, val_loss_every=0)
+    sched = TrainingSchedule(tiny_stages(batch_tokens=512, seq_len=256), steps, 0, split_embed_stage=0)
+    sched.split_step = 1
+    math_obj = BatchingMath(torch.float64) if batched else TorchMath(torch.float64)
+    tr = Trainer(small_track1_model(1024), sched, hp, env, param_dtype=torch.float32, math=math_obj,
+                 logger=RunLogger("t", env.master, log_dir=os.path.join(root, "logs"), quiet=True))
+    for s in range(steps):
+        tr.train_step(s)
+    torch.save(dict(model={k: v.clone() for k, v in tr.model.state_dict().items()}, calls=BatchingMath.calls), out)
+    shutdown()
+
+
+def test_small_parameters_update_in_one_batch(tiny_corpus, tmp_path):
+    """A math object that offers `adam_batch` receives all small replicated Adam parameters of a step in one call (never a
+    NorMuon bank or a sharded table), on Adam steps only, and the result equals the one-by-one path bit for bit."""
+    spawn(_train_batched, 1, tiny_corpus, str(tmp_path / "a.pt"), 4, False)
+    spawn(_train_batched, 1, tiny_corpus, str(tmp_path / "b.pt"), 4, True)
+    a, b = torch.load(tmp_path / "a.pt"), torch.load(tmp_path / "b.pt")
+    assert a["calls"] == [] and len(b["calls"]) >= 1
+    for labels in b["calls"]:
+        assert len(labels) >= 8 and len(set(labels)) == len(labels)
+        assert {"scalars", "smear_gate", "post_lambdas", "resid_lambdas"} <= set(labels)
+        assert not {"lm_head", "embed", "value_embeds", "bigram_embed", "qk_bank", "vo_bank", "mlp_bank"} & set(labels)
+    for k, va in a["model"].items():
+        assert torch.equal(va, b["model"][k]), k
