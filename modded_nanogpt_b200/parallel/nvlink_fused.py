@@ -22,11 +22,13 @@ communication themselves (`csrc/optim.cu`):
   spin that reports through the status word) after backward and one after the updates.
 
 This replaces `reduce_scatter_tensor` / `all_reduce` / `all_gather_into_tensor` of
-`train_gpt.py:588-642` for every parameter whose shard is 16-byte aligned; the handful of tiny
-parameters that are not fall back to NCCL through the base class.  Loads and stores are ordinary
+`train_gpt.py:588-642` for every parameter whose shard is 16-byte aligned; the small replicated parameters are updated together by one
+kernel that reads all ranks' copies of their gradients, and what neither path takes falls back to NCCL through the base class.  Loads and stores are ordinary
 global accesses on peer pointers: no TMA multicast, no library kernel is handed a peer pointer.
 """
 from __future__ import annotations
+
+import os
 
 import torch
 import torch.distributed as dist
@@ -50,7 +52,6 @@ class NvlinkCollectives(TorchCollectives):
         assert self.world_size <= 8
         self.math = math
         self.device = env.device
-        import os
         layout, off = {}, PAD_BYTES
         params = [(getattr(p, "label", n), p) for n, p in model.named_parameters()]
         for label, p in params:
@@ -65,14 +66,12 @@ class NvlinkCollectives(TorchCollectives):
             from ..trainer import track1_param_table
             table = track1_param_table()
         is_muon = lambda label: table.get(label, {}).get("optim") == "normuon"
-        self.grad_lo = off
-        for label, p in sorted(params, key=lambda lp: not is_muon(lp[0])):
-            if not is_muon(label) and not hasattr(self, "grad_muon_hi"):
-                self.grad_muon_hi = off
+        self.grad_lo = self.grad_muon_hi = off
+        for label, p in sorted(params, key=lambda lp: not is_muon(lp[0])):       # stable: NorMuon parameters first
             layout[label][1] = off
             off += _align(layout[label][2])
-        if not hasattr(self, "grad_muon_hi"):
-            self.grad_muon_hi = off
+            if is_muon(label):
+                self.grad_muon_hi = off
         self.grad_hi = off
         self.arena = symm.empty(off, dtype=torch.uint8, device=env.device)
         self.handle = symm.rendezvous(self.arena, dist.group.WORLD.group_name)
