@@ -1,4 +1,5 @@
-// Optimizer kernels.  Each one can fold the neighbouring collective into its memory traffic:
+// Optimizer kernels (the math of `train_gpt.py:724-864`: Nesterov momentum, NorMuon variance reduction, cautious weight
+// decay on a split fp32 master, Adam).  Each one can fold the neighbouring collective into its memory traffic:
 // gradients are read from every rank's buffer through NVLink peer pointers (reduce-scatter /
 // all-reduce fused into the first read) and updated weights are stored straight into every rank's
 // parameter tensor (all-gather fused into the last write).  When the buffers also have an NVSwitch
@@ -138,8 +139,8 @@ adam_kernel(PeerPtrs grads, PeerPtrs params, long long off, float* __restrict__ 
   }
 }
 
-// One launch for a batch of small replicated parameters (gates, scalars, the MUDD matrices): blockIdx.y picks the
-// parameter, elements are handled one by one so that no size or alignment rule applies.  Every rank sums all ranks'
+// One launch for a batch of small replicated parameters (gates, scalars, the MUDD matrices; `train_gpt.py:597-599`
+// issues one all-reduce and `:840-864` one compiled update per such parameter): blockIdx.y picks the parameter, elements are handled one by one so that no size or alignment rule applies.  Every rank sums all ranks'
 // gradients in the same order and updates its own copy, so the copies stay bitwise equal.
 __global__ void __launch_bounds__(256)
 adam_small_kernel(const __grid_constant__ SmallAdamTable t) {
