@@ -28,7 +28,6 @@ import os
 from dataclasses import asdict, dataclass
 
 import torch
-import torch.distributed as dist
 from torch import Tensor, nn
 
 from ..ops import reference as ref

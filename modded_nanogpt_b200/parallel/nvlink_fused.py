@@ -34,7 +34,7 @@ import torch
 import torch.distributed as dist
 
 from ..ops.native import lib
-from .collectives import TorchCollectives, _Done
+from .collectives import TorchCollectives
 
 PAD_BYTES = 4096
 
