@@ -169,3 +169,129 @@ def test_small_parameters_update_in_one_batch(tiny_corpus, tmp_path):
         assert not {"lm_head", "embed", "value_embeds", "bigram_embed", "qk_bank", "vo_bank", "mlp_bank"} & set(labels)
     for k, va in a["model"].items():
         assert torch.equal(va, b["model"][k]), k
+
+
+def _train_fused_pattern(rank, world, root, out, steps, fused_pattern):
+    import torch
+    import torch.distributed as dist
+    from modded_nanogpt_b200.config import Hyperparameters, TrainingSchedule, small_track1_model, tiny_stages
+    from modded_nanogpt_b200.optim.normuon_adam import TorchMath
+    from modded_nanogpt_b200.parallel.collectives import TorchCollectives
+    from modded_nanogpt_b200.runtime.dist import init_distributed, shutdown
+    from modded_nanogpt_b200.trainer import Trainer
+    from modded_nanogpt_b200.utils.logging import RunLogger
+
+    class BatchingMath(TorchMath):
+        batch_on_cpu = True
+
+        def adam_batch(self, items, base_ptrs=None, grad_mul=1.0):
+            raise AssertionError("with several ranks the collectives object updates the small parameters")
+
+    class FusedPattern(TorchCollectives):
+        """The call pattern of the peer-memory collectives on gloo tensors: gradients stay where they are, nothing is
+        launched in phase 1, one call per parameter does reduction + update + gather, the small replicated parameters
+        go through one call, and gradients are cleared in place."""
+        fused = True
+
+        def __init__(self, math):
+            super().__init__()
+            self.math, self.offsets, self.log, self.opt = math, {}, [], None
+
+        def prepare(self, optimizer):
+            self.opt = optimizer
+            self.offsets = {label: (0, 0) for label in optimizer.params}
+
+        def enable_row_masks(self, label, param):
+            return False
+
+        def handles(self, cfg):
+            return cfg.label != "ve_gate_bank"                 # one parameter stays on the library path
+
+        def launch_fused_reduce(self, label, grad, cfg, state):
+            return (None, None)
+
+        def reduce_barrier(self):
+            self.log.append("reduce_barrier")
+            dist.barrier()
+
+        def gather_barrier(self):
+            self.log.append("gather_barrier")
+            dist.barrier()
+
+        def clear_grad(self, p):
+            raise AssertionError("clear_grads replaces the per-parameter clears")
+
+        def clear_grads(self, do_adam):
+            self.log.append(("clear", do_adam))
+            for label, p in self.opt.params.items():
+                if p.grad is not None and (do_adam or self.opt.cfgs[label].optim == "normuon"):
+                    p.grad.zero_()
+
+        def fused_small_adam(self, labels, optimizer):
+            self.log.append(("small", tuple(labels)))
+            for label in labels:
+                g = optimizer.params[label].grad.clone()
+                self.all_reduce(g).wait()
+                step_size, eff_wd = optimizer.adam_scalars(label)
+                self.math.adam(optimizer.params[label].data, g, optimizer.state[label], optimizer.cfgs[label], step_size, eff_wd)
+
+        def fused_update_and_gather(self, label, _grad, cfg, state, optimizer, do_adam):
+            assert _grad is None
+            p = optimizer.params[label]
+            if cfg.comms.startswith("sharded"):
+                src = p.grad.view(cfg.reshape) if cfg.optim == "normuon" else p.grad
+                chunk = torch.empty((cfg.chunk_size, *src.shape[1:]), dtype=src.dtype)
+                self.reduce_scatter(chunk, src).wait()
+                shard = optimizer._shard_of(label)
+                if cfg.optim == "normuon":
+                    self.math.normuon_apply(shard, state, self.math.normuon_direction(chunk, state, cfg), cfg)
+                else:
+                    optimizer._adam_update(label, shard, chunk)
+                self.all_gather(optimizer._full_of(label), shard).wait()
+            else:
+                g = p.grad.clone()
+                self.all_reduce(g).wait()
+                optimizer._adam_update(label, p.data, g)
+            return None
+
+    env = init_distributed(accum_base=2)
+    hp = Hyperparameters(data_path=root, num_scheduled_iterations=steps, num_extension_iterations=0,
+                         val_batch_size=2048, val_tokens=4096, val_loss_every=0)
+    sched = TrainingSchedule(tiny_stages(batch_tokens=512, seq_len=256), steps, 0, split_embed_stage=0)
+    sched.split_step = 2
+    math_obj = BatchingMath(torch.float64) if fused_pattern else TorchMath(torch.float64)
+    coll = FusedPattern(math_obj) if fused_pattern else None
+    tr = Trainer(small_track1_model(1024), sched, hp, env, param_dtype=torch.float32, math=math_obj, collectives=coll,
+                 logger=RunLogger("t", env.master, log_dir=os.path.join(root, "logs"), quiet=True))
+    for s in range(steps):
+        tr.train_step(s)
+    if rank == 0:
+        torch.save(dict(model={k: v.clone() for k, v in tr.model.state_dict().items()}, log=coll.log if coll else []), out)
+    shutdown()
+
+
+def test_fused_collectives_call_pattern_matches_library_path(tiny_corpus, tmp_path):
+    """Two gloo ranks drive `NorMuonAndAdam.step` through the interface of the peer-memory collectives (stated with
+    library collectives): same parameters as the plain library path, through the embed untie; barriers bracket the
+    updates, the small replicated parameters go through one call on Adam steps only, gradients are cleared in one call."""
+    steps = 5
+    spawn(_train_fused_pattern, 2, tiny_corpus, str(tmp_path / "a.pt"), steps, False)
+    spawn(_train_fused_pattern, 2, tiny_corpus, str(tmp_path / "b.pt"), steps, True)
+    a, b = torch.load(tmp_path / "a.pt"), torch.load(tmp_path / "b.pt")
+    for k, va in a["model"].items():
+        tol = 2e-2 if k in ("value_embeds", "bigram_embed.weight") else 1e-5
+        assert (va.float() - b["model"][k].float()).abs().max() < tol, k
+    log = b["log"]
+    assert log.count("reduce_barrier") == steps and log.count("gather_barrier") == steps
+    smalls = [e for e in log if isinstance(e, tuple) and e[0] == "small"]
+    clears = [e for e in log if isinstance(e, tuple) and e[0] == "clear"]
+    assert len(clears) == steps and 0 < len(smalls) == sum(1 for c in clears if c[1])
+    for e in smalls:
+        assert "ve_gate_bank" in e[1] and "lm_head" not in e[1] and "qk_bank" not in e[1]
+    i = 0
+    for step in range(steps):                                  # per step: barrier, [small], barrier, clear
+        assert log[i] == "reduce_barrier"
+        i += 2 if (isinstance(log[i + 1], tuple) and log[i + 1][0] == "small") else 1
+        assert log[i] == "gather_barrier" and log[i + 1][0] == "clear"
+        i += 2
+    assert i == len(log)
